@@ -1,0 +1,150 @@
+/*
+ * rpfq_b200.h — C ABI of the B200 (sm_100a) packed complex-phase linear layer.
+ *
+ * Drop-in boundary for the hot path of RPFQ-ViT (Fmylalala/RPFQ-review): the
+ * widely-linear layer y = U x + W conj(x) whose U and W are stored as
+ * residual stages of 2-bit phase codes plus fp16 magnitude scales, in the
+ * exporter's packed layout. All entry points take plain device pointers and
+ * sizes, launch on the given CUDA stream, never synchronise the device and
+ * never allocate (the caller owns every buffer). They return RPFQ_OK or a
+ * nonzero status; rpfq_last_error() gives the message (thread-local).
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   - QATLinearComplexPhase.forward           RPFQ-ViT-main/quant_models/quant_i.py:513-554
+ *   - torch.ops.quant.QATLinearComplexPhaseV2_forward
+ *                                             RPFQ-ViT-main/quant_models/kernel.py:599-605
+ *   - wideLinear / wideLinearReference        RPFQ-ViTAndroid/app/src/main/cpp/ops/phase_linear.h:59-68
+ *   - buildFusedWideLinearCache               RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.h:30-31
+ *   - ActivationQuantSTE.forward              RPFQ-ViT-main/quant_models/quant_i.py:442-455
+ *
+ * Layout conventions (unchanged from the reference):
+ *   real Linear(in = K, out = N) = complex map k_c = K/2 -> n_c = N/2;
+ *   x[:, 0:k_c] = Re(x), x[:, k_c:K] = Im(x); y likewise with n_c.
+ *   Packed plane (one residual stage of U or W):
+ *     codes       uint8 [n_cp, k_cp * code_bits / 8], codes LSB-first
+ *                 (2-bit codebook 0:-1, 1:+1, 2:-i, 3:+i)
+ *     gamma_real  fp16  [n_cp, k_cp / 256]   (1 / scale, per row and 256-column block)
+ *     gamma_imag  fp16  [n_cp, k_cp / 256]
+ *   with n_cp, k_cp the complex dims rounded up to 256
+ *   (RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py:148-159,189-224,384-423).
+ */
+#ifndef RPFQ_B200_H
+#define RPFQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* rpfq_stream_t; /* a cudaStream_t; NULL = the legacy default stream */
+
+enum {
+    RPFQ_OK = 0,
+    RPFQ_ERR_INVALID = 1,     /* bad argument (shape, alignment, null pointer)        */
+    RPFQ_ERR_UNSUPPORTED = 2, /* valid but not supported on this path                 */
+    RPFQ_ERR_CUDA = 3,        /* a CUDA runtime call failed (message has the details) */
+    RPFQ_ERR_DEVICE = 4       /* a kernel reported a device-side error (bounded wait) */
+};
+
+enum { RPFQ_ACT_NONE = 0, RPFQ_ACT_GELU = 1 };               /* epilogue activation */
+enum { RPFQ_ROUND_NEAREST_EVEN = 0, RPFQ_ROUND_TIES_AWAY = 1 }; /* fp32 -> fp16 of K1 */
+
+/* One residual stage of U or W. Replaces PhaseLinearParams
+ * (RPFQ-ViTAndroid/app/src/main/cpp/ops/phase_linear.h:15-26). */
+typedef struct RpfqPhasePlane {
+    const uint8_t* codes;
+    const uint16_t* gamma_real; /* fp16 bits */
+    const uint16_t* gamma_imag; /* fp16 bits */
+} RpfqPhasePlane;
+
+/* A packed widely-linear layer. Replaces WideLinearParams
+ * (RPFQ-ViTAndroid/app/src/main/cpp/ops/phase_linear.h:28-40). */
+typedef struct RpfqPackedLinear {
+    int32_t n_c, k_c;   /* complex output / input dims (unpadded)           */
+    int32_t n_cp, k_cp; /* padded dims, multiples of 256                    */
+    int32_t stages;     /* residual stages per U and per W, 1..4            */
+    int32_t code_bits;  /* 2 (reference codebook); 3 or 4 (uniform phases)  */
+    RpfqPhasePlane u[4];
+    RpfqPhasePlane w[4];
+} RpfqPackedLinear;
+
+/* K1 — decode a packed layer into the dense fp16 coefficient matrix
+ * dense[2 n_c, 2 k_c] = [[rr, ir], [ri, ii]] (row-major), the B operand of
+ * rpfq_gemm_sm100. Bit-exact with the reference's fp16 coefficient cache:
+ * buildFusedWideLinearCache, RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.cpp:117-166
+ * (rounding = RPFQ_ROUND_TIES_AWAY reproduces its floatToHalfBits, :91-115;
+ * RPFQ_ROUND_NEAREST_EVEN is the IEEE conversion). Runs once per layer. */
+int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32_t rounding,
+                       rpfq_stream_t stream);
+
+/* K2 — y[m, n] = act(x[m, :] . w[n, :] + bias[n]) + residual[m, n], fp16 in/out,
+ * fp32 accumulation on tcgen05 tensor cores. Replaces the dense product
+ * F.linear(x, q_weight, bias) of QATLinearComplexPhase.forward
+ * (RPFQ-ViT-main/quant_models/quant_i.py:554) and the F.linear call of
+ * QATLinearComplexPhaseV2_autograd.forward (kernel.py:573).
+ * Requirements: k % 8 == 0, n % 8 == 0, ldx % 8 == 0, ldy % 8 == 0,
+ * ldr % 8 == 0, 16-byte aligned x / w / y / bias / residual. */
+typedef struct RpfqGemmArgs {
+    const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements) */
+    int64_t ldx;
+    const uint16_t* w;        /* fp16 [n, k], contiguous                 */
+    const uint16_t* bias;     /* fp16 [n] or NULL                        */
+    const uint16_t* residual; /* fp16 [m, n], row stride ldr, or NULL    */
+    int64_t ldr;
+    uint16_t* y;              /* fp16 [m, n], row stride ldy             */
+    int64_t ldy;
+    int64_t m;
+    int32_t n, k;
+    int32_t activation;       /* RPFQ_ACT_NONE or RPFQ_ACT_GELU (erf)    */
+    int32_t block_n;          /* 0 = automatic; else 64, 128 or 256      */
+} RpfqGemmArgs;
+int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
+
+/* Activation quantization of a complex input (per row, Re and Im halves
+ * separately), fp16 in / fp16 out. Replaces ActivationQuantSTE.forward
+ * (RPFQ-ViT-main/quant_models/quant_i.py:442-455). x and xq may alias.
+ * num_bits in 2..8; k = 2 k_c real columns. */
+int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t m, int32_t k,
+                         int32_t num_bits, rpfq_stream_t stream);
+
+/* Whole layer — QATLinearComplexPhase.forward on packed weights
+ * (RPFQ-ViT-main/quant_models/quant_i.py:513-554; Android wideLinear,
+ * phase_linear.cpp:279-326): optional activation quantization, then the
+ * tcgen05 GEMM over the dense coefficients `dense` (from rpfq_prepack_sm100),
+ * bias and optional GELU / residual in the epilogue.
+ * When act_bits > 0, `scratch` must hold m * 2 k_c fp16 values (the quantized
+ * activations); otherwise it may be NULL. */
+typedef struct RpfqWideLinearArgs {
+    const RpfqPackedLinear* layer; /* shapes (n_c, k_c); planes unused when dense != NULL */
+    const uint16_t* dense;         /* fp16 [2 n_c, 2 k_c] from rpfq_prepack_sm100 */
+    const uint16_t* x;             /* fp16 [m, 2 k_c], row stride ldx */
+    int64_t ldx;
+    const uint16_t* bias;          /* fp16 [2 n_c] or NULL */
+    const uint16_t* residual;      /* fp16 [m, 2 n_c] or NULL, row stride ldr */
+    int64_t ldr;
+    uint16_t* y;                   /* fp16 [m, 2 n_c], row stride ldy */
+    int64_t ldy;
+    int64_t m;
+    int32_t act_bits;              /* 0 = no activation quantization, else 2..8 */
+    int32_t activation;            /* RPFQ_ACT_NONE or RPFQ_ACT_GELU */
+    uint16_t* scratch;             /* fp16 [m, 2 k_c] when act_bits > 0 */
+} RpfqWideLinearArgs;
+int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* rpfq_last_error(void);
+
+/* Reads and clears the device-side error word of the current device (a
+ * bounded wait inside a kernel that ran out records its site there).
+ * Synchronises the device. *code_out = 0 when no kernel reported an error. */
+int rpfq_device_error(int32_t* code_out);
+
+/* Library ABI version (major * 100 + minor). */
+int rpfq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RPFQ_B200_H */

@@ -1,0 +1,306 @@
+// K2: persistent, warp-specialised tcgen05 GEMM with a fused epilogue.
+//
+//   y[m, n] = act( x[m, :] . w[n, :] + bias[n] ) (+ residual[m, n])
+//
+// x: fp16 [M, K] (K-major activations, Re half then Im half of each row),
+// w: fp16 [N, K] (the dense coefficient matrix [[rr, ir], [ri, ii]] decoded
+// from the packed phase codes by K1), y / residual: fp16 [M, N]. fp32
+// accumulation in TMEM. One real GEMM carries the whole widely-linear map
+// (four real blocks, 2*M*K*N flops), which is the minimum for U x + W conj(x).
+//
+// CTA = 6 warps, one CTA per SM, persistent over 128 x BN output tiles:
+//   warp 0      TMA producer: x tile [128 x 64] and w tile [BN x 64] per
+//               k-block into a STAGES-deep ring (128-byte swizzle).
+//   warp 1      TMEM owner + MMA issuer: one elected thread issues
+//               4 x tcgen05.mma (K = 16 each) per k-block into one of two
+//               TMEM accumulators (2 x BN fp32 columns), so the epilogue of
+//               tile i overlaps the main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 64 columns per step,
+//               bias / GELU / residual in fp32, fp16 pack, 128-byte swizzled
+//               smem staging per warp, TMA store of [32 x 64] boxes.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace rpfq {
+
+enum : int { kActNone = 0, kActGelu = 1 };
+
+struct GemmParams {
+    const __half* bias;      // [N] or nullptr
+    const __half* residual;  // [M, N] (row stride ldr) or nullptr
+    int64_t ldr;
+    int64_t m;
+    int32_t n, k;
+    int32_t activation;
+    int* err;                // device error word
+};
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int BM = 128;
+    static constexpr int BK = 64;  // 64 fp16 = 128 B = one swizzle row
+    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int EPI_WARPS = 4;
+    static constexpr int EPI_BUF_BYTES = 32 * 128;  // 32 rows x 64 fp16
+    static constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+    static constexpr int THREADS = 192;
+    static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM cols");
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                          const __grid_constant__ CUtensorMap tm_y, const GemmParams p) {
+    using C = GemmCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage_base = smem;
+    uint8_t* epi_base = smem + C::STAGES * C::STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_base + C::EPI_BYTES);
+    uint64_t* full_bar = bars;                       // [STAGES]
+    uint64_t* empty_bar = bars + C::STAGES;          // [STAGES]
+    uint64_t* tfull_bar = bars + 2 * C::STAGES;      // [2]
+    uint64_t* tempty_bar = bars + 2 * C::STAGES + 2; // [2]
+    uint64_t* drain_bar = bars + 2 * C::STAGES + 4;  // [1] teardown drain of MMAs
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    const int num_m = static_cast<int>((p.m + C::BM - 1) / C::BM);
+    const int num_n = (p.n + BN - 1) / BN;
+    const int num_k = (p.k + C::BK - 1) / C::BK;
+    const int num_tiles = num_m * num_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull_bar[b], 1);
+            mbar_init(&tempty_bar[b], C::EPI_WARPS);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tm_x);
+        prefetch_tmap(&tm_w);
+        prefetch_tmap(&tm_y);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / num_n) * C::BM;
+                const int n0 = (tile % num_n) * BN;
+                for (int kb = 0; kb < num_k; ++kb) {
+                    if (!wait_bar(&empty_bar[stage], phase ^ 1, abort_flag, p.err, 101)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+                    tma_load_2d(sa, &tm_x, &full_bar[stage], kb * C::BK, m0);
+                    tma_load_2d(sa + C::A_BYTES, &tm_w, &full_bar[stage], kb * C::BK, n0);
+                    ++issued;
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain: every load issued into the ring must have landed before the
+            // CTA may exit (normally already consumed by the MMA warp).
+            const int pending = issued < C::STAGES ? issued : C::STAGES;
+            for (int i = 1; i <= pending; ++i) {
+                int s = stage - i;
+                uint32_t ph = phase;
+                if (s < 0) {
+                    s += C::STAGES;
+                    ph ^= 1;
+                }
+                volatile int no_abort = 0;
+                wait_bar(&full_bar[s], ph, &no_abort, p.err, 102);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(C::BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                if (!wait_bar(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, 201)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < num_k; ++kb) {
+                    if (!wait_bar(&full_bar[stage], phase, abort_flag, p.err, 202)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(stage_base + stage * C::STAGE_BYTES);
+                    const uint64_t a_desc = umma_desc_sw128_kmajor(a_addr);
+                    const uint64_t b_desc = umma_desc_sw128_kmajor(a_addr + C::A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 16; ++kk) {
+                        // +32 B per K step of 16 fp16 inside the 128-B swizzle row
+                        umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                    }
+                    umma_commit(&empty_bar[stage]);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull_bar[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            // Teardown: make sure no MMA is still writing TMEM before it is freed.
+            umma_commit(drain_bar);
+            volatile int no_abort = 0;
+            wait_bar(drain_bar, 0, &no_abort, p.err, 203);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;  // TMEM lane quarter accessible to this warp
+        uint8_t* stage_buf = epi_base + (warp - 2) * 2 * C::EPI_BUF_BYTES;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        int chunk_count = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
+            tc_fence_after();
+            const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::BM;
+            const int n0 = (tile % num_n) * BN;
+            const int64_t row0 = m0 + 32 * q;
+            const int64_t row = row0 + lane;
+            const bool row_ok = row < p.m;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 64; ++c) {
+                const int col0 = n0 + c * 64;
+                if (col0 >= p.n) break;
+                uint32_t r0[32], r1[32];
+                tmem_ld_32x32b_x32(t_row + c * 64, r0);
+                tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
+                tmem_ld_wait();
+                float v[64];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    v[j] = __uint_as_float(r0[j]);
+                    v[32 + j] = __uint_as_float(r1[j]);
+                }
+                if (p.bias != nullptr) {
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        if (col0 + 8 * g < p.n) {
+                            const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + col0 + 8 * g));
+                            const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 f = __half22float2(bh[e]);
+                                v[8 * g + 2 * e] += f.x;
+                                v[8 * g + 2 * e + 1] += f.y;
+                            }
+                        }
+                    }
+                }
+                if (p.activation == kActGelu) {
+#pragma unroll
+                    for (int j = 0; j < 64; ++j) v[j] = gelu_erf(v[j]);
+                }
+                if (p.residual != nullptr && row_ok) {
+                    const __half* rrow = p.residual + row * p.ldr + col0;
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        if (col0 + 8 * g < p.n) {
+                            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
+                            const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 f = __half22float2(rh[e]);
+                                v[8 * g + 2 * e] += f.x;
+                                v[8 * g + 2 * e + 1] += f.y;
+                            }
+                        }
+                    }
+                }
+                // staging buffer (double-buffered per warp): wait until the TMA
+                // store that last read it has finished reading shared memory.
+                uint8_t* buf = stage_buf + (chunk_count & 1) * C::EPI_BUF_BYTES;
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                    uint4 pk;
+                    __half2 h0 = __floats2half2_rn(v[8 * g + 0], v[8 * g + 1]);
+                    __half2 h1 = __floats2half2_rn(v[8 * g + 2], v[8 * g + 3]);
+                    __half2 h2 = __floats2half2_rn(v[8 * g + 4], v[8 * g + 5]);
+                    __half2 h3 = __floats2half2_rn(v[8 * g + 6], v[8 * g + 7]);
+                    pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                    pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                    pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                    pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                    // 128-B swizzle: 16-B granule g of row `lane` lives at g ^ (lane & 7)
+                    *reinterpret_cast<uint4*>(buf + lane * 128 + ((g ^ (lane & 7)) << 4)) = pk;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && row0 < p.m) {
+                    tma_store_2d(&tm_y, buf, col0, static_cast<int32_t>(row0));
+                }
+                if (lane == 0) bulk_commit_group();
+                ++chunk_count;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace rpfq

@@ -1,0 +1,385 @@
+// C ABI of the B200 packed complex-phase linear layer (declared in
+// include/rpfq_b200.h). Host-side validation, TMA descriptor encoding and
+// launches; the kernels live in the included .cuh files. One translation unit
+// so that all kernels share the device error word without relocatable code.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/rpfq_b200.h"
+#include "actquant.cuh"
+#include "gemm.cuh"
+#include "prepack.cuh"
+
+namespace rpfq {
+
+// Device-side error word: the first bounded wait that runs out records its
+// site code here (see ptx.cuh wait_bar). Read and cleared by rpfq_device_error.
+__device__ int g_device_error;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define RPFQ_CUDA(call)                                                                                    \
+    do {                                                                                                   \
+        cudaError_t e_ = (call);                                                                           \
+        if (e_ != cudaSuccess) return fail(RPFQ_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+// ---------------------------------------------------------------- per-device state
+struct DeviceState {
+    std::once_flag once;
+    int status = RPFQ_OK;
+    std::string error;
+    int sm_count = 0;
+    int* err_word = nullptr;  // device address of g_device_error
+};
+DeviceState g_dev[kMaxDevices];
+
+template <int BN>
+cudaError_t configure_gemm() {
+    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                GemmCfg<BN>::SMEM_BYTES);
+}
+
+// Per-device set-up, done once with that device current: SM count, device
+// error word address, kernel shared-memory limits, arch check.
+int device_state(DeviceState** out) {
+    int dev = 0;
+    RPFQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(RPFQ_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    DeviceState& st = g_dev[dev];
+    std::call_once(st.once, [&st, dev]() {
+        cudaDeviceProp prop;
+        cudaError_t e = cudaGetDeviceProperties(&prop, dev);
+        if (e != cudaSuccess) {
+            st.status = RPFQ_ERR_CUDA;
+            st.error = std::string("cudaGetDeviceProperties: ") + cudaGetErrorString(e);
+            return;
+        }
+        if (prop.major != 10 || prop.minor != 0) {
+            st.status = RPFQ_ERR_UNSUPPORTED;
+            st.error = "this library is built for sm_100a (B200); device is sm_" + std::to_string(prop.major) +
+                       std::to_string(prop.minor);
+            return;
+        }
+        st.sm_count = prop.multiProcessorCount;
+        void* addr = nullptr;
+        e = cudaGetSymbolAddress(&addr, g_device_error);
+        if (e == cudaSuccess) e = configure_gemm<256>();
+        if (e == cudaSuccess) e = configure_gemm<128>();
+        if (e == cudaSuccess) e = configure_gemm<64>();
+        if (e != cudaSuccess) {
+            st.status = RPFQ_ERR_CUDA;
+            st.error = std::string("device set-up: ") + cudaGetErrorString(e);
+            return;
+        }
+        st.err_word = static_cast<int*>(addr);
+    });
+    if (st.status != RPFQ_OK) return fail(st.status, "%s", st.error.c_str());
+    *out = &st;
+    return RPFQ_OK;
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn* out) {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    static std::string err;
+    std::call_once(once, []() {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr) {
+            err = "cuTensorMapEncodeTiled is not available from the driver";
+            return;
+        }
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) return fail(RPFQ_ERR_CUDA, "%s", err.c_str());
+    *out = fn;
+    return RPFQ_OK;
+}
+
+// Row-major fp16 matrix [rows, cols] (row stride ld elements), box [box_rows, box_cols], 128-B swizzle.
+int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                  int box_cols) {
+    EncodeTiledFn fn;
+    int rc = encode_fn(&fn);
+    if (rc) return rc;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a [%lld x %lld] fp16 matrix", (int)r,
+                    (long long)rows, (long long)cols);
+    return RPFQ_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// ---------------------------------------------------------------- GEMM launch
+template <int BN>
+int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
+    using C = GemmCfg<BN>;
+    CUtensorMap tx, tw, ty;
+    int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
+    if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, BN, C::BK);
+    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, 64);
+    if (rc) return rc;
+    GemmParams p;
+    p.bias = reinterpret_cast<const __half*>(a->bias);
+    p.residual = reinterpret_cast<const __half*>(a->residual);
+    p.ldr = a->ldr;
+    p.m = a->m;
+    p.n = a->n;
+    p.k = a->k;
+    p.activation = a->activation;
+    p.err = st->err_word;
+    const int64_t tiles = ((a->m + C::BM - 1) / C::BM) * ((a->n + BN - 1) / BN);
+    const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
+    gemm_f16_sm100_kernel<BN><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, p);
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+int pick_block_n(int64_t m, int n, int sm_count) {
+    // Fewest padded columns first; among equals the widest tile (more reuse of x).
+    int best = 256;
+    int64_t best_cost = -1;
+    for (int bn : {256, 128, 64}) {
+        const int64_t ntiles = (n + bn - 1) / bn;
+        const int64_t padded = ntiles * bn;
+        const int64_t mt = (m + 127) / 128;
+        // waves of the persistent grid, weighted by tile width
+        const int64_t waves = (mt * ntiles + sm_count - 1) / sm_count;
+        const int64_t cost = waves * bn * 4 + padded;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
+    if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: null args");
+    if (!a->x || !a->w || !a->y) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: x, w and y are required");
+    if (a->m < 0 || a->n <= 0 || a->k <= 0) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: bad shape m=%lld n=%d k=%d", (long long)a->m, a->n, a->k);
+    if (a->k % 8 || a->n % 8)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: k (%d) and n (%d) must be multiples of 8", a->k, a->n);
+    if (a->ldx < a->k || a->ldx % 8 || a->ldy < a->n || a->ldy % 8)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: row strides must be >= the row length and multiples of 8");
+    if (a->residual && (a->ldr < a->n || a->ldr % 8))
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: residual row stride must be >= n and a multiple of 8");
+    if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->y) || (a->bias && !aligned16(a->bias)) ||
+        (a->residual && !aligned16(a->residual)))
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: all pointers must be 16-byte aligned");
+    if (a->activation != RPFQ_ACT_NONE && a->activation != RPFQ_ACT_GELU)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: unknown activation %d", a->activation);
+    if (a->m > (int64_t(1) << 31) - 256) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_gemm_sm100: m too large");
+    if (a->m == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    int bn = a->block_n ? a->block_n : pick_block_n(a->m, a->n, st->sm_count);
+    switch (bn) {
+        case 256: return launch_gemm<256>(a, st, stream);
+        case 128: return launch_gemm<128>(a, st, stream);
+        case 64: return launch_gemm<64>(a, st, stream);
+        default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 64, 128 or 256 (got %d)", bn);
+    }
+}
+
+// ---------------------------------------------------------------- packed-layer validation
+int check_layer(const RpfqPackedLinear* l, const char* who) {
+    if (!l) return fail(RPFQ_ERR_INVALID, "%s: null layer", who);
+    if (l->n_c <= 0 || l->k_c <= 0) return fail(RPFQ_ERR_INVALID, "%s: n_c and k_c must be positive", who);
+    if (l->n_cp % 256 || l->k_cp % 256 || l->n_cp < l->n_c || l->k_cp < l->k_c)
+        return fail(RPFQ_ERR_INVALID,
+                    "%s: padded dims must be multiples of 256 covering the valid dims (n_c=%d n_cp=%d k_c=%d k_cp=%d)",
+                    who, l->n_c, l->n_cp, l->k_c, l->k_cp);
+    if (l->stages < 1 || l->stages > 4) return fail(RPFQ_ERR_INVALID, "%s: stages must be 1..4 (got %d)", who, l->stages);
+    if (l->code_bits < 2 || l->code_bits > 4)
+        return fail(RPFQ_ERR_INVALID, "%s: code_bits must be 2, 3 or 4 (got %d)", who, l->code_bits);
+    return RPFQ_OK;
+}
+
+int check_planes(const RpfqPackedLinear* l, const char* who) {
+    for (int s = 0; s < l->stages; ++s) {
+        const RpfqPhasePlane* ps[2] = {&l->u[s], &l->w[s]};
+        for (const RpfqPhasePlane* p : ps)
+            if (!p->codes || !p->gamma_real || !p->gamma_imag)
+                return fail(RPFQ_ERR_INVALID, "%s: stage %d has a null codes/gamma pointer", who, s);
+    }
+    return RPFQ_OK;
+}
+
+}  // namespace
+}  // namespace rpfq
+
+using namespace rpfq;
+
+extern "C" {
+
+int rpfq_version(void) { return 100; }
+
+const char* rpfq_last_error(void) { return g_last_error.c_str(); }
+
+int rpfq_device_error(int32_t* code_out) {
+    if (!code_out) return fail(RPFQ_ERR_INVALID, "rpfq_device_error: null output");
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    RPFQ_CUDA(cudaDeviceSynchronize());
+    int v = 0, zero = 0;
+    RPFQ_CUDA(cudaMemcpy(&v, st->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+    RPFQ_CUDA(cudaMemcpy(st->err_word, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    *code_out = v;
+    return RPFQ_OK;
+}
+
+int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32_t rounding,
+                       rpfq_stream_t stream) {
+    int rc = check_layer(layer, "rpfq_prepack_sm100");
+    if (!rc) rc = check_planes(layer, "rpfq_prepack_sm100");
+    if (rc) return rc;
+    if (!dense_out) return fail(RPFQ_ERR_INVALID, "rpfq_prepack_sm100: null output");
+    if (rounding != RPFQ_ROUND_NEAREST_EVEN && rounding != RPFQ_ROUND_TIES_AWAY)
+        return fail(RPFQ_ERR_INVALID, "rpfq_prepack_sm100: unknown rounding %d", rounding);
+    DeviceState* st;
+    rc = device_state(&st);
+    if (rc) return rc;
+    PrepackParams p;
+    std::memset(&p, 0, sizeof(p));
+    for (int s = 0; s < layer->stages; ++s) {
+        p.u[s] = {layer->u[s].codes, reinterpret_cast<const __half*>(layer->u[s].gamma_real),
+                  reinterpret_cast<const __half*>(layer->u[s].gamma_imag)};
+        p.w[s] = {layer->w[s].codes, reinterpret_cast<const __half*>(layer->w[s].gamma_real),
+                  reinterpret_cast<const __half*>(layer->w[s].gamma_imag)};
+    }
+    p.stages = layer->stages;
+    p.code_bits = layer->code_bits;
+    p.n_c = layer->n_c;
+    p.k_c = layer->k_c;
+    p.n_cp = layer->n_cp;
+    p.k_cp = layer->k_cp;
+    p.rounding = rounding;
+    // Uniform-phase tables for the 3/4-bit extension: cos/sin of 2 pi c / 2^b
+    // in double, exact zeros kept exact, rounded once to float.
+    const int nphase = 1 << layer->code_bits;
+    for (int c = 0; c < 16; ++c) {
+        double a = 2.0 * M_PI * (c % nphase) / nphase;
+        double cs = std::cos(a), sn = std::sin(a);
+        if (std::fabs(cs) < 1e-12) cs = 0.0;
+        if (std::fabs(sn) < 1e-12) sn = 0.0;
+        p.cos_tab[c] = static_cast<float>(cs);
+        p.sin_tab[c] = static_cast<float>(sn);
+    }
+    p.out = reinterpret_cast<__half*>(dense_out);
+    const int groups = (layer->k_c + 3) / 4;
+    dim3 block(128);
+    dim3 grid((groups + 127) / 128, layer->n_c);
+    prepack_kernel<<<grid, block, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream) {
+    return gemm(args, static_cast<cudaStream_t>(stream));
+}
+
+int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t m, int32_t k,
+                         int32_t num_bits, rpfq_stream_t stream) {
+    if (!x || !xq) return fail(RPFQ_ERR_INVALID, "rpfq_act_quant_sm100: null pointer");
+    if (k <= 0 || k % 2) return fail(RPFQ_ERR_INVALID, "rpfq_act_quant_sm100: k must be positive and even (got %d)", k);
+    if (m < 0 || ldx < k || ldq < k) return fail(RPFQ_ERR_INVALID, "rpfq_act_quant_sm100: bad shape or stride");
+    if (num_bits < 2 || num_bits > 8)
+        return fail(RPFQ_ERR_INVALID, "rpfq_act_quant_sm100: num_bits must be 2..8 (got %d)", num_bits);
+    if (m == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    ActQuantParams p;
+    p.x = reinterpret_cast<const __half*>(x);
+    p.y = reinterpret_cast<__half*>(xq);
+    p.ldx = ldx;
+    p.ldy = ldq;
+    p.m = m;
+    p.k_c = k / 2;
+    p.num_bits = num_bits;
+    const int warps = 8;
+    const int64_t blocks = (m + warps - 1) / warps;
+    if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_act_quant_sm100: m too large");
+    act_quant_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
+    if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_wide_linear_sm100: null args");
+    int rc = check_layer(a->layer, "rpfq_wide_linear_sm100");
+    if (rc) return rc;
+    if (!a->dense)
+        return fail(RPFQ_ERR_INVALID,
+                    "rpfq_wide_linear_sm100: dense coefficients are required (decode them once with rpfq_prepack_sm100)");
+    const int32_t K = 2 * a->layer->k_c;
+    const int32_t N = 2 * a->layer->n_c;
+    const uint16_t* xin = a->x;
+    int64_t ldx = a->ldx;
+    if (a->act_bits != 0) {
+        if (!a->scratch)
+            return fail(RPFQ_ERR_INVALID, "rpfq_wide_linear_sm100: act_bits > 0 needs a scratch buffer of m x %d fp16", K);
+        rc = rpfq_act_quant_sm100(a->x, a->ldx, a->scratch, K, a->m, K, a->act_bits, stream);
+        if (rc) return rc;
+        xin = a->scratch;
+        ldx = K;
+    }
+    RpfqGemmArgs g;
+    std::memset(&g, 0, sizeof(g));
+    g.x = xin;
+    g.ldx = ldx;
+    g.w = a->dense;
+    g.bias = a->bias;
+    g.residual = a->residual;
+    g.ldr = a->ldr;
+    g.y = a->y;
+    g.ldy = a->ldy;
+    g.m = a->m;
+    g.n = N;
+    g.k = K;
+    g.activation = a->activation;
+    return gemm(&g, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

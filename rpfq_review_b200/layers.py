@@ -1,0 +1,173 @@
+"""Drop-in modules for the complex-phase linear layer.
+
+* :class:`QATLinearComplexPhase` keeps the reference module's constructor and
+  ``forward(x) -> y`` contract (RPFQ-ViT-main/quant_models/quant_i.py:475-554),
+  so the model adapters' ``target_linear`` hook (quant_rpfq_vit.py:75-103,
+  quant_rpfq_deit.py:65-92, quant_rpfq_swin.py:64-91) can instantiate it
+  unchanged. Its float weight is packed with the exporter's algorithm (the
+  deployment quantization) and cached until the weight changes.
+* :class:`PackedPhaseLinear` holds the exporter's packed tensors as buffers
+  under the exporter's keys (``u_s0.codes``, ``u_s0.gamma_real``, …,
+  ``bias``), loads them from an exported state dict, and runs the B200 path.
+
+Both run only on CUDA tensors through ``librpfq_b200.so``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .packing import AXIAL_STAGES, BLOCK_SIZE, SUPPORTED_QUANT_METHODS, PackedLayer, pack_linear, round_up
+
+
+class PhasePlane(nn.Module):
+    """Buffers of one residual stage: ``codes``, ``gamma_real``, ``gamma_imag``."""
+
+    def __init__(self, n_cp: int, k_cp: int, code_bits: int = 2, device=None):
+        super().__init__()
+        self.register_buffer("codes", torch.zeros((n_cp, k_cp * code_bits // 8), dtype=torch.uint8, device=device))
+        blocks = k_cp // BLOCK_SIZE
+        self.register_buffer("gamma_real", torch.ones((n_cp, blocks), dtype=torch.float16, device=device))
+        self.register_buffer("gamma_imag", torch.ones((n_cp, blocks), dtype=torch.float16, device=device))
+
+
+class PackedPhaseLinear(nn.Module):
+    """Inference layer over the packed phase-code layout.
+
+    ``forward(x[..., in_features]) -> y[..., out_features]`` computes
+    ``act(U x + W conj(x) + bias)`` (+ ``residual``) with optional activation
+    quantization of x (``act_num_bits``). The dense fp16 coefficients are
+    decoded once on the GPU (K1) and kept as a non-persistent buffer.
+    """
+
+    def __init__(self, in_features: int, out_features: int, stages: int = 2, code_bits: int = 2,
+                 enable_act_quant: bool = False, act_num_bits: int = 4, activation: str = "none",
+                 rounding: str = "rne", device=None):
+        super().__init__()
+        if in_features % 2 or out_features % 2:
+            raise ValueError("Complex-phase QAT requires even in/out features.")
+        self.in_features, self.out_features = in_features, out_features
+        self.n_c, self.k_c = out_features // 2, in_features // 2
+        self.stages, self.code_bits = stages, code_bits
+        self.act_bits = act_num_bits if enable_act_quant else 0
+        self.activation = activation
+        self.rounding = rounding
+        n_cp, k_cp = round_up(self.n_c, BLOCK_SIZE), round_up(self.k_c, BLOCK_SIZE)
+        for tag in ("u", "w"):
+            for s in range(stages):
+                self.add_module(f"{tag}_s{s}", PhasePlane(n_cp, k_cp, code_bits, device))
+        self.register_buffer("bias", torch.zeros(out_features, dtype=torch.float16, device=device))
+        self.register_buffer("dense", None, persistent=False)
+
+    # -- construction ---------------------------------------------------------
+    @classmethod
+    def from_packed(cls, layer: PackedLayer, **kw) -> "PackedPhaseLinear":
+        dev = layer.planes["u_s0"][0].device
+        m = cls(2 * layer.k_c, 2 * layer.n_c, layer.stages, layer.code_bits, device=dev, **kw)
+        for name, (c, gr, gi) in layer.planes.items():
+            plane = getattr(m, name)
+            plane.codes.copy_(c)
+            plane.gamma_real.copy_(gr)
+            plane.gamma_imag.copy_(gi)
+        if layer.bias is not None:
+            m.bias.copy_(layer.bias)
+        return m
+
+    @classmethod
+    def from_state_dict(cls, sd: dict, prefix: str, in_features: int, out_features: int, **kw):
+        """Load an exporter-layout layer (keys ``{prefix}u_s0.codes`` …)."""
+        return cls.from_packed(PackedLayer.from_state_dict(sd, prefix, in_features, out_features), **kw)
+
+    @classmethod
+    def from_linear(cls, linear: nn.Linear, stages: int = 2, **kw) -> "PackedPhaseLinear":
+        """Pack a float ``nn.Linear`` with the exporter's algorithm."""
+        return cls.from_packed(pack_linear(linear.weight, linear.bias, stages), **kw)
+
+    def packed(self) -> PackedLayer:
+        planes = {}
+        for tag in ("u", "w"):
+            for s in range(self.stages):
+                p = getattr(self, f"{tag}_s{s}")
+                planes[f"{tag}_s{s}"] = (p.codes, p.gamma_real, p.gamma_imag)
+        return PackedLayer(self.n_c, self.k_c, self.stages, self.code_bits, planes, self.bias)
+
+    # -- execution ------------------------------------------------------------
+    def prepack(self) -> torch.Tensor:
+        self.dense = ops.prepack(self.packed(), self.rounding)
+        return self.dense
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        if self.dense is None or self.dense.device != x.device:
+            self.prepack()
+        x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
+        r16 = None if residual is None else residual.to(torch.float16)
+        y = ops.wide_linear(x16, self.packed(), self.dense, self.act_bits, self.activation, r16)
+        return y if x.dtype == torch.float16 else y.to(x.dtype)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, stages={self.stages}, "
+                f"code_bits={self.code_bits}, act_bits={self.act_bits}, activation={self.activation}")
+
+
+class QATLinearComplexPhase(nn.Linear):
+    """Drop-in for the reference ``QATLinearComplexPhase`` (quant_i.py:475-554).
+
+    Same constructor and forward contract. The weight is quantized with the
+    exporter's axial residual algorithm into the packed layout (what the
+    deployed model runs) and the product runs on the B200 kernels; the packed
+    form is rebuilt whenever the weight or bias changes.
+
+    Error behaviour follows the reference: odd in/out features and unknown
+    method names raise ``ValueError``. Methods whose weights the packed axial
+    layout cannot represent (``complex_phase_new_v2``, ``complex_phase_next_v1``,
+    different stage counts for U and W, ``enable_rotation=True``) raise
+    ``NotImplementedError``: the reference exporter has no layout for them
+    either (export_rpfq_vit_to_mlx.py:463-468 offers v1 and v2 only).
+    """
+
+    def __init__(self, quant_method_u: str = "complex_phase_v1", quant_method_w: str = "complex_phase_v1",
+                 enable_act_quant: bool = True, act_num_bits: int = 4, enable_rotation: bool = False,
+                 quant_group_size: int = 32, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        if self.in_features % 2 != 0 or self.out_features % 2 != 0:
+            raise ValueError("Complex-phase QAT requires even in/out features.")
+        for m in (quant_method_u, quant_method_w):
+            if m not in SUPPORTED_QUANT_METHODS:
+                raise ValueError(f"Unsupported quantization method: {m}")
+            if m not in AXIAL_STAGES:
+                raise NotImplementedError(f"{m} has no packed phase-code layout; use complex_phase_v1..v4")
+        if AXIAL_STAGES[quant_method_u] != AXIAL_STAGES[quant_method_w]:
+            raise NotImplementedError("the packed layout stores the same number of stages for U and W")
+        if enable_rotation:
+            raise NotImplementedError("the packed phase-code layout has no rotation; use enable_rotation=False")
+        self.quant_method_u, self.quant_method_w = quant_method_u, quant_method_w
+        self.stages = AXIAL_STAGES[quant_method_u]
+        self.enable_act_quant = enable_act_quant
+        self.act_num_bits = act_num_bits
+        self.enable_rotation = enable_rotation
+        self.quant_group_size = quant_group_size
+        self._cache_key = None
+        self._packed: PackedPhaseLinear | None = None
+
+    def _key(self):
+        b = self.bias
+        return (self.weight.device, self.weight.data_ptr(), self.weight._version,
+                None if b is None else (b.data_ptr(), b._version))
+
+    def packed_module(self) -> PackedPhaseLinear:
+        key = self._key()
+        if self._packed is None or key != self._cache_key:
+            with torch.no_grad():
+                layer = pack_linear(self.weight, self.bias, self.stages)
+            self._packed = PackedPhaseLinear.from_packed(layer, enable_act_quant=self.enable_act_quant,
+                                                         act_num_bits=self.act_num_bits)
+            self._packed.prepack()
+            self._cache_key = key
+        return self._packed
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("QATLinearComplexPhase (B200) runs on CUDA tensors only")
+        return self.packed_module()(x)

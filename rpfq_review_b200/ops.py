@@ -1,0 +1,200 @@
+"""PyTorch entry points over the C ABI (``include/rpfq_b200.h``).
+
+Functional wrappers (:func:`prepack`, :func:`gemm`, :func:`act_quant`,
+:func:`wide_linear`) and the ``torch.ops.rpfq`` operators, registered with
+``torch.library`` in the same way the reference registers its GPU op
+(``Library("quant", "DEF")`` + ``define`` + ``impl``,
+RPFQ-ViT-main/quant_models/kernel.py:599-605). Every op has a CUDA
+implementation only: calling one on CPU tensors fails in the dispatcher, and
+a missing library raises — there is no fallback path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .packing import PackedLayer
+
+_ACT = {"none": _lib.ACT_NONE, "gelu": _lib.ACT_GELU, None: _lib.ACT_NONE,
+        _lib.ACT_NONE: _lib.ACT_NONE, _lib.ACT_GELU: _lib.ACT_GELU}
+_ROUND = {"rne": _lib.ROUND_NEAREST_EVEN, "ties_away": _lib.ROUND_TIES_AWAY}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _require(t: torch.Tensor, name: str, dtype=torch.float16):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the packed phase-linear path has no CPU implementation)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _rows(x: torch.Tensor, k: int, name: str):
+    """View ``x[..., k]`` as a 2-D row-major matrix with unit column stride."""
+    if x.shape[-1] != k:
+        raise ValueError(f"{name}: last dim {x.shape[-1]} != {k}")
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    ld = x2.stride(0) if x2.shape[0] > 1 else k
+    return x2, ld
+
+
+def layer_struct(layer: PackedLayer) -> _lib.RpfqPackedLinear:
+    s = _lib.RpfqPackedLinear()
+    s.n_c, s.k_c = layer.n_c, layer.k_c
+    s.n_cp, s.k_cp = layer.n_cp, layer.k_cp
+    s.stages, s.code_bits = layer.stages, layer.code_bits
+    for i in range(layer.stages):
+        for tag, arr in (("u", s.u), ("w", s.w)):
+            c, gr, gi = layer.planes[f"{tag}_s{i}"]
+            arr[i].codes, arr[i].gamma_real, arr[i].gamma_imag = c.data_ptr(), gr.data_ptr(), gi.data_ptr()
+    return s
+
+
+def prepack(layer: PackedLayer, rounding: str = "rne") -> torch.Tensor:
+    """K1: packed planes -> dense fp16 ``[2 n_c, 2 k_c]`` = ``[[rr, ir], [ri, ii]]``."""
+    c0 = layer.planes["u_s0"][0]
+    _require(c0, "codes", torch.uint8)
+    dev = c0.device
+    out = torch.empty((2 * layer.n_c, 2 * layer.k_c), dtype=torch.float16, device=dev)
+    s = layer_struct(layer)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().rpfq_prepack_sm100(ctypes.byref(s), out.data_ptr(), _ROUND[rounding], _stream(dev)),
+                   "rpfq_prepack_sm100")
+    return out
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+         residual: torch.Tensor | None = None, activation="none", block_n: int = 0,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """K2: ``act(x @ w.T + bias) + residual`` with fp16 operands, fp32 accumulation."""
+    _require(x, "x")
+    _require(w, "w")
+    n, k = w.shape
+    if not w.is_contiguous():
+        w = w.contiguous()
+    x2, ldx = _rows(x, k, "x")
+    m = x2.shape[0]
+    if bias is not None:
+        _require(bias, "bias")
+        bias = bias.contiguous()
+    r2, ldr = (None, 0)
+    if residual is not None:
+        _require(residual, "residual")
+        r2, ldr = _rows(residual, n, "residual")
+        if r2.shape[0] != m:
+            raise ValueError("residual rows do not match x")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), dtype=torch.float16, device=x.device)
+    y2, ldy = _rows(out, n, "out")
+    if y2.data_ptr() != out.data_ptr() or y2.shape[0] != m:
+        raise ValueError("out must be a row-major view with unit column stride")
+    a = _lib.RpfqGemmArgs(x=x2.data_ptr(), ldx=ldx, w=w.data_ptr(), bias=_p(bias), residual=_p(r2), ldr=ldr,
+                          y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().rpfq_gemm_sm100(ctypes.byref(a), _stream(x.device)), "rpfq_gemm_sm100")
+    return out
+
+
+def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-row symmetric quantization of the Re / Im halves (ActivationQuantSTE)."""
+    _require(x, "x")
+    k = x.shape[-1]
+    x2, ldx = _rows(x, k, "x")
+    if out is None:
+        out = torch.empty_like(x2)
+    o2, ldo = _rows(out, k, "out")
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().rpfq_act_quant_sm100(x2.data_ptr(), ldx, o2.data_ptr(), ldo, x2.shape[0], k,
+                                                   int(num_bits), _stream(x.device)), "rpfq_act_quant_sm100")
+    return out.reshape(x.shape)
+
+
+def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor, act_bits: int = 0,
+                activation="none", residual: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Whole layer through ``rpfq_wide_linear_sm100``: optional activation
+    quantization, then the GEMM over the prepacked coefficients with bias and
+    epilogue. ``x`` is fp16 ``[..., 2 k_c]``."""
+    _require(x, "x")
+    _require(dense, "dense")
+    K, N = 2 * layer.k_c, 2 * layer.n_c
+    x2, ldx = _rows(x, K, "x")
+    m = x2.shape[0]
+    r2, ldr = (None, 0)
+    if residual is not None:
+        _require(residual, "residual")
+        r2, ldr = _rows(residual, N, "residual")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], N), dtype=torch.float16, device=x.device)
+    y2, ldy = _rows(out, N, "out")
+    scratch = torch.empty((m, K), dtype=torch.float16, device=x.device) if act_bits else None
+    s = layer_struct(layer)
+    a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=dense.data_ptr(), x=x2.data_ptr(), ldx=ldx,
+                                bias=_p(layer.bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
+                                act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch))
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().rpfq_wide_linear_sm100(ctypes.byref(a), _stream(x.device)), "rpfq_wide_linear_sm100")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# torch.ops.rpfq.* (CUDA only)
+# ---------------------------------------------------------------------------
+
+_LIB = torch.library.Library("rpfq", "DEF")
+_LIB.define("gemm(Tensor x, Tensor w, Tensor? bias=None, Tensor? residual=None, int activation=0) -> Tensor")
+_LIB.define("act_quant(Tensor x, int num_bits) -> Tensor")
+_LIB.define("prepack(Tensor[] codes, Tensor[] gamma_real, Tensor[] gamma_imag, int n_c, int k_c, "
+            "int code_bits=2, int rounding=0) -> Tensor")
+_LIB.define("wide_linear(Tensor x, Tensor dense, Tensor? bias, int n_c, int k_c, int act_bits=0, "
+            "int activation=0, Tensor? residual=None) -> Tensor")
+
+
+def _op_gemm(x, w, bias=None, residual=None, activation=0):
+    return gemm(x, w, bias, residual, int(activation))
+
+
+def _op_act_quant(x, num_bits):
+    return act_quant(x, int(num_bits))
+
+
+def _planes_from_lists(codes, gamma_real, gamma_imag, n_c, k_c, code_bits):
+    if len(codes) % 2 or not (len(codes) == len(gamma_real) == len(gamma_imag)):
+        raise ValueError("codes / gammas must list the U stages then the W stages")
+    stages = len(codes) // 2
+    planes = {}
+    for i in range(stages):
+        planes[f"u_s{i}"] = (codes[i], gamma_real[i], gamma_imag[i])
+        planes[f"w_s{i}"] = (codes[stages + i], gamma_real[stages + i], gamma_imag[stages + i])
+    return PackedLayer(int(n_c), int(k_c), stages, int(code_bits), planes, None)
+
+
+def _op_prepack(codes, gamma_real, gamma_imag, n_c, k_c, code_bits=2, rounding=0):
+    layer = _planes_from_lists(codes, gamma_real, gamma_imag, n_c, k_c, code_bits)
+    return prepack(layer, "rne" if int(rounding) == 0 else "ties_away")
+
+
+def _op_wide_linear(x, dense, bias, n_c, k_c, act_bits=0, activation=0, residual=None):
+    _require(x, "x")
+    if tuple(dense.shape) != (2 * int(n_c), 2 * int(k_c)):
+        raise ValueError(f"dense must be [{2 * int(n_c)}, {2 * int(k_c)}], got {tuple(dense.shape)}")
+    if act_bits:
+        x = act_quant(x, int(act_bits))
+    return gemm(x, dense, bias, residual, int(activation))
+
+
+_LIB.impl("gemm", _op_gemm, "CUDA")
+_LIB.impl("act_quant", _op_act_quant, "CUDA")
+_LIB.impl("prepack", _op_prepack, "CUDA")
+_LIB.impl("wide_linear", _op_wide_linear, "CUDA")

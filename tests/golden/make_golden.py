@@ -1,0 +1,130 @@
+#!/usr/bin/env python3
+"""Generate the golden fixtures in tests/golden/ from the reference itself.
+
+Run in a container where the reference checkout is mounted (``--ref``,
+default ``/root/reference``); the fixtures it writes are committed, so the
+tests never need the reference at run time. Fixtures:
+
+* ``golden_exporter.npz`` — the reference exporter
+  (RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py): ``save_quantized_linear``
+  packed planes, ``quantized_forward_weight`` dense weight and the layer output
+  ``F.linear(x, W_q, b)`` for seeded float weights (a generic case, a case
+  full of |re| == |im| ties, and a 1-stage case).
+* ``golden_actquant.npz`` — ``ActivationQuantSTE.forward``
+  (RPFQ-ViT-main/quant_models/quant_i.py:442-455) at 2, 4 and 8 bits,
+  including an all-zero row and exact .5 products.
+* ``golden_qat.npz`` — ``QATLinearComplexPhase.forward`` (quant_i.py:513-554)
+  with complex_phase_v2 on the same weights, act-quant on and off.
+* ``golden_refcpp.npz`` — the reference's C++ runtime built from its sources
+  (oracle/_ref): ``wideLinearReference`` output and the fp16 coefficient
+  planes of ``buildFusedWideLinearCache`` for a seeded synthetic packed layer.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.join(args.ref, "RPFQ-ViTApple", "scripts"))
+    sys.path.insert(0, os.path.join(args.ref, "RPFQ-ViT-main", "quant_models"))
+    sys.path.insert(0, REPO)
+    import export_rpfq_vit_to_mlx as ex  # noqa: E402
+    import quant_i  # noqa: E402
+
+    torch.manual_seed(0)
+    out: dict[str, np.ndarray] = {}
+
+    # ---- exporter cases --------------------------------------------------
+    cases = {
+        "generic": (40, 72, 2, lambda g, n, k: torch.randn(n, k, generator=g) * 0.02),
+        "medium": (70, 260, 2, lambda g, n, k: torch.randn(n, k, generator=g) * 0.05),
+        # integer weights: many |re| == |im| ties and exact zeros
+        "ties": (24, 40, 2, lambda g, n, k: torch.randint(-2, 3, (n, k), generator=g).float()),
+        "onestage": (40, 72, 1, lambda g, n, k: torch.randn(n, k, generator=g) * 0.02),
+    }
+    for name, (n_c, k_c, stages, draw) in cases.items():
+        g = torch.Generator().manual_seed(1000 + n_c + k_c + stages)
+        w = draw(g, 2 * n_c, 2 * k_c)
+        b = torch.randn(2 * n_c, generator=g) * 0.02
+        x = torch.randn(7, 2 * k_c, generator=g)
+        n_cp = ex.round_up(n_c, ex.BLOCK_SIZE)
+        k_cp = ex.round_up(k_c, ex.BLOCK_SIZE)
+        target: dict[str, torch.Tensor] = {}
+        ex.save_quantized_linear(target, "layer", w, b, k_cp, n_cp, stages)
+        dense = ex.quantized_forward_weight(w, stages)
+        y = F.linear(x, dense, target["layer.bias"].float())
+        out[f"{name}.weight"] = w.numpy()
+        out[f"{name}.bias_f32"] = b.numpy()
+        out[f"{name}.x"] = x.numpy()
+        out[f"{name}.dims"] = np.array([n_c, k_c, stages], np.int64)
+        for key, t in target.items():
+            out[f"{name}.{key[len('layer.'):]}"] = t.numpy()
+        out[f"{name}.dense"] = dense.numpy()
+        out[f"{name}.y"] = y.numpy()
+    np.savez_compressed(os.path.join(HERE, "golden_exporter.npz"), **out)
+
+    # ---- activation quantization ------------------------------------------
+    aq: dict[str, np.ndarray] = {}
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(9, 96, generator=g) * 3.0
+    x[3] = 0.0                           # amax clamp at 1e-5
+    x[4, :48] = torch.linspace(-1.0, 1.0, 48)
+    x[5, :48] = torch.arange(48).float() / 47.0 * 7.0 - 3.5   # products near .5
+    x = x.half().float()                  # fp16-representable, as the GPU path sees it
+    aq["x"] = x.numpy()
+    for bits in (2, 4, 8):
+        qr, qi = quant_i.ActivationQuantSTE.forward(None, x[:, :48], x[:, 48:], bits)
+        aq[f"q{bits}"] = torch.cat((qr, qi), dim=-1).numpy()
+    np.savez_compressed(os.path.join(HERE, "golden_actquant.npz"), **aq)
+
+    # ---- QAT module forward (module-interface reference) ------------------
+    qat: dict[str, np.ndarray] = {}
+    gen = cases["generic"]
+    n_c, k_c = gen[0], gen[1]
+    for act in (False, True):
+        layer = quant_i.QATLinearComplexPhase(
+            quant_method_u="complex_phase_v2", quant_method_w="complex_phase_v2",
+            enable_act_quant=act, act_num_bits=4, in_features=2 * k_c, out_features=2 * n_c, bias=True)
+        with torch.no_grad():
+            layer.weight.copy_(torch.from_numpy(out["generic.weight"]))
+            layer.bias.copy_(torch.from_numpy(out["generic.bias_f32"]))
+            y = layer(torch.from_numpy(out["generic.x"]))
+        qat[f"y_act{int(act)}"] = y.numpy()
+    np.savez_compressed(os.path.join(HERE, "golden_qat.npz"), **qat)
+
+    # ---- reference C++ runtime -------------------------------------------
+    from oracle import packed_ref as pr  # noqa: E402
+    from oracle import ref_lib  # noqa: E402
+    if ref_lib.load() is None:
+        raise SystemExit("oracle/_ref/librpfq_ref.so missing: run `make -C oracle` first")
+    rc: dict[str, np.ndarray] = {}
+    n_c, k_c = 100, 300
+    packed = pr.random_packed_numpy(n_c, k_c, seed=11)
+    xr = np.random.default_rng(12).standard_normal((5, 2 * k_c)).astype(np.float16).astype(np.float32)
+    rc["dims"] = np.array([n_c, k_c], np.int64)
+    rc["x"] = xr
+    for key, val in packed.items():
+        rc[f"packed.{key}"] = val
+    rc["y_reference"] = ref_lib.wide_linear(packed, xr, n_c, k_c, mode=0)
+    rc["y_fp16cache"] = ref_lib.wide_linear(packed, xr, n_c, k_c, mode=2, threads=2)
+    for key, val in ref_lib.coefficient_planes(packed, n_c, k_c).items():
+        rc[f"plane.{key}"] = val
+    np.savez_compressed(os.path.join(HERE, "golden_refcpp.npz"), **rc)
+    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+
+
+if __name__ == "__main__":
+    main()

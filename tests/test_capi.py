@@ -1,0 +1,91 @@
+"""CPU tests of the C-ABI library: it loads, exports every symbol that
+include/rpfq_b200.h declares, and its host-side validation rejects bad
+descriptors before anything touches a GPU (no compute call is made here)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from rpfq_review_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    src = open(os.path.join(REPO, "include", "rpfq_b200.h")).read()
+    return sorted(set(re.findall(r"\b(rpfq_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_matches_binding():
+    assert _declared_symbols() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in _declared_symbols():
+        assert hasattr(L, name), name
+    assert L.rpfq_version() >= 100
+
+
+def test_struct_layouts_match_header():
+    """ctypes mirrors of the header structs have the C sizes."""
+    assert ctypes.sizeof(_lib.RpfqPhasePlane) == 24
+    assert ctypes.sizeof(_lib.RpfqPackedLinear) == 6 * 4 + 8 * 24
+    assert ctypes.sizeof(_lib.RpfqGemmArgs) == 8 * 9 + 4 * 4
+
+
+@pytest.mark.parametrize("bad", ["null", "k", "n", "ldx", "act", "block_n"])
+def test_gemm_validation_rejects_before_launch(bad):
+    L = _lib.lib()
+    a = _lib.RpfqGemmArgs(x=16, ldx=64, w=32, y=48, ldy=64, m=4, n=64, k=64)
+    if bad == "null":
+        a.x = None
+    elif bad == "k":
+        a.k = 60
+    elif bad == "n":
+        a.n = 12
+    elif bad == "ldx":
+        a.ldx = 32
+    elif bad == "act":
+        a.activation = 7
+    elif bad == "block_n":
+        a.block_n = 96
+    rc = L.rpfq_gemm_sm100(ctypes.byref(a), None)
+    if bad == "block_n":
+        # block_n is checked after the device set-up, which needs a GPU
+        assert rc != _lib.RPFQ_OK
+        return
+    assert rc == _lib.RPFQ_ERR_INVALID
+    assert L.rpfq_last_error().decode()
+
+
+def test_prepack_validation():
+    L = _lib.lib()
+    s = _lib.RpfqPackedLinear(n_c=10, k_c=10, n_cp=250, k_cp=256, stages=2, code_bits=2)
+    assert L.rpfq_prepack_sm100(ctypes.byref(s), 16, 0, None) == _lib.RPFQ_ERR_INVALID
+    assert b"multiples of 256" in L.rpfq_last_error()
+    s.n_cp = 256
+    s.stages = 5
+    assert L.rpfq_prepack_sm100(ctypes.byref(s), 16, 0, None) == _lib.RPFQ_ERR_INVALID
+    s.stages = 2
+    assert L.rpfq_prepack_sm100(ctypes.byref(s), 16, 0, None) == _lib.RPFQ_ERR_INVALID  # null planes
+    assert b"null" in L.rpfq_last_error()
+
+
+def test_act_quant_validation():
+    L = _lib.lib()
+    assert L.rpfq_act_quant_sm100(16, 8, 16, 8, 4, 7, 4, None) == _lib.RPFQ_ERR_INVALID
+    assert L.rpfq_act_quant_sm100(16, 8, 16, 8, 4, 8, 9, None) == _lib.RPFQ_ERR_INVALID
+    assert L.rpfq_act_quant_sm100(None, 8, 16, 8, 4, 8, 4, None) == _lib.RPFQ_ERR_INVALID
+
+
+def test_torch_ops_registered():
+    import torch
+    import rpfq_review_b200.ops  # noqa: F401
+    for name in ("gemm", "act_quant", "prepack", "wide_linear"):
+        assert hasattr(torch.ops.rpfq, name)
+    # CUDA-only: a CPU call fails in the dispatcher instead of falling back
+    with pytest.raises(Exception):
+        torch.ops.rpfq.act_quant(torch.zeros(2, 8, dtype=torch.float16), 4)

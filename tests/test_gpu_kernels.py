@@ -1,0 +1,247 @@
+"""GPU parity tests of the sm_100a kernels through the C ABI (needs a B200).
+
+Bars (stated per test):
+* K1 decode (prepack): bit-exact fp16 against the oracle's restatement of
+  buildFusedWideLinearCache (RNE) and against the reference C++ cache
+  (ties-away mode).
+* activation quantization: bit-exact fp16 against fp16(ActivationQuantSTE).
+* GEMM / layer: max|y - y_ref| / max|y_ref| <= 1e-3 against the float64
+  oracle; the GEMM against the fp16 coefficients
+  it consumes is held to 2e-3 of the element-wise fp16 output rounding bound.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import packed_ref as pr
+from tests.helpers import from_numpy_packed, rel_err, to_numpy_packed
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = 1e-3
+
+
+def _ops():
+    from rpfq_review_b200 import ops
+    return ops
+
+
+@pytest.mark.parametrize("n_c,k_c,stages", [(384, 384, 2), (1152, 384, 2), (40, 72, 2), (500, 384, 2),
+                                            (48, 48, 2), (37, 130, 1), (64, 300, 3), (96, 260, 4)])
+def test_prepack_bit_exact(cuda, n_c, k_c, stages):
+    from rpfq_review_b200.packing import random_packed
+    layer = random_packed(n_c, k_c, seed=n_c * 7 + k_c, stages=stages, device=cuda)
+    dense = _ops().prepack(layer).cpu().numpy()
+    want = pr.dense_fp16_from_planes(pr.coefficient_planes(to_numpy_packed(layer), n_c, k_c))
+    assert dense.shape == (2 * n_c, 2 * k_c)
+    assert np.array_equal(dense.view(np.uint16), want.view(np.uint16))
+
+
+def test_prepack_ties_away_matches_reference_cpp(cuda):
+    """Ties-away mode reproduces the reference's buildFusedWideLinearCache
+    output (golden_refcpp.npz) bit for bit."""
+    g = np.load(os.path.join(GOLD, "golden_refcpp.npz"))
+    n_c, k_c = (int(v) for v in g["dims"])
+    packed = {k[len("packed."):]: g[k] for k in g.files if k.startswith("packed.")}
+    layer = from_numpy_packed(packed, n_c, k_c, cuda)
+    dense = _ops().prepack(layer, rounding="ties_away").cpu().numpy().view(np.uint16)
+    planes = {"rr": dense[:n_c, :k_c], "ir": dense[:n_c, k_c:], "ri": dense[n_c:, :k_c], "ii": dense[n_c:, k_c:]}
+    for key, val in planes.items():
+        assert np.array_equal(val, g[f"plane.{key}"].view(np.uint16)), key
+
+
+def test_prepack_exhaustive_codes(cuda):
+    """Every byte value 0..255 in every one of the 4 planes (all 4 lanes of
+    each byte), against the oracle decode, bit for bit."""
+    from rpfq_review_b200.packing import random_packed
+    n_c, k_c = 1024, 4  # row r: plane r // 256 holds byte value r % 256
+    layer = random_packed(n_c, k_c, seed=5, device="cpu")
+    for p, name in enumerate(("u_s0", "u_s1", "w_s0", "w_s1")):
+        codes = layer.planes[name][0].clone()
+        codes[p * 256:(p + 1) * 256, 0] = torch.arange(256, dtype=torch.uint8)
+        layer.planes[name] = (codes, *layer.planes[name][1:])
+    np_layer = to_numpy_packed(layer)
+    dense = _ops().prepack(layer.to(cuda)).cpu().numpy()
+    want = pr.dense_fp16_from_planes(pr.coefficient_planes(np_layer, n_c, k_c))
+    assert np.array_equal(dense.view(np.uint16), want.view(np.uint16))
+
+
+@pytest.mark.parametrize("bits", (3, 4))
+def test_prepack_wide_codes(cuda, bits):
+    """3/4-bit uniform-phase extension against the oracle (bit-exact)."""
+    from rpfq_review_b200.packing import random_packed
+    layer = random_packed(200, 300, seed=bits, code_bits=bits, device=cuda)
+    dense = _ops().prepack(layer).cpu().numpy()
+    want = pr.dense_fp16_from_planes(pr.coefficient_planes(to_numpy_packed(layer), 200, 300, code_bits=bits))
+    assert np.array_equal(dense.view(np.uint16), want.view(np.uint16))
+
+
+GEMM_SHAPES = [
+    # (m, n, k)
+    (1576, 768, 768),     # cfg1: ViT-B proj at batch 8
+    (1576, 2304, 768),    # ViT-B qkv
+    (394, 3072, 768),     # ViT-B fc1
+    (394, 768, 3072),     # ViT-B fc2
+    (1, 768, 768),
+    (127, 1000, 768),     # head, partial last tile
+    (129, 96, 96),        # Swin-T stage-1 proj (K tail 96 = 64 + 32)
+    (300, 264, 136),
+    (5000, 384, 384),
+]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+@pytest.mark.parametrize("block_n", [0, 64, 128, 256])
+def test_gemm_matches_fp64(cuda, m, n, k, block_n):
+    g = torch.Generator().manual_seed(m + n + k)
+    x = torch.randn(m, k, generator=g).half()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, generator=g) * 0.1).half()
+    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), block_n=block_n).cpu()
+    ref = x.double() @ w.double().T + b.double()
+    assert rel_err(y.numpy(), ref.numpy()) < TOL
+    # fp32 accumulation: every element within its fp16 output rounding + accumulation slack
+    err = (y.double() - ref).abs()
+    assert torch.all(err <= ref.abs() * 2.0 ** -10 + 1e-3 * ref.abs().max())
+
+
+def test_gemm_epilogue_gelu_residual(cuda):
+    g = torch.Generator().manual_seed(3)
+    m, n, k = 777, 3072, 768
+    x = torch.randn(m, k, generator=g).half()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, generator=g) * 0.1).half()
+    r = torch.randn(m, n, generator=g).half()
+    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=r.to(cuda), activation="gelu").cpu()
+    lin = x.double() @ w.double().T + b.double()
+    ref = torch.nn.functional.gelu(lin) + r.double()
+    assert rel_err(y.numpy(), ref.numpy()) < TOL
+
+
+def test_gemm_strided_rows(cuda):
+    """x and y as column slices of wider buffers (row strides != row length)."""
+    g = torch.Generator().manual_seed(4)
+    big = torch.randn(300, 1024, generator=g).half().to(cuda)
+    w = (torch.randn(256, 768, generator=g) / 28.0).half().to(cuda)
+    out = torch.zeros(300, 512, dtype=torch.float16, device=cuda)
+    _ops().gemm(big[:, 128:896], w, out=out[:, 128:384])
+    ref = big[:, 128:896].double() @ w.double().T
+    assert rel_err(out[:, 128:384].cpu().numpy(), ref.cpu().numpy()) < TOL
+    assert torch.all(out[:, :128] == 0) and torch.all(out[:, 384:] == 0)
+
+
+@pytest.mark.parametrize("bits", (2, 4, 8))
+def test_act_quant_bit_exact(cuda, bits):
+    g = np.load(os.path.join(GOLD, "golden_actquant.npz"))
+    x = torch.from_numpy(g["x"]).half().to(cuda)
+    y = _ops().act_quant(x, bits).cpu().numpy()
+    want = g[f"q{bits}"].astype(np.float16)
+    assert np.array_equal(y.view(np.uint16), want.view(np.uint16))
+
+
+@pytest.mark.parametrize("m,k", [(1576, 768), (33, 3072), (5, 96), (3, 100)])
+def test_act_quant_random_bit_exact(cuda, m, k):
+    gen = torch.Generator().manual_seed(m * k)
+    x = (torch.randn(m, k, generator=gen) * 2).half()
+    y = _ops().act_quant(x.to(cuda), 4).cpu().numpy()
+    want = pr.act_quant(x.float().numpy(), 4).astype(np.float16)
+    assert np.array_equal(y.view(np.uint16), want.view(np.uint16))
+
+
+@pytest.mark.parametrize("act_bits", [0, 4])
+def test_layer_cfg1_vs_reference_path(cuda, act_bits):
+    """cfg1 (M = 8 x 197, K = N = 768): the whole layer against the reference
+    deployment path F.linear(act_quant(x), quantized_forward_weight) in float64."""
+    from rpfq_review_b200 import PackedPhaseLinear
+    from rpfq_review_b200.packing import random_packed
+    layer = random_packed(384, 384, seed=0, device=cuda)
+    mod = PackedPhaseLinear.from_packed(layer, enable_act_quant=act_bits > 0, act_num_bits=act_bits or 4)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(1576, 768, generator=g).half()
+    y = mod(x.to(cuda)).float().cpu().numpy()
+    np_layer = to_numpy_packed(layer)
+    dense = pr.dense_weight_from_packed(np_layer, 384, 384)
+    ref = pr.wide_linear(x.float().numpy(), dense, np_layer["bias"].astype(np.float32),
+                         act_bits=act_bits or None)
+    assert rel_err(y, ref) < TOL
+
+
+def test_layer_against_reference_cpp_golden(cuda):
+    """Against wideLinearReference of the reference's C++ runtime (golden)."""
+    from rpfq_review_b200 import PackedPhaseLinear
+    g = np.load(os.path.join(GOLD, "golden_refcpp.npz"))
+    n_c, k_c = (int(v) for v in g["dims"])
+    packed = {k[len("packed."):]: g[k] for k in g.files if k.startswith("packed.")}
+    mod = PackedPhaseLinear.from_packed(from_numpy_packed(packed, n_c, k_c, cuda))
+    y = mod(torch.from_numpy(g["x"]).to(cuda)).cpu().numpy()
+    assert rel_err(y, g["y_reference"]) < TOL
+
+
+@pytest.mark.parametrize("name", ["generic", "medium", "ties", "onestage"])
+def test_drop_in_module_vs_exporter_golden(cuda, name):
+    """QATLinearComplexPhase (drop-in) packs the float weight like the exporter
+    and matches F.linear(x, quantized_forward_weight(W), b) from the golden."""
+    from rpfq_review_b200 import QATLinearComplexPhase
+    g = np.load(os.path.join(GOLD, "golden_exporter.npz"))
+    n_c, k_c, stages = (int(v) for v in g[f"{name}.dims"])
+    method = f"complex_phase_v{stages}"
+    layer = QATLinearComplexPhase(method, method, False, 4, False, 32, 2 * k_c, 2 * n_c, bias=True).to(cuda)
+    with torch.no_grad():
+        layer.weight.copy_(torch.from_numpy(g[f"{name}.weight"]))
+        layer.bias.copy_(torch.from_numpy(g[f"{name}.bias_f32"]))
+    x = torch.from_numpy(g[f"{name}.x"]).to(cuda)
+    y = layer(x).cpu().numpy()
+    # the GPU path sees x in fp16; compare against the reference path on the same input
+    ref = pr.wide_linear(x.half().float().cpu().numpy(), g[f"{name}.dense"], g[f"{name}.bias"].astype(np.float32))
+    assert rel_err(y, ref) < TOL
+    assert rel_err(y, g[f"{name}.y"]) < 2e-3  # includes fp16 rounding of x itself
+
+
+def test_drop_in_module_act_quant_vs_qat_reference(cuda):
+    """With act-quant 4 bit the drop-in matches the deployment path with
+    ActivationQuantSTE; the reference QAT forward (golden_qat.npz) differs only
+    by the fp16 storage of the scales (the reference's own audit measures the
+    same gap, audit_report.json: max_abs 0.0099 on weights)."""
+    from rpfq_review_b200 import QATLinearComplexPhase
+    g = np.load(os.path.join(GOLD, "golden_exporter.npz"))
+    q = np.load(os.path.join(GOLD, "golden_qat.npz"))
+    n_c, k_c = 40, 72
+    layer = QATLinearComplexPhase("complex_phase_v2", "complex_phase_v2", True, 4, False, 32, 2 * k_c, 2 * n_c,
+                                  bias=True).to(cuda)
+    with torch.no_grad():
+        layer.weight.copy_(torch.from_numpy(g["generic.weight"]))
+        layer.bias.copy_(torch.from_numpy(g["generic.bias_f32"]))
+    x = torch.from_numpy(g["generic.x"]).to(cuda).half()
+    y = layer(x).float().cpu().numpy()
+    ref = pr.wide_linear(x.float().cpu().numpy(), g["generic.dense"], g["generic.bias"].astype(np.float32), act_bits=4)
+    assert rel_err(y, ref) < TOL
+    assert rel_err(y, q["y_act1"]) < 0.05
+
+
+def test_cuda_graph_capture_replays(cuda):
+    """The layer launches no host sync and captures into a CUDA graph."""
+    from rpfq_review_b200 import PackedPhaseLinear
+    from rpfq_review_b200.packing import random_packed
+    mod = PackedPhaseLinear.from_packed(random_packed(384, 384, seed=2, device=cuda), activation="gelu")
+    x = torch.randn(512, 768, device=cuda).half()
+    y0 = mod(x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        mod(x)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y = mod(x)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, y0)
+
+
+def test_no_device_errors_recorded(cuda):
+    from rpfq_review_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
