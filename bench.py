@@ -1,0 +1,480 @@
+#!/usr/bin/env python3
+"""Benchmark: packed complex-phase GEMMs inside ViT-B/16 inference on B200.
+
+Workload: ViT-B/16 at 224x224, 12 layers, d = 768,
+12 heads, MLP 3072, 1000 classes; every linear a 2-bit phase-quantized
+complex layer packed from seeded random init; fp16 activations; a batch of
+256 synthetic N(0, 1) images per GPU. One step = one forward of that batch
+(49 packed GEMMs + patch-embedding GEMM through the tcgen05 kernel, attention
+/ LayerNorm through PyTorch), replayed from a CUDA graph. Multi-GPU: one
+process per GPU (torchrun), a full weight replica per rank, images sharded by
+rank (weak scaling: 256 images per GPU), and one NCCL all-gather of the
+logits per step.
+
+Reported (one JSON line on rank 0):
+* value — images/s over all ranks, device-timed (CUDA events, max over ranks);
+* e2e — the same through the public API from pinned host images, with the
+  host->device copy of the images and the device->host copy of the logits
+  inside the timed region;
+* roofline — the GEMM kernel: algorithmic flops (2 M K N per launch) over its
+  CUDA-event durations inside the timed region, against the measured
+  sustained bf16/fp16 tensor peak;
+* cpu_baseline — the reference's own C++ CPU runtime for the packed layer
+  (oracle/_ref, fp16 coefficient cache, all host threads) plus PyTorch CPU
+  for the rest of the forward, on a bounded sample of images.
+
+``--impl reference`` runs only that CPU implementation (rank 0) and prints
+its line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "complex-GEMM TFLOP/s & ViT-B/16 images/sec at 1/2/4/8 B200 vs roofline"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--model", default="vit_base_patch16_224")
+    ap.add_argument("--batch", type=int, default=256, help="images per GPU")
+    ap.add_argument("--act-bits", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-sample", type=int, default=1, help="images per CPU-baseline step")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline in the GPU arm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--gemm", default=None, help="M,N,K: time one packed layer instead of the model")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [ln.strip().split(", ") for ln in self.file.read().splitlines() if ln.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU side
+def cpu_forward_factory(cfg, model, threads: int):
+    """CPU forward of the same model on host cores: every packed linear through
+    the reference's C++ runtime (fp16 coefficient cache, wide_linear_cache_neon.cpp
+    path, prepared once like the reference loader) when oracle/_ref is built
+    ("reference"), else through the oracle's dense restatement ("port");
+    attention / LayerNorm / GELU through PyTorch CPU in float32."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import ref_lib, vit_ref
+    from oracle import packed_ref as pr
+
+    torch.set_num_threads(threads)
+    kind = "reference" if ref_lib.load() is not None else "port"
+    linears = {}
+    for name, mod in model.quantized_linears():
+        np_layer = vit_ref.packed_to_numpy(mod.packed())
+        if kind == "reference":
+            linears[name] = ref_lib.PreparedLayer(np_layer, mod.n_c, mod.k_c)
+        else:
+            dense = torch.from_numpy(pr.dense_weight_from_packed(np_layer, mod.n_c, mod.k_c))
+            linears[name] = (dense, torch.from_numpy(np_layer["bias"].astype(np.float32)))
+    small = {k: getattr(model, k).float().cpu() for k in ("patch_w", "patch_b", "cls_tokens", "pos_embed",
+                                                          "norm_w", "norm_b")}
+    norms = [{n: getattr(b, n).detach().float().cpu() for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b")}
+             for b in model.blocks]
+
+    def lin(name, t):
+        shape = t.shape
+        if kind == "reference":
+            y = linears[name].run(t.reshape(-1, shape[-1]).numpy(), threads)
+            return torch.from_numpy(y).reshape(*shape[:-1], -1)
+        W, b = linears[name]
+        return F.linear(t, W, b)
+
+    def forward(images):
+        x = images.float()
+        B = x.shape[0]
+        p = cfg.patch
+        pt = x.reshape(B, 3, cfg.img // p, p, cfg.img // p, p).permute(0, 2, 4, 1, 3, 5).reshape(B, -1, 3 * p * p)
+        x = torch.cat((small["cls_tokens"].expand(B, -1, -1), F.linear(pt, small["patch_w"], small["patch_b"])), 1)
+        x = x + small["pos_embed"]
+        d, H = cfg.dim, cfg.heads
+        L = x.shape[1]
+        for i in range(cfg.depth):
+            nm = norms[i]
+            h = F.layer_norm(x, (d,), nm["norm1_w"], nm["norm1_b"], cfg.eps)
+            qkv = lin(f"blocks.{i}.qkv", h).view(B, L, 3, H, d // H).permute(2, 0, 3, 1, 4)
+            a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2]).transpose(1, 2).reshape(B, L, d)
+            x = x + lin(f"blocks.{i}.proj", a)
+            h = F.layer_norm(x, (d,), nm["norm2_w"], nm["norm2_b"], cfg.eps)
+            x = x + lin(f"blocks.{i}.fc2", F.gelu(lin(f"blocks.{i}.fc1", h)))
+        ntok = 2 if cfg.distilled else 1
+        cls = F.layer_norm(x[:, :ntok], (d,), small["norm_w"], small["norm_b"], cfg.eps)
+        logits = lin("head", cls[:, 0].contiguous())
+        if cfg.distilled:
+            logits = (logits + lin("head_dist", cls[:, 1].contiguous())) / 2
+        return logits
+
+    return forward, kind
+
+
+def time_cpu(forward, images, steps: int, warmup: int, budget_s: float | None = None):
+    for _ in range(warmup):
+        forward(images)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        forward(images)
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and time.perf_counter() - t_start > budget_s:
+            break
+    return times
+
+
+# ----------------------------------------------------------------------------- main arms
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+
+    from rpfq_review_b200.vit import CONFIGS, PackedViT
+
+    cfg = CONFIGS[args.model]
+    threads = os.cpu_count() or 1
+    # Same seeded weights as the GPU arm, packed on the CPU (no CUDA involved).
+    model = PackedViT(cfg, "cpu", seed=0, act_bits=args.act_bits, prepack=False)
+    forward, kind = cpu_forward_factory(cfg, model, threads)
+    g = torch.Generator().manual_seed(1234)
+    images = torch.randn(args.cpu_sample, 3, cfg.img, cfg.img, generator=g).half()
+    with torch.no_grad():
+        times = time_cpu(forward, images, args.steps, args.warmup)
+    total = sum(times)
+    value = args.cpu_sample * len(times) / total
+    line = {
+        "metric": METRIC, "value": value, "unit": "images/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) images, seeded random-init packed weights",
+        "config": {"workload": f"{cfg.name} packed 2-bit phase inference (CPU sample)",
+                   "images_per_step": args.cpu_sample, "tokens": cfg.tokens, "act_bits": args.act_bits},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind,
+                         "sample": f"{args.cpu_sample} image(s) per step of the {cfg.name} forward; packed "
+                                   f"linears through the reference C++ fp16-cache runtime "
+                                   f"(oracle/_ref), rest through PyTorch CPU fp32"},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from rpfq_review_b200 import ops
+    from rpfq_review_b200.vit import CONFIGS, PackedViT
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    cfg = CONFIGS[args.model]
+    B = args.batch
+    model = PackedViT(cfg, dev, seed=0, act_bits=args.act_bits)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    images = torch.randn(B, 3, cfg.img, cfg.img, device=dev, generator=g).half()
+    gathered = torch.empty((world * B, cfg.classes), dtype=torch.float32, device=dev) if world > 1 else None
+
+    timer = ops.LaunchTimer()
+    use_graph = not args.no_graph
+    graph = None
+    static_out = None
+    if use_graph:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                model(images)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        ops.set_launch_timer(timer)
+        with torch.cuda.graph(graph):
+            static_out = model(images)
+        ops.set_launch_timer(None)
+        launches_per_step = timer.launches
+
+        def step():
+            graph.replay()
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, static_out)
+            return static_out
+    else:
+        def step():
+            timer.gemm_events.clear()
+            ops.set_launch_timer(timer)
+            out = model(images)
+            ops.set_launch_timer(None)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out)
+            return out
+        timer.launches = 0
+        step()
+        launches_per_step = timer.launches
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    barrier()
+    clk = clocks.stop()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    gemm_ms, gemm_flops = timer.gemm_ms_and_flops()  # last step's launches
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = world * B * args.steps / (max_ms / 1000.0)
+
+    # ---- end to end through the public API: pinned host images -> logits on host
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    host_imgs = images.cpu().pin_memory()
+    host_out = torch.empty((B, cfg.classes), dtype=torch.float32).pin_memory()
+    dev_imgs = images  # the graph's static input buffer
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        dev_imgs.copy_(host_imgs, non_blocking=True)
+        out = step()
+        host_out.copy_(out, non_blocking=True)
+    e1.record()
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * e2e_steps / (float(te.item()) / 1000.0)
+
+    # sanity: the logits are finite
+    finite = bool(torch.isfinite(host_out).all())
+
+    if world > 1:
+        if graph is not None:
+            del graph
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+    flops_img = cfg.gemm_flops_per_image()
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            threads = os.cpu_count() or 1
+            forward, kind = cpu_forward_factory(cfg, model, threads)
+            gc = torch.Generator().manual_seed(99)
+            sample = torch.randn(args.cpu_sample, 3, cfg.img, cfg.img, generator=gc).half()
+            with torch.no_grad():
+                times = time_cpu(forward, sample, steps=50, warmup=1, budget_s=args.cpu_seconds)
+            cpu = {"value": args.cpu_sample * len(times) / sum(times), "unit": "images/s", "cores": threads,
+                   "kind": kind,
+                   "sample": f"{len(times)} forward(s) of {args.cpu_sample} image(s) of {cfg.name}; packed linears "
+                             f"through {'the reference C++ fp16-cache runtime (oracle/_ref)' if kind == 'reference' else 'the oracle dense restatement'}, "
+                             "rest PyTorch CPU fp32"}
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {type(e).__name__}: {e}"}
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "images/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic: N(0,1) images (seeded per rank), random-init weights packed to 2-bit phase codes",
+        "config": {
+            "workload": f"{cfg.name} inference, packed 2-bit complex-phase linears (2 residual stages), "
+                        f"batch {B} per GPU",
+            "batch_per_gpu": B, "global_batch": world * B, "tokens": cfg.tokens, "act_bits": args.act_bits,
+            "parallelism": f"dp{world} (weight replica per rank, NCCL all-gather of logits)",
+            "l2": "per-step working set (activations of 49 GEMMs, >= 77 MB each) far larger than the 126 MB L2",
+            "cuda_graph": use_graph,
+        },
+        "gemm": {"tflops": achieved, "flops_per_image": flops_img,
+                 "ms_per_step": gemm_ms, "share_of_step": (gemm_ms / (max_ms / args.steps)) if gemm_ms else None},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "peak_source": f"{peak_src} bf16_tflops_sustained (cuBLAS, power-capped loop)",
+                     "kernel": "gemm_f16_sm100_kernel (tcgen05, 128x256 tiles)"},
+        "e2e": {"value": e2e_value, "unit": "images/s",
+                "h2d_bytes_per_step": int(host_imgs.numel() * host_imgs.element_size()),
+                "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size())},
+        "gpu_launches": int(launches_per_step * args.steps),
+        "clocks": clk,
+        "logits_finite": finite,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_gemm(args):
+    """--gemm M,N,K: one packed complex-phase layer (synthetic cfg1-style
+    weights: uniform 2-bit codes, lognormal(0, 0.5) scales) on one GPU — the
+    standalone complex-GEMM sweep of configs[4] and the small case for ncu."""
+    import torch
+
+    from rpfq_review_b200 import PackedPhaseLinear
+    from rpfq_review_b200.packing import random_packed
+
+    m, n, k = (int(v) for v in args.gemm.split(","))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layer = random_packed(n // 2, k // 2, seed=0, device=dev)
+    mod = PackedPhaseLinear.from_packed(layer, enable_act_quant=args.act_bits > 0, act_num_bits=args.act_bits or 4)
+    mod.prepack()
+    g = torch.Generator(device=dev).manual_seed(1)
+    # two input / output sets, alternated, so that consecutive launches do not
+    # find their operands in L2 when the set is larger than L2
+    xs = [torch.randn(m, k, device=dev, generator=g).half() for _ in range(2)]
+    ys = [torch.empty(m, n, device=dev, dtype=torch.float16) for _ in range(2)]
+    from rpfq_review_b200 import ops
+    packed = mod.packed()
+
+    def step(i):
+        ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = 2 * m * n * k
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    tf = flops / (ms / 1000) / 1e12
+    hbm_bytes = 2 * m * k + 2 * m * n + n * k // 4 + 2 * n
+    print(json.dumps({"metric": "complex-GEMM TFLOP/s", "value": tf, "unit": "TFLOP/s", "shape": [m, n, k],
+                      "us_per_launch": ms * 1000, "act_bits": args.act_bits,
+                      "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                   "frac": tf / peak, "peak_source": f"{src} bf16_tflops (burst)"},
+                      "hbm_gbs_algorithmic": hbm_bytes / (ms / 1000) / 1e9}))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.gemm:
+        return run_gemm(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -94,8 +94,21 @@ class PackedPhaseLinear(nn.Module):
         return PackedLayer(self.n_c, self.k_c, self.stages, self.code_bits, planes, self.bias)
 
     # -- execution ------------------------------------------------------------
+    @property
+    def _aligned(self) -> bool:
+        # The TMA path needs 16-byte row strides: real K and N multiples of 8.
+        return self.in_features % 8 == 0 and self.out_features % 8 == 0
+
     def prepack(self) -> torch.Tensor:
-        self.dense = ops.prepack(self.packed(), self.rounding)
+        """Decode the packed planes once (K1). Layers whose real dims are not
+        multiples of 8 keep a zero-padded copy ``[N8, K8]`` for the GEMM."""
+        dense = ops.prepack(self.packed(), self.rounding)
+        if not self._aligned:
+            n8, k8 = round_up(self.out_features, 8), round_up(self.in_features, 8)
+            padded = torch.zeros((n8, k8), dtype=torch.float16, device=dense.device)
+            padded[: self.out_features, : self.in_features] = dense
+            dense = padded
+        self.dense = dense
         return self.dense
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
@@ -103,8 +116,29 @@ class PackedPhaseLinear(nn.Module):
             self.prepack()
         x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
         r16 = None if residual is None else residual.to(torch.float16)
-        y = ops.wide_linear(x16, self.packed(), self.dense, self.act_bits, self.activation, r16)
+        if self._aligned:
+            y = ops.wide_linear(x16, self.packed(), self.dense, self.act_bits, self.activation, r16)
+        else:
+            y = self._forward_padded(x16, r16)
         return y if x.dtype == torch.float16 else y.to(x.dtype)
+
+    def _forward_padded(self, x16: torch.Tensor, r16: torch.Tensor | None) -> torch.Tensor:
+        K, N = self.in_features, self.out_features
+        n8, k8 = self.dense.shape
+        lead = x16.shape[:-1]
+        x2 = x16.reshape(-1, K)
+        if self.act_bits:
+            x2 = ops.act_quant(x2.contiguous(), self.act_bits)
+        xp = torch.zeros((x2.shape[0], k8), dtype=torch.float16, device=x16.device)
+        xp[:, :K] = x2
+        bias = torch.zeros(n8, dtype=torch.float16, device=x16.device)
+        bias[:N] = self.bias
+        rp = None
+        if r16 is not None:
+            rp = torch.zeros((x2.shape[0], n8), dtype=torch.float16, device=x16.device)
+            rp[:, :N] = r16.reshape(-1, N)
+        y = ops.gemm(xp, self.dense, bias, rp, self.activation)
+        return y[:, :N].contiguous().reshape(*lead, N)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, stages={self.stages}, "

@@ -27,6 +27,34 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+class LaunchTimer:
+    """Optional instrumentation: CUDA events around every GEMM launch and a
+    count of every kernel this library launches. Events are created with
+    ``external=True`` so that they become event-record nodes when the launches
+    are captured into a CUDA graph (timings are then those of the last replay)."""
+
+    def __init__(self):
+        self.gemm_events: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
+        self.launches = 0
+
+    def gemm_ms_and_flops(self) -> tuple[float, int]:
+        ms = sum(s.elapsed_time(e) for s, e, _ in self.gemm_events)
+        return ms, sum(f for _, _, f in self.gemm_events)
+
+
+_timer: LaunchTimer | None = None
+
+
+def set_launch_timer(timer: LaunchTimer | None) -> None:
+    global _timer
+    _timer = timer
+
+
+def _count_launch(n: int = 1) -> None:
+    if _timer is not None:
+        _timer.launches += n
+
+
 def _p(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
 
@@ -101,8 +129,18 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
         raise ValueError("out must be a row-major view with unit column stride")
     a = _lib.RpfqGemmArgs(x=x2.data_ptr(), ldx=ldx, w=w.data_ptr(), bias=_p(bias), residual=_p(r2), ldr=ldr,
                           y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n)
+    timer = _timer
     with torch.cuda.device(x.device):
+        if timer is not None:
+            ev0 = torch.cuda.Event(enable_timing=True, external=True)
+            ev1 = torch.cuda.Event(enable_timing=True, external=True)
+            ev0.record()
         _lib.check(_lib.lib().rpfq_gemm_sm100(ctypes.byref(a), _stream(x.device)), "rpfq_gemm_sm100")
+        if timer is not None:
+            ev1.record()
+            timer.gemm_events.append((ev0, ev1, 2 * m * n * k))
+    if m:
+        _count_launch()
     return out
 
 
@@ -117,6 +155,8 @@ def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -
     with torch.cuda.device(x.device):
         _lib.check(_lib.lib().rpfq_act_quant_sm100(x2.data_ptr(), ldx, o2.data_ptr(), ldo, x2.shape[0], k,
                                                    int(num_bits), _stream(x.device)), "rpfq_act_quant_sm100")
+    if x2.shape[0]:
+        _count_launch()
     return out.reshape(x.shape)
 
 
@@ -143,8 +183,19 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor, act_bi
     a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=dense.data_ptr(), x=x2.data_ptr(), ldx=ldx,
                                 bias=_p(layer.bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
                                 act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch))
+    timer = _timer
     with torch.cuda.device(x.device):
+        if timer is not None:
+            # With act_bits > 0 the span also holds the quantization kernel.
+            ev0 = torch.cuda.Event(enable_timing=True, external=True)
+            ev1 = torch.cuda.Event(enable_timing=True, external=True)
+            ev0.record()
         _lib.check(_lib.lib().rpfq_wide_linear_sm100(ctypes.byref(a), _stream(x.device)), "rpfq_wide_linear_sm100")
+        if timer is not None:
+            ev1.record()
+            timer.gemm_events.append((ev0, ev1, 2 * m * N * K))
+    if m:
+        _count_launch(2 if act_bits else 1)
     return out
 
 
