@@ -447,10 +447,22 @@ def run_gemm(args):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    # the timed launches are replayed from one CUDA graph, so that small shapes
+    # measure device time rather than host launch overhead
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        step(0)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            step(i)
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.steps):
-        step(i)
+    graph.replay()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps

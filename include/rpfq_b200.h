@@ -48,6 +48,7 @@ enum {
 };
 
 enum { RPFQ_ACT_NONE = 0, RPFQ_ACT_GELU = 1 };               /* epilogue activation */
+enum { RPFQ_GEMM_OUT_F32 = 1, RPFQ_GEMM_RESIDUAL_F32 = 2 };  /* RpfqGemmArgs.flags */
 enum { RPFQ_ROUND_NEAREST_EVEN = 0, RPFQ_ROUND_TIES_AWAY = 1 }; /* fp32 -> fp16 of K1 */
 
 /* One residual stage of U or W. Replaces PhaseLinearParams
@@ -78,26 +79,29 @@ typedef struct RpfqPackedLinear {
 int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32_t rounding,
                        rpfq_stream_t stream);
 
-/* K2 — y[m, n] = act(x[m, :] . w[n, :] + bias[n]) + residual[m, n], fp16 in/out,
- * fp32 accumulation on tcgen05 tensor cores. Replaces the dense product
- * F.linear(x, q_weight, bias) of QATLinearComplexPhase.forward
- * (RPFQ-ViT-main/quant_models/quant_i.py:554) and the F.linear call of
- * QATLinearComplexPhaseV2_autograd.forward (kernel.py:573).
+/* K2 — y[m, n] = act(x[m, :] . w[n, :] + bias[n]) + residual[m, n], fp16
+ * operands, fp32 accumulation on tcgen05 tensor cores, fp16 or fp32 output
+ * and residual (flags). Replaces the dense product F.linear(x, q_weight, bias)
+ * of QATLinearComplexPhase.forward (RPFQ-ViT-main/quant_models/quant_i.py:554)
+ * and the F.linear call of QATLinearComplexPhaseV2_autograd.forward
+ * (kernel.py:573). y may alias residual (in-place residual add).
  * Requirements: k % 8 == 0, n % 8 == 0, ldx % 8 == 0, ldy % 8 == 0,
  * ldr % 8 == 0, 16-byte aligned x / w / y / bias / residual. */
 typedef struct RpfqGemmArgs {
-    const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements) */
+    const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements)                */
     int64_t ldx;
-    const uint16_t* w;        /* fp16 [n, k], contiguous                 */
-    const uint16_t* bias;     /* fp16 [n] or NULL                        */
-    const uint16_t* residual; /* fp16 [m, n], row stride ldr, or NULL    */
+    const uint16_t* w;        /* fp16 [n, k], contiguous                                */
+    const uint16_t* bias;     /* fp16 [n] or NULL                                       */
+    const void* residual;     /* [m, n] fp16 (fp32 with RPFQ_GEMM_RESIDUAL_F32) or NULL */
     int64_t ldr;
-    uint16_t* y;              /* fp16 [m, n], row stride ldy             */
+    void* y;                  /* [m, n] fp16 (fp32 with RPFQ_GEMM_OUT_F32), stride ldy  */
     int64_t ldy;
     int64_t m;
     int32_t n, k;
-    int32_t activation;       /* RPFQ_ACT_NONE or RPFQ_ACT_GELU (erf)    */
-    int32_t block_n;          /* 0 = automatic; else 64, 128 or 256      */
+    int32_t activation;       /* RPFQ_ACT_NONE or RPFQ_ACT_GELU (erf)                   */
+    int32_t block_n;          /* 0 = automatic; else 64, 128 or 256                     */
+    int32_t flags;            /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32             */
+    int32_t reserved;
 } RpfqGemmArgs;
 int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
 
@@ -107,6 +111,15 @@ int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
  * num_bits in 2..8; k = 2 k_c real columns. */
 int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t m, int32_t k,
                          int32_t num_bits, rpfq_stream_t stream);
+
+/* LayerNorm of an fp32 residual stream row (d = 384, 768 or 1024) into the
+ * fp16 input of the next packed GEMM; with act_bits > 0 the activation
+ * quantization of that GEMM's complex input (ActivationQuantSTE,
+ * RPFQ-ViT-main/quant_models/quant_i.py:442-455) is applied in the same pass.
+ * Replaces the LayerNorm -> quantizer pair in front of the reference's
+ * complex linears (timm Block norm1 / norm2; Android ops/layernorm.cpp:8). */
+int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, const uint16_t* bias, uint16_t* y,
+                         int64_t ldy, int64_t m, int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream);
 
 /* Whole layer — QATLinearComplexPhase.forward on packed weights
  * (RPFQ-ViT-main/quant_models/quant_i.py:513-554; Android wideLinear,
@@ -121,14 +134,16 @@ typedef struct RpfqWideLinearArgs {
     const uint16_t* x;             /* fp16 [m, 2 k_c], row stride ldx */
     int64_t ldx;
     const uint16_t* bias;          /* fp16 [2 n_c] or NULL */
-    const uint16_t* residual;      /* fp16 [m, 2 n_c] or NULL, row stride ldr */
+    const void* residual;          /* [m, 2 n_c] or NULL, row stride ldr (fp32 with RPFQ_GEMM_RESIDUAL_F32) */
     int64_t ldr;
-    uint16_t* y;                   /* fp16 [m, 2 n_c], row stride ldy */
+    void* y;                       /* [m, 2 n_c], row stride ldy (fp32 with RPFQ_GEMM_OUT_F32) */
     int64_t ldy;
     int64_t m;
     int32_t act_bits;              /* 0 = no activation quantization, else 2..8 */
     int32_t activation;            /* RPFQ_ACT_NONE or RPFQ_ACT_GELU */
     uint16_t* scratch;             /* fp16 [m, 2 k_c] when act_bits > 0 */
+    int32_t flags;                 /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32 */
+    int32_t reserved;
 } RpfqWideLinearArgs;
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
 

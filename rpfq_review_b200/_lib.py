@@ -22,6 +22,8 @@ RPFQ_ERR_DEVICE = 4
 
 ACT_NONE = 0
 ACT_GELU = 1
+GEMM_OUT_F32 = 1
+GEMM_RESIDUAL_F32 = 2
 ROUND_NEAREST_EVEN = 0
 ROUND_TIES_AWAY = 1
 
@@ -30,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_prepack_sm100",
     "rpfq_gemm_sm100",
     "rpfq_act_quant_sm100",
+    "rpfq_layernorm_sm100",
     "rpfq_wide_linear_sm100",
     "rpfq_last_error",
     "rpfq_device_error",
@@ -59,6 +62,7 @@ class RpfqGemmArgs(ctypes.Structure):
         ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
         ("m", ctypes.c_int64), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
         ("activation", ctypes.c_int32), ("block_n", ctypes.c_int32),
+        ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32),
     ]
 
 
@@ -73,6 +77,7 @@ class RpfqWideLinearArgs(ctypes.Structure):
         ("m", ctypes.c_int64),
         ("act_bits", ctypes.c_int32), ("activation", ctypes.c_int32),
         ("scratch", ctypes.c_void_p),
+        ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32),
     ]
 
 
@@ -99,11 +104,12 @@ def lib() -> ctypes.CDLL:
         L.rpfq_prepack_sm100.argtypes = [ctypes.POINTER(RpfqPackedLinear), P, I32, P]
         L.rpfq_gemm_sm100.argtypes = [ctypes.POINTER(RpfqGemmArgs), P]
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
+        L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_wide_linear_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_last_error.restype = ctypes.c_char_p
         L.rpfq_device_error.argtypes = [ctypes.POINTER(I32)]
-        for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_wide_linear_sm100",
-                     "rpfq_device_error", "rpfq_version"):
+        for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
+                     "rpfq_wide_linear_sm100", "rpfq_device_error", "rpfq_version"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
         return L

@@ -4,8 +4,9 @@
 //
 // x: fp16 [M, K] (K-major activations, Re half then Im half of each row),
 // w: fp16 [N, K] (the dense coefficient matrix [[rr, ir], [ri, ii]] decoded
-// from the packed phase codes by K1), y / residual: fp16 [M, N]. fp32
-// accumulation in TMEM. One real GEMM carries the whole widely-linear map
+// from the packed phase codes by K1), y / residual: fp16 or fp32 [M, N]
+// (y may alias the residual: each element is read and written by the same
+// thread, before its TMA store). fp32 accumulation in TMEM. One real GEMM carries the whole widely-linear map
 // (four real blocks, 2*M*K*N flops), which is the minimum for U x + W conj(x).
 //
 // CTA = 6 warps, one CTA per SM, persistent over 128 x BN output tiles:
@@ -16,8 +17,9 @@
 //               TMEM accumulators (2 x BN fp32 columns), so the epilogue of
 //               tile i overlaps the main loop of tile i+1.
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 64 columns per step,
-//               bias / GELU / residual in fp32, fp16 pack, 128-byte swizzled
-//               smem staging per warp, TMA store of [32 x 64] boxes.
+//               bias / GELU / residual (fp16 or fp32) in fp32, fp16 or fp32
+//               output, 128-byte swizzled smem staging per warp, TMA store
+//               of [32 rows x 128 B] boxes.
 #pragma once
 
 #include "ptx.cuh"
@@ -28,8 +30,9 @@ enum : int { kActNone = 0, kActGelu = 1 };
 
 struct GemmParams {
     const __half* bias;      // [N] or nullptr
-    const __half* residual;  // [M, N] (row stride ldr) or nullptr
+    const void* residual;    // [M, N] fp16 or fp32 (row stride ldr) or nullptr
     int64_t ldr;
+    int32_t residual_f32;
     int64_t m;
     int32_t n, k;
     int32_t activation;
@@ -45,7 +48,7 @@ struct GemmCfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_WARPS = 4;
-    static constexpr int EPI_BUF_BYTES = 32 * 128;  // 32 rows x 64 fp16
+    static constexpr int EPI_BUF_BYTES = 32 * 128;  // 32 rows x 128 B (64 fp16 or 32 fp32)
     static constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
     static constexpr int BAR_BYTES = 256;
@@ -57,7 +60,7 @@ struct GemmCfg {
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 
-template <int BN>
+template <int BN, bool OUT_F32>
 __global__ void __launch_bounds__(192, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_y, const GemmParams p) {
@@ -195,6 +198,9 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue
+        // Each step handles CW output columns = 128 bytes per row (64 fp16 or
+        // 32 fp32), staged 32 rows x 128 B with the 128-B swizzle, stored by TMA.
+        constexpr int CW = OUT_F32 ? 32 : 64;
         const int q = warp & 3;  // TMEM lane quarter accessible to this warp
         uint8_t* stage_buf = epi_base + (warp - 2) * 2 * C::EPI_BUF_BYTES;
         int acc = 0;
@@ -210,22 +216,22 @@ __global__ void __launch_bounds__(192, 1)
             const bool row_ok = row < p.m;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN / 64; ++c) {
-                const int col0 = n0 + c * 64;
+            for (int c = 0; c < BN / CW; ++c) {
+                const int col0 = n0 + c * CW;
                 if (col0 >= p.n) break;
-                uint32_t r0[32], r1[32];
-                tmem_ld_32x32b_x32(t_row + c * 64, r0);
-                tmem_ld_32x32b_x32(t_row + c * 64 + 32, r1);
-                tmem_ld_wait();
-                float v[64];
+                float v[CW];
+                {
+                    uint32_t r[CW];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    v[j] = __uint_as_float(r0[j]);
-                    v[32 + j] = __uint_as_float(r1[j]);
+                    for (int h = 0; h < CW / 32; ++h)
+                        tmem_ld_32x32b_x32(t_row + c * CW + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(r[j]);
                 }
                 if (p.bias != nullptr) {
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
+                    for (int g = 0; g < CW / 8; ++g) {
                         if (col0 + 8 * g < p.n) {
                             const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + col0 + 8 * g));
                             const __half2* bh = reinterpret_cast<const __half2*>(&bv);
@@ -240,20 +246,34 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 if (p.activation == kActGelu) {
 #pragma unroll
-                    for (int j = 0; j < 64; ++j) v[j] = gelu_erf(v[j]);
+                    for (int j = 0; j < CW; ++j) v[j] = gelu_erf(v[j]);
                 }
                 if (p.residual != nullptr && row_ok) {
-                    const __half* rrow = p.residual + row * p.ldr + col0;
+                    if (p.residual_f32) {
+                        const float* rrow = static_cast<const float*>(p.residual) + row * p.ldr + col0;
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        if (col0 + 8 * g < p.n) {
-                            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
-                            const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+                        for (int g = 0; g < CW / 4; ++g) {
+                            if (col0 + 4 * g < p.n) {
+                                const float4 rv = *reinterpret_cast<const float4*>(rrow + 4 * g);
+                                v[4 * g + 0] += rv.x;
+                                v[4 * g + 1] += rv.y;
+                                v[4 * g + 2] += rv.z;
+                                v[4 * g + 3] += rv.w;
+                            }
+                        }
+                    } else {
+                        const __half* rrow = static_cast<const __half*>(p.residual) + row * p.ldr + col0;
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 f = __half22float2(rh[e]);
-                                v[8 * g + 2 * e] += f.x;
-                                v[8 * g + 2 * e + 1] += f.y;
+                        for (int g = 0; g < CW / 8; ++g) {
+                            if (col0 + 8 * g < p.n) {
+                                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
+                                const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float2 f = __half22float2(rh[e]);
+                                    v[8 * g + 2 * e] += f.x;
+                                    v[8 * g + 2 * e + 1] += f.y;
+                                }
                             }
                         }
                     }
@@ -264,16 +284,23 @@ __global__ void __launch_bounds__(192, 1)
                 if (lane == 0) bulk_wait_group_read<1>();
                 __syncwarp();
 #pragma unroll
-                for (int g = 0; g < 8; ++g) {
+                for (int g = 0; g < 8; ++g) {  // eight 16-B granules per 128-B row
                     uint4 pk;
-                    __half2 h0 = __floats2half2_rn(v[8 * g + 0], v[8 * g + 1]);
-                    __half2 h1 = __floats2half2_rn(v[8 * g + 2], v[8 * g + 3]);
-                    __half2 h2 = __floats2half2_rn(v[8 * g + 4], v[8 * g + 5]);
-                    __half2 h3 = __floats2half2_rn(v[8 * g + 6], v[8 * g + 7]);
-                    pk.x = *reinterpret_cast<uint32_t*>(&h0);
-                    pk.y = *reinterpret_cast<uint32_t*>(&h1);
-                    pk.z = *reinterpret_cast<uint32_t*>(&h2);
-                    pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                    if constexpr (OUT_F32) {
+                        pk.x = __float_as_uint(v[4 * g + 0]);
+                        pk.y = __float_as_uint(v[4 * g + 1]);
+                        pk.z = __float_as_uint(v[4 * g + 2]);
+                        pk.w = __float_as_uint(v[4 * g + 3]);
+                    } else {
+                        __half2 h0 = __floats2half2_rn(v[8 * g + 0], v[8 * g + 1]);
+                        __half2 h1 = __floats2half2_rn(v[8 * g + 2], v[8 * g + 3]);
+                        __half2 h2 = __floats2half2_rn(v[8 * g + 4], v[8 * g + 5]);
+                        __half2 h3 = __floats2half2_rn(v[8 * g + 6], v[8 * g + 7]);
+                        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                        pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                        pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                    }
                     // 128-B swizzle: 16-B granule g of row `lane` lives at g ^ (lane & 7)
                     *reinterpret_cast<uint4*>(buf + lane * 128 + ((g ^ (lane & 7)) << 4)) = pk;
                 }

@@ -1,0 +1,122 @@
+// LayerNorm of the fp32 residual stream into the fp16 input of the next
+// packed GEMM, optionally followed by the activation quantization of that
+// GEMM's complex input (ActivationQuantSTE, quant_i.py:442-455 of the
+// reference), so that the quantized activations are produced in the same
+// pass: one warp per row, the row held in registers.
+//
+//   mean = sum(x) / d;  var = sum((x - mean)^2) / d;  h = (x - mean) * rsqrt(var + eps) * w + b
+//   act_bits > 0:  per Re / Im half of h: s = fl(fl(1 / max(amax, 1e-5)) * qmax),
+//                  h' = fl(clamp(rint(fl(h * s)), qmin, qmax) / s)
+//
+// Loads: float4 per lane, element e of lane l at 4 l + 128 j (+ 0..3).
+#pragma once
+
+#include "ptx.cuh"
+
+namespace rpfq {
+
+struct LayerNormParams {
+    const float* x;
+    const __half* w;
+    const __half* b;
+    __half* y;
+    int64_t ldx, ldy;
+    int64_t m;
+    float eps;
+    int32_t act_bits;
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormParams p) {
+    static_assert(D % 128 == 0, "row length must be a multiple of 128");
+    constexpr int J = D / 128;  // float4 per lane
+    const int warps = blockDim.x >> 5;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= p.m) return;
+    const float* xr = p.x + row * p.ldx;
+    float v[J][4];
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const float4 t = *reinterpret_cast<const float4*>(xr + 128 * j + 4 * lane);
+        v[j][0] = t.x;
+        v[j][1] = t.y;
+        v[j][2] = t.z;
+        v[j][3] = t.w;
+        sum += (t.x + t.y) + (t.z + t.w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / static_cast<float>(D);
+    float sq = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float dlt = v[j][e] - mean;
+            sq += dlt * dlt;
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rstd = rsqrtf(sq / static_cast<float>(D) + p.eps);
+    float amax_re = 0.0f, amax_im = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int col = 128 * j + 4 * lane;
+        const uint2 wv = *reinterpret_cast<const uint2*>(p.w + col);
+        const uint2 bv = *reinterpret_cast<const uint2*>(p.b + col);
+        const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+        const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+        const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bv.x));
+        const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bv.y));
+        const float wf[4] = {w01.x, w01.y, w23.x, w23.y};
+        const float bf[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            v[j][e] = (v[j][e] - mean) * rstd * wf[e] + bf[e];
+            const float a = fabsf(v[j][e]);
+            if (col + e < D / 2)
+                amax_re = fmaxf(amax_re, a);
+            else
+                amax_im = fmaxf(amax_im, a);
+        }
+    }
+    float s_re = 0.0f, s_im = 0.0f, qmax = 0.0f, qmin = 0.0f;
+    if (p.act_bits > 0) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            amax_re = fmaxf(amax_re, __shfl_xor_sync(0xffffffffu, amax_re, o));
+            amax_im = fmaxf(amax_im, __shfl_xor_sync(0xffffffffu, amax_im, o));
+        }
+        qmax = static_cast<float>((1 << (p.act_bits - 1)) - 1);
+        qmin = -static_cast<float>(1 << (p.act_bits - 1));
+        // The quantizer sees the fp16 GEMM input, as in the unfused path.
+        s_re = __fmul_rn(__frcp_rn(fmaxf(__half2float(__float2half_rn(amax_re)), 1e-5f)), qmax);
+        s_im = __fmul_rn(__frcp_rn(fmaxf(__half2float(__float2half_rn(amax_im)), 1e-5f)), qmax);
+    }
+    __half* yr = p.y + row * p.ldy;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int col = 128 * j + 4 * lane;
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            o[e] = v[j][e];
+            if (p.act_bits > 0) {
+                const float s = (col + e < D / 2) ? s_re : s_im;
+                const float h = __half2float(__float2half_rn(o[e]));
+                const float q = fminf(fmaxf(rintf(__fmul_rn(h, s)), qmin), qmax);
+                o[e] = __fdiv_rn(q, s);
+            }
+        }
+        __half2 h01 = __floats2half2_rn(o[0], o[1]);
+        __half2 h23 = __floats2half2_rn(o[2], o[3]);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&h01);
+        pk.y = *reinterpret_cast<uint32_t*>(&h23);
+        *reinterpret_cast<uint2*>(yr + col) = pk;
+    }
+}
+
+}  // namespace rpfq

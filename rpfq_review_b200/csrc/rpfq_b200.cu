@@ -18,6 +18,7 @@
 #include "../../include/rpfq_b200.h"
 #include "actquant.cuh"
 #include "gemm.cuh"
+#include "layernorm.cuh"
 #include "prepack.cuh"
 
 namespace rpfq {
@@ -60,7 +61,10 @@ DeviceState g_dev[kMaxDevices];
 
 template <int BN>
 cudaError_t configure_gemm() {
-    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 GemmCfg<BN>::SMEM_BYTES);
 }
 
@@ -127,21 +131,23 @@ int encode_fn(EncodeTiledFn* out) {
     return RPFQ_OK;
 }
 
-// Row-major fp16 matrix [rows, cols] (row stride ld elements), box [box_rows, box_cols], 128-B swizzle.
+// Row-major matrix [rows, cols] of fp16 (esize 2) or fp32 (esize 4), row
+// stride ld elements, box [box_rows, box_cols], 128-B swizzle.
 int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-                  int box_cols) {
+                  int box_cols, int esize = 2) {
     EncodeTiledFn fn;
     int rc = encode_fn(&fn);
     if (rc) return rc;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
-        return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a [%lld x %lld] fp16 matrix", (int)r,
+        return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a [%lld x %lld] matrix", (int)r,
                     (long long)rows, (long long)cols);
     return RPFQ_OK;
 }
@@ -149,18 +155,19 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // ---------------------------------------------------------------- GEMM launch
-template <int BN>
+template <int BN, bool OUT_F32>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     using C = GemmCfg<BN>;
     CUtensorMap tx, tw, ty;
     int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
     if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, BN, C::BK);
-    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, 64);
+    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, OUT_F32 ? 32 : 64, OUT_F32 ? 4 : 2);
     if (rc) return rc;
     GemmParams p;
     p.bias = reinterpret_cast<const __half*>(a->bias);
-    p.residual = reinterpret_cast<const __half*>(a->residual);
+    p.residual = a->residual;
     p.ldr = a->ldr;
+    p.residual_f32 = (a->flags & RPFQ_GEMM_RESIDUAL_F32) ? 1 : 0;
     p.m = a->m;
     p.n = a->n;
     p.k = a->k;
@@ -168,7 +175,7 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     p.err = st->err_word;
     const int64_t tiles = ((a->m + C::BM - 1) / C::BM) * ((a->n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
-    gemm_f16_sm100_kernel<BN><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, p);
+    gemm_f16_sm100_kernel<BN, OUT_F32><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, p);
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }
@@ -198,6 +205,8 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     if (a->m < 0 || a->n <= 0 || a->k <= 0) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: bad shape m=%lld n=%d k=%d", (long long)a->m, a->n, a->k);
     if (a->k % 8 || a->n % 8)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: k (%d) and n (%d) must be multiples of 8", a->k, a->n);
+    if (a->flags & ~(RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32))
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: unknown flags 0x%x", a->flags);
     if (a->ldx < a->k || a->ldx % 8 || a->ldy < a->n || a->ldy % 8)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: row strides must be >= the row length and multiples of 8");
     if (a->residual && (a->ldr < a->n || a->ldr % 8))
@@ -213,10 +222,11 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     int rc = device_state(&st);
     if (rc) return rc;
     int bn = a->block_n ? a->block_n : pick_block_n(a->m, a->n, st->sm_count);
+    const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
     switch (bn) {
-        case 256: return launch_gemm<256>(a, st, stream);
-        case 128: return launch_gemm<128>(a, st, stream);
-        case 64: return launch_gemm<64>(a, st, stream);
+        case 256: return f32 ? launch_gemm<256, true>(a, st, stream) : launch_gemm<256, false>(a, st, stream);
+        case 128: return f32 ? launch_gemm<128, true>(a, st, stream) : launch_gemm<128, false>(a, st, stream);
+        case 64: return f32 ? launch_gemm<64, true>(a, st, stream) : launch_gemm<64, false>(a, st, stream);
         default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 64, 128 or 256 (got %d)", bn);
     }
 }
@@ -346,6 +356,46 @@ int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t l
     return RPFQ_OK;
 }
 
+int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, const uint16_t* bias, uint16_t* y,
+                         int64_t ldy, int64_t m, int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream) {
+    if (!x || !weight || !bias || !y) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: null pointer");
+    if (m < 0 || ldx < d || ldy < d || ldx % 4 || ldy % 4)
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: bad shape or stride (strides must be multiples of 4)");
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(y) & 7) || (reinterpret_cast<uintptr_t>(weight) & 7) ||
+        (reinterpret_cast<uintptr_t>(bias) & 7))
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: x must be 16-byte and y, weight, bias 8-byte aligned");
+    if (act_bits != 0 && (act_bits < 2 || act_bits > 8))
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: act_bits must be 0 or 2..8 (got %d)", act_bits);
+    if (act_bits != 0 && (d / 2) % 4)
+        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: act-quant fusion needs d/2 %% 4 == 0");
+    if (m == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    LayerNormParams p;
+    p.x = x;
+    p.w = reinterpret_cast<const __half*>(weight);
+    p.b = reinterpret_cast<const __half*>(bias);
+    p.y = reinterpret_cast<__half*>(y);
+    p.ldx = ldx;
+    p.ldy = ldy;
+    p.m = m;
+    p.eps = eps;
+    p.act_bits = act_bits;
+    const int warps = 8;
+    const int64_t blocks = (m + warps - 1) / warps;
+    if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: m too large");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (d) {
+        case 384: layernorm_f32_f16_kernel<384><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
+        case 768: layernorm_f32_f16_kernel<768><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
+        case 1024: layernorm_f32_f16_kernel<1024><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
+        default: return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: row length %d (supported: 384, 768, 1024)", d);
+    }
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
     if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_wide_linear_sm100: null args");
     int rc = check_layer(a->layer, "rpfq_wide_linear_sm100");
@@ -379,6 +429,7 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
     g.n = N;
     g.k = K;
     g.activation = a->activation;
+    g.flags = a->flags;
     return gemm(&g, static_cast<cudaStream_t>(stream));
 }
 

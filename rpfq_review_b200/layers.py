@@ -111,33 +111,51 @@ class PackedPhaseLinear(nn.Module):
         self.dense = dense
         return self.dense
 
-    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None, prequantized: bool = False) -> torch.Tensor:
+        """``x[..., in_features]`` -> ``y[..., out_features]``.
+
+        fp16 and fp32 inputs are supported; the output has the input's dtype
+        unless ``out`` / ``out_dtype`` say otherwise (fp16 or fp32, written by
+        the GEMM epilogue directly). ``residual`` (fp16 or fp32) is added in
+        the epilogue and may be ``out`` itself. ``prequantized=True`` skips the
+        activation quantization (already applied by the producer, e.g. the
+        fused LayerNorm kernel)."""
         if self.dense is None or self.dense.device != x.device:
             self.prepack()
+        if out_dtype is None:
+            out_dtype = out.dtype if out is not None else (x.dtype if x.dtype in (torch.float16, torch.float32)
+                                                           else torch.float16)
         x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
-        r16 = None if residual is None else residual.to(torch.float16)
+        act_bits = 0 if prequantized else self.act_bits
         if self._aligned:
-            y = ops.wide_linear(x16, self.packed(), self.dense, self.act_bits, self.activation, r16)
-        else:
-            y = self._forward_padded(x16, r16)
-        return y if x.dtype == torch.float16 else y.to(x.dtype)
+            return ops.wide_linear(x16, self.packed(), self.dense, act_bits, self.activation, residual, out=out,
+                                   out_dtype=out_dtype)
+        y = self._forward_padded(x16, residual, act_bits, out_dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
-    def _forward_padded(self, x16: torch.Tensor, r16: torch.Tensor | None) -> torch.Tensor:
+    def _forward_padded(self, x16: torch.Tensor, residual: torch.Tensor | None, act_bits: int,
+                        out_dtype: torch.dtype) -> torch.Tensor:
+        """Layers whose K or N is not a multiple of 8: run the GEMM on
+        zero-padded copies (x, bias, residual) and crop the output."""
         K, N = self.in_features, self.out_features
         n8, k8 = self.dense.shape
         lead = x16.shape[:-1]
         x2 = x16.reshape(-1, K)
-        if self.act_bits:
-            x2 = ops.act_quant(x2.contiguous(), self.act_bits)
+        if act_bits:
+            x2 = ops.act_quant(x2.contiguous(), act_bits)
         xp = torch.zeros((x2.shape[0], k8), dtype=torch.float16, device=x16.device)
         xp[:, :K] = x2
         bias = torch.zeros(n8, dtype=torch.float16, device=x16.device)
         bias[:N] = self.bias
         rp = None
-        if r16 is not None:
-            rp = torch.zeros((x2.shape[0], n8), dtype=torch.float16, device=x16.device)
-            rp[:, :N] = r16.reshape(-1, N)
-        y = ops.gemm(xp, self.dense, bias, rp, self.activation)
+        if residual is not None:
+            rp = torch.zeros((x2.shape[0], n8), dtype=residual.dtype, device=x16.device)
+            rp[:, :N] = residual.reshape(-1, N)
+        y = ops.gemm(xp, self.dense, bias, rp, self.activation, out_dtype=out_dtype)
         return y[:, :N].contiguous().reshape(*lead, N)
 
     def extra_repr(self) -> str:

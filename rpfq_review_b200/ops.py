@@ -102,10 +102,26 @@ def prepack(layer: PackedLayer, rounding: str = "rne") -> torch.Tensor:
     return out
 
 
+def _flags(out: torch.Tensor, residual: torch.Tensor | None) -> int:
+    f = 0
+    if out.dtype == torch.float32:
+        f |= _lib.GEMM_OUT_F32
+    elif out.dtype != torch.float16:
+        raise ValueError(f"out must be float16 or float32, got {out.dtype}")
+    if residual is not None:
+        if residual.dtype == torch.float32:
+            f |= _lib.GEMM_RESIDUAL_F32
+        elif residual.dtype != torch.float16:
+            raise ValueError(f"residual must be float16 or float32, got {residual.dtype}")
+    return f
+
+
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, activation="none", block_n: int = 0,
-         out: torch.Tensor | None = None) -> torch.Tensor:
-    """K2: ``act(x @ w.T + bias) + residual`` with fp16 operands, fp32 accumulation."""
+         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """K2: ``act(x @ w.T + bias) + residual`` with fp16 operands, fp32
+    accumulation; ``residual`` and ``out`` may be fp16 or fp32 (and may be the
+    same tensor for an in-place residual add)."""
     _require(x, "x")
     _require(w, "w")
     n, k = w.shape
@@ -118,17 +134,19 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
         bias = bias.contiguous()
     r2, ldr = (None, 0)
     if residual is not None:
-        _require(residual, "residual")
+        if not residual.is_cuda:
+            raise ValueError("residual must be a CUDA tensor")
         r2, ldr = _rows(residual, n, "residual")
         if r2.shape[0] != m:
             raise ValueError("residual rows do not match x")
     if out is None:
-        out = torch.empty((*x.shape[:-1], n), dtype=torch.float16, device=x.device)
+        out = torch.empty((*x.shape[:-1], n), dtype=out_dtype, device=x.device)
     y2, ldy = _rows(out, n, "out")
     if y2.data_ptr() != out.data_ptr() or y2.shape[0] != m:
         raise ValueError("out must be a row-major view with unit column stride")
     a = _lib.RpfqGemmArgs(x=x2.data_ptr(), ldx=ldx, w=w.data_ptr(), bias=_p(bias), residual=_p(r2), ldr=ldr,
-                          y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n)
+                          y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n,
+                          flags=_flags(out, r2))
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:
@@ -140,6 +158,28 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
             ev1.record()
             timer.gemm_events.append((ev0, ev1, 2 * m * n * k))
     if m:
+        _count_launch()
+    return out
+
+
+def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, act_bits: int = 0,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm of an fp32 ``x[..., d]`` into fp16, with the activation
+    quantization of the next packed GEMM fused in when ``act_bits > 0``."""
+    if not x.is_cuda or x.dtype != torch.float32:
+        raise ValueError("layernorm: x must be a float32 CUDA tensor")
+    _require(weight, "weight")
+    _require(bias, "bias")
+    d = x.shape[-1]
+    x2, ldx = _rows(x, d, "x")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    y2, ldy = _rows(out, d, "out")
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().rpfq_layernorm_sm100(x2.data_ptr(), ldx, weight.data_ptr(), bias.data_ptr(),
+                                                   y2.data_ptr(), ldy, x2.shape[0], d, float(eps), int(act_bits),
+                                                   _stream(x.device)), "rpfq_layernorm_sm100")
+    if x2.shape[0]:
         _count_launch()
     return out
 
@@ -162,10 +202,11 @@ def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -
 
 def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor, act_bits: int = 0,
                 activation="none", residual: torch.Tensor | None = None,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
     """Whole layer through ``rpfq_wide_linear_sm100``: optional activation
     quantization, then the GEMM over the prepacked coefficients with bias and
-    epilogue. ``x`` is fp16 ``[..., 2 k_c]``."""
+    epilogue. ``x`` is fp16 ``[..., 2 k_c]``; ``residual`` / ``out`` fp16 or
+    fp32 (``out`` may be ``residual`` for an in-place residual add)."""
     _require(x, "x")
     _require(dense, "dense")
     K, N = 2 * layer.k_c, 2 * layer.n_c
@@ -173,16 +214,20 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor, act_bi
     m = x2.shape[0]
     r2, ldr = (None, 0)
     if residual is not None:
-        _require(residual, "residual")
+        if not residual.is_cuda:
+            raise ValueError("residual must be a CUDA tensor")
         r2, ldr = _rows(residual, N, "residual")
     if out is None:
-        out = torch.empty((*x.shape[:-1], N), dtype=torch.float16, device=x.device)
+        out = torch.empty((*x.shape[:-1], N), dtype=out_dtype, device=x.device)
     y2, ldy = _rows(out, N, "out")
+    if y2.data_ptr() != out.data_ptr() or y2.shape[0] != m:
+        raise ValueError("out must be a row-major view with unit column stride")
     scratch = torch.empty((m, K), dtype=torch.float16, device=x.device) if act_bits else None
     s = layer_struct(layer)
     a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=dense.data_ptr(), x=x2.data_ptr(), ldx=ldx,
                                 bias=_p(layer.bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
-                                act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch))
+                                act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch),
+                                flags=_flags(out, r2))
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:

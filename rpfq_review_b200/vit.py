@@ -155,27 +155,34 @@ class PackedViT(nn.Module):
 
     @torch.no_grad()
     def forward(self, images: torch.Tensor) -> torch.Tensor:
-        """images fp16 ``[B, 3, 224, 224]`` (already normalised) -> logits fp32 ``[B, classes]``."""
+        """images ``[B, 3, 224, 224]`` (already normalised; fp16 or fp32) ->
+        logits fp32 ``[B, classes]``.
+
+        The residual stream is kept in fp32: LayerNorm reads it and writes the
+        fp16 GEMM input (with the activation quantization fused in when
+        enabled); proj and fc2 add their output to it in place in the GEMM
+        epilogue. GEMM operands are fp16 with fp32 accumulation."""
         cfg = self.cfg
         B = images.shape[0]
         d, H = cfg.dim, cfg.heads
         hd = d // H
+        ab = self.act_bits
         patches = self.patchify(images.to(torch.float16))
-        emb = ops.gemm(patches, self.patch_w, self.patch_b)
+        emb = ops.gemm(patches, self.patch_w, self.patch_b, out_dtype=torch.float32)
         ntok = cfg.tokens - patches.shape[1]
-        x = torch.cat((self.cls_tokens.expand(B, -1, -1), emb), dim=1)
-        x += self.pos_embed
+        x = torch.cat((self.cls_tokens.float().expand(B, -1, -1), emb), dim=1)
+        x += self.pos_embed.float()
         L = cfg.tokens
         for blk in self.blocks:
-            h = F.layer_norm(x, (d,), blk.norm1_w, blk.norm1_b, cfg.eps)
-            qkv = blk.qkv(h).view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
+            h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab)
+            qkv = blk.qkv(h, prequantized=True).view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
             a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2])
             a = a.transpose(1, 2).reshape(B, L, d)
-            x = blk.proj(a, residual=x)
-            h = F.layer_norm(x, (d,), blk.norm2_w, blk.norm2_b, cfg.eps)
-            x = blk.fc2(blk.fc1(h), residual=x)
-        cls = F.layer_norm(x[:, :ntok], (d,), self.norm_w, self.norm_b, cfg.eps)
-        logits = self.head(cls[:, 0].contiguous()).float()
+            blk.proj(a, residual=x, out=x)
+            h = ops.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab)
+            blk.fc2(blk.fc1(h, prequantized=True), residual=x, out=x)
+        cls = ops.layernorm(x[:, :ntok], self.norm_w, self.norm_b, cfg.eps, ab)
+        logits = self.head(cls[:, 0], out_dtype=torch.float32, prequantized=True)
         if self.head_dist is not None:
-            logits = (logits + self.head_dist(cls[:, 1].contiguous()).float()) / 2
+            logits = (logits + self.head_dist(cls[:, 1], out_dtype=torch.float32, prequantized=True)) / 2
         return logits

