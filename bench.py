@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--gemm", default=None, help="M,N,K: time one packed layer instead of the model")
+    ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
+    ap.add_argument("--gemm-breakdown", action="store_true", help="print per-GEMM event times (stderr)")
     return ap.parse_args()
 
 
@@ -311,12 +313,18 @@ def run_b200(args):
     clocks.start()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.cudart().cudaProfilerStart()  # lets `ncu --profile-from-start off` see only the timed steps
     ev0.record()
     for _ in range(args.steps):
         step()
     ev1.record()
     barrier()
+    torch.cuda.cudart().cudaProfilerStop()
     clk = clocks.stop()
+    if args.gemm_breakdown and rank == 0:
+        for s_ev, e_ev, fl in timer.gemm_events:
+            ms_ = s_ev.elapsed_time(e_ev)
+            print(f"gemm {fl / 1e9:8.2f} GFLOP {ms_ * 1000:8.1f} us {fl / ms_ / 1e9:7.1f} TFLOP/s", file=sys.stderr)
     elapsed_ms = ev0.elapsed_time(ev1)
     gemm_ms, gemm_flops = timer.gemm_ms_and_flops()  # last step's launches
     t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
@@ -442,7 +450,10 @@ def run_gemm(args):
     packed = mod.packed()
 
     def step(i):
-        ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1])
+        if args.block_n:
+            ops.gemm(xs[i & 1], mod.dense, mod.bias, block_n=args.block_n, out=ys[i & 1])
+        else:
+            ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1])
 
     for i in range(args.warmup):
         step(i)

@@ -181,17 +181,18 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
 }
 
 int pick_block_n(int64_t m, int n, int sm_count) {
-    // Fewest padded columns first; among equals the widest tile (more reuse of x).
+    // Estimated time ~ waves of the persistent grid x tile width / relative
+    // per-tile efficiency (measured on B200: 128-wide tiles run at ~0.78 and
+    // 64-wide at ~0.42 of the flop rate of 256-wide tiles).
+    const int64_t mt = (m + 127) / 128;
     int best = 256;
-    int64_t best_cost = -1;
+    double best_cost = -1.0;
     for (int bn : {256, 128, 64}) {
+        const double eff = bn == 256 ? 1.0 : (bn == 128 ? 0.78 : 0.42);
         const int64_t ntiles = (n + bn - 1) / bn;
-        const int64_t padded = ntiles * bn;
-        const int64_t mt = (m + 127) / 128;
-        // waves of the persistent grid, weighted by tile width
         const int64_t waves = (mt * ntiles + sm_count - 1) / sm_count;
-        const int64_t cost = waves * bn * 4 + padded;
-        if (best_cost < 0 || cost < best_cost) {
+        const double cost = static_cast<double>(waves) * bn / eff;
+        if (best_cost < 0 || cost < best_cost * 0.999) {
             best_cost = cost;
             best = bn;
         }
