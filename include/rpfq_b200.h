@@ -84,7 +84,8 @@ int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32
  * and residual (flags). Replaces the dense product F.linear(x, q_weight, bias)
  * of QATLinearComplexPhase.forward (RPFQ-ViT-main/quant_models/quant_i.py:554)
  * and the F.linear call of QATLinearComplexPhaseV2_autograd.forward
- * (kernel.py:573). y may alias residual (in-place residual add).
+ * (kernel.py:573). y may alias residual (in-place residual add); the residual
+ * has the output's dtype (RPFQ_GEMM_RESIDUAL_F32 iff RPFQ_GEMM_OUT_F32).
  * Requirements: k % 8 == 0, n % 8 == 0, ldx % 8 == 0, ldy % 8 == 0,
  * ldr % 8 == 0, 16-byte aligned x / w / y / bias / residual. */
 typedef struct RpfqGemmArgs {

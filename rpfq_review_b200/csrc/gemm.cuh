@@ -30,9 +30,8 @@ enum : int { kActNone = 0, kActGelu = 1 };
 
 struct GemmParams {
     const __half* bias;      // [N] or nullptr
-    const void* residual;    // [M, N] fp16 or fp32 (row stride ldr) or nullptr
+    const void* residual;    // [M, N], same dtype as y (row stride ldr), or nullptr
     int64_t ldr;
-    int32_t residual_f32;
     int64_t m;
     int32_t n, k;
     int32_t activation;
@@ -200,25 +199,59 @@ __global__ void __launch_bounds__(192, 1)
         // ------------------------------------------------------------ epilogue
         // Each step handles CW output columns = 128 bytes per row (64 fp16 or
         // 32 fp32), staged 32 rows x 128 B with the 128-B swizzle, stored by TMA.
+        // The residual (same dtype as the output, so also 128 B per row and
+        // step) is prefetched into L2 one tile ahead with bulk prefetches and
+        // loaded into registers one step ahead, so its latency overlaps the
+        // previous step instead of stalling every step.
         constexpr int CW = OUT_F32 ? 32 : 64;
+        constexpr int ESZ = OUT_F32 ? 4 : 2;
         const int q = warp & 3;  // TMEM lane quarter accessible to this warp
         uint8_t* stage_buf = epi_base + (warp - 2) * 2 * C::EPI_BUF_BYTES;
+        const uint8_t* res_base = static_cast<const uint8_t*>(p.residual);
+        // residual row segment of (tile, this thread's row) into L2
+        auto prefetch_tile_residual = [&](int t) {
+            if (res_base == nullptr || t >= num_tiles) return;
+            const int64_t r = static_cast<int64_t>(t / num_n) * C::BM + 32 * q + lane;
+            const int n0t = (t % num_n) * BN;
+            if (r >= p.m) return;
+            const int cols = min(BN, p.n - n0t);
+            prefetch_l2_bulk(res_base + (r * p.ldr + n0t) * ESZ, static_cast<uint32_t>(cols * ESZ));
+        };
+        // one 128-B residual step of this thread's row into registers
+        auto load_residual = [&](int64_t r, int col0, uint4 (&dst)[8]) {
+            const uint4* src = reinterpret_cast<const uint4*>(res_base + (r * p.ldr + col0) * ESZ);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                if (col0 + g * (16 / ESZ) < p.n)
+                    dst[g] = __ldcs(src + g);  // streamed: read once
+                else
+                    dst[g] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        };
+        prefetch_tile_residual(blockIdx.x);
         int acc = 0;
         uint32_t acc_phase = 0;
         int chunk_count = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
-            tc_fence_after();
+            prefetch_tile_residual(tile + gridDim.x);
             const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::BM;
             const int n0 = (tile % num_n) * BN;
             const int64_t row0 = m0 + 32 * q;
             const int64_t row = row0 + lane;
-            const bool row_ok = row < p.m;
+            const bool use_res = res_base != nullptr && row < p.m;
+            const int nsteps = min(BN, p.n - n0 + CW - 1) / CW;  // steps with at least one valid column
+            uint4 rnext[8];
+            if (use_res) load_residual(row, n0, rnext);
+            if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
+            tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN / CW; ++c) {
+            for (int c = 0; c < nsteps; ++c) {
                 const int col0 = n0 + c * CW;
-                if (col0 >= p.n) break;
+                uint4 rcur[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g) rcur[g] = rnext[g];
+                if (use_res && c + 1 < nsteps) load_residual(row, col0 + CW, rnext);
                 float v[CW];
                 {
                     uint32_t r[CW];
@@ -248,32 +281,21 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int j = 0; j < CW; ++j) v[j] = gelu_erf(v[j]);
                 }
-                if (p.residual != nullptr && row_ok) {
-                    if (p.residual_f32) {
-                        const float* rrow = static_cast<const float*>(p.residual) + row * p.ldr + col0;
+                if (use_res) {
 #pragma unroll
-                        for (int g = 0; g < CW / 4; ++g) {
-                            if (col0 + 4 * g < p.n) {
-                                const float4 rv = *reinterpret_cast<const float4*>(rrow + 4 * g);
-                                v[4 * g + 0] += rv.x;
-                                v[4 * g + 1] += rv.y;
-                                v[4 * g + 2] += rv.z;
-                                v[4 * g + 3] += rv.w;
-                            }
-                        }
-                    } else {
-                        const __half* rrow = static_cast<const __half*>(p.residual) + row * p.ldr + col0;
+                    for (int g = 0; g < 8; ++g) {
+                        if constexpr (OUT_F32) {
+                            v[4 * g + 0] += __uint_as_float(rcur[g].x);
+                            v[4 * g + 1] += __uint_as_float(rcur[g].y);
+                            v[4 * g + 2] += __uint_as_float(rcur[g].z);
+                            v[4 * g + 3] += __uint_as_float(rcur[g].w);
+                        } else {
+                            const __half2* rh = reinterpret_cast<const __half2*>(&rcur[g]);
 #pragma unroll
-                        for (int g = 0; g < CW / 8; ++g) {
-                            if (col0 + 8 * g < p.n) {
-                                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
-                                const __half2* rh = reinterpret_cast<const __half2*>(&rv);
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    const float2 f = __half22float2(rh[e]);
-                                    v[8 * g + 2 * e] += f.x;
-                                    v[8 * g + 2 * e + 1] += f.y;
-                                }
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 f = __half22float2(rh[e]);
+                                v[8 * g + 2 * e] += f.x;
+                                v[8 * g + 2 * e + 1] += f.y;
                             }
                         }
                     }

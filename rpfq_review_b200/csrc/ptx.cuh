@@ -101,6 +101,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* s
 
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
+// Fire-and-forget prefetch of a contiguous global range into L2 (16-B aligned,
+// size a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
 template <int N>
 __device__ __forceinline__ void bulk_wait_group_read() {
     asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");

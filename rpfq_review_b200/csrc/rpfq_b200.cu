@@ -167,7 +167,6 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     p.bias = reinterpret_cast<const __half*>(a->bias);
     p.residual = a->residual;
     p.ldr = a->ldr;
-    p.residual_f32 = (a->flags & RPFQ_GEMM_RESIDUAL_F32) ? 1 : 0;
     p.m = a->m;
     p.n = a->n;
     p.k = a->k;
@@ -212,6 +211,8 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: row strides must be >= the row length and multiples of 8");
     if (a->residual && (a->ldr < a->n || a->ldr % 8))
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: residual row stride must be >= n and a multiple of 8");
+    if (a->residual && (((a->flags & RPFQ_GEMM_RESIDUAL_F32) != 0) != ((a->flags & RPFQ_GEMM_OUT_F32) != 0)))
+        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_gemm_sm100: the residual must have the output's dtype");
     if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->y) || (a->bias && !aligned16(a->bias)) ||
         (a->residual && !aligned16(a->residual)))
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: all pointers must be 16-byte aligned");
