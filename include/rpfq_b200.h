@@ -100,7 +100,7 @@ typedef struct RpfqGemmArgs {
     int64_t m;
     int32_t n, k;
     int32_t activation;       /* RPFQ_ACT_NONE or RPFQ_ACT_GELU (erf)                   */
-    int32_t block_n;          /* 0 = automatic; else 64, 128 or 256                     */
+    int32_t block_n;          /* 0 = automatic; else 128 or 256                         */
     int32_t flags;            /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32             */
     int32_t reserved;
 } RpfqGemmArgs;

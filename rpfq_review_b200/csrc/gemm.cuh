@@ -4,22 +4,29 @@
 //
 // x: fp16 [M, K] (K-major activations, Re half then Im half of each row),
 // w: fp16 [N, K] (the dense coefficient matrix [[rr, ir], [ri, ii]] decoded
-// from the packed phase codes by K1), y / residual: fp16 or fp32 [M, N]
-// (y may alias the residual: each element is read and written by the same
-// thread, before its TMA store). fp32 accumulation in TMEM. One real GEMM carries the whole widely-linear map
-// (four real blocks, 2*M*K*N flops), which is the minimum for U x + W conj(x).
+// from the packed phase codes by K1), y / residual: fp16 or fp32 [M, N] (the
+// residual has y's dtype; y may alias it: each element is read and written by
+// the same thread, before its TMA store). fp32 accumulation in TMEM. One real
+// GEMM carries the whole widely-linear map (four real blocks, 2*M*K*N flops),
+// which is the minimum for U x + W conj(x).
 //
-// CTA = 6 warps, one CTA per SM, persistent over 128 x BN output tiles:
-//   warp 0      TMA producer: x tile [128 x 64] and w tile [BN x 64] per
-//               k-block into a STAGES-deep ring (128-byte swizzle).
-//   warp 1      TMEM owner + MMA issuer: one elected thread issues
-//               4 x tcgen05.mma (K = 16 each) per k-block into one of two
-//               TMEM accumulators (2 x BN fp32 columns), so the epilogue of
-//               tile i overlaps the main loop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 64 columns per step,
-//               bias / GELU / residual (fp16 or fp32) in fp32, fp16 or fp32
-//               output, 128-byte swizzled smem staging per warp, TMA store
-//               of [32 rows x 128 B] boxes.
+// CTA = 12 warps in 3 warpgroups, one CTA per SM, persistent over 128 x BN
+// output tiles:
+//   WG0  warp 0   TMA producer: x tile [128 x 64] and w tile [BN x 64] per
+//                 k-block into a STAGES-deep ring (128-byte swizzle).
+//        warp 1   TMEM owner + MMA issuer: one thread issues 4 x tcgen05.mma
+//                 (K = 16 each) per k-block into one of two TMEM accumulators
+//                 (2 x BN fp32 columns), so the epilogue of tile i overlaps
+//                 the main loop of tile i+1.
+//        (WG0 runs with 40 registers per thread: setmaxnreg.dec)
+//   WG1  warps 4..7   epilogue, tile columns [0, BN/2)
+//   WG2  warps 8..11  epilogue, tile columns [BN/2, BN)   (232 registers: setmaxnreg.inc)
+//        Each epilogue warp owns the 32 TMEM lanes (tile rows) of quarter
+//        warp % 4 and walks its column half in steps of 128 bytes of output
+//        per row: tcgen05.ld, bias, GELU, residual (prefetched into L2 one
+//        tile ahead, into registers one step ahead), pack, 128-B-swizzled
+//        smem staging, TMA store of a [32 rows x 128 B] box.
+// Register split: 128 x 40 + 256 x 232 = 64512 = 384 threads x 168 at launch.
 #pragma once
 
 #include "ptx.cuh"
@@ -40,27 +47,52 @@ struct GemmParams {
 
 template <int BN>
 struct GemmCfg {
+    static_assert(BN == 128 || BN == 256, "tile width");
     static constexpr int BM = 128;
     static constexpr int BK = 64;  // 64 fp16 = 128 B = one swizzle row
-    static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int EPI_WARPS = 4;
-    static constexpr int EPI_BUF_BYTES = 32 * 128;  // 32 rows x 128 B (64 fp16 or 32 fp32)
-    static constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int EPI_BUF_BYTES = 32 * 128;  // 32 rows x 128 B, one per epilogue warp
+    static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
-    static constexpr int THREADS = 192;
+    static constexpr int THREADS = 384;
+    static constexpr int LAUNCH_REGS = 168;  // 65536 / 384, rounded down to the allocation granule
+    static constexpr int REGS_PRODUCER = 40;
+    static constexpr int REGS_EPILOGUE = 232;
+    static_assert(128 * REGS_PRODUCER + 256 * REGS_EPILOGUE <= THREADS * LAUNCH_REGS,
+                  "register split exceeds the launch allocation");
     static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM cols");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+// GELU(v) = v/2 (1 + erf(v / sqrt 2)) with erf from Abramowitz & Stegun
+// 7.1.26 (Hastings): erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^{-z^2},
+// t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7. For v < 0 the result is
+// v/2 * (1 - erf(|v|/sqrt 2)), computed directly from the tail term.
+__device__ __forceinline__ float gelu_erf(float v) {
+    const float z = fabsf(v) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    const float poly =
+        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f),
+                 0.254829592f);
+    const float tail = poly * __expf(-z * z);  // = 1 - erf(z)
+    return 0.5f * v * (v >= 0.0f ? 2.0f - tail : tail);
+}
+
+__device__ __forceinline__ void setmaxnreg_dec40() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
+}
+__device__ __forceinline__ void setmaxnreg_inc232() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
+}
 
 template <int BN, bool OUT_F32>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_y, const GemmParams p) {
     using C = GemmCfg<BN>;
@@ -110,9 +142,10 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
+    if (warp < 4) {
+        setmaxnreg_dec40();
+        if (warp == 0 && lane == 0) {
+            // -------------------------------------------------------- producer
             int stage = 0;
             uint32_t phase = 0;
             int issued = 0;
@@ -149,10 +182,8 @@ __global__ void __launch_bounds__(192, 1)
                 volatile int no_abort = 0;
                 wait_bar(&full_bar[s], ph, &no_abort, p.err, 102);
             }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        } else if (warp == 1 && lane == 0) {
+            // -------------------------------------------------------- MMA issuer
             constexpr uint32_t idesc = umma_idesc_f16(C::BM, BN);
             int stage = 0;
             uint32_t phase = 0;
@@ -196,26 +227,25 @@ __global__ void __launch_bounds__(192, 1)
             wait_bar(drain_bar, 0, &no_abort, p.err, 203);
         }
     } else {
+        setmaxnreg_inc232();
         // ------------------------------------------------------------ epilogue
-        // Each step handles CW output columns = 128 bytes per row (64 fp16 or
-        // 32 fp32), staged 32 rows x 128 B with the 128-B swizzle, stored by TMA.
-        // The residual (same dtype as the output, so also 128 B per row and
-        // step) is prefetched into L2 one tile ahead with bulk prefetches and
-        // loaded into registers one step ahead, so its latency overlaps the
-        // previous step instead of stalling every step.
+        // CW output columns per step = 128 bytes per row (64 fp16 or 32 fp32).
         constexpr int CW = OUT_F32 ? 32 : 64;
         constexpr int ESZ = OUT_F32 ? 4 : 2;
-        const int q = warp & 3;  // TMEM lane quarter accessible to this warp
-        uint8_t* stage_buf = epi_base + (warp - 2) * 2 * C::EPI_BUF_BYTES;
+        constexpr int HALF = BN / 2;
+        static_assert(HALF % CW == 0, "column half must hold whole steps");
+        const int q = warp & 3;                // TMEM lane quarter accessible to this warp
+        const int col_half = (warp - 4) >> 2;  // 0: columns [0, BN/2), 1: [BN/2, BN)
+        uint8_t* buf = epi_base + (warp - 4) * C::EPI_BUF_BYTES;
         const uint8_t* res_base = static_cast<const uint8_t*>(p.residual);
-        // residual row segment of (tile, this thread's row) into L2
+        // residual row segment (this warp's half of a tile, this thread's row) into L2
         auto prefetch_tile_residual = [&](int t) {
             if (res_base == nullptr || t >= num_tiles) return;
             const int64_t r = static_cast<int64_t>(t / num_n) * C::BM + 32 * q + lane;
-            const int n0t = (t % num_n) * BN;
-            if (r >= p.m) return;
-            const int cols = min(BN, p.n - n0t);
-            prefetch_l2_bulk(res_base + (r * p.ldr + n0t) * ESZ, static_cast<uint32_t>(cols * ESZ));
+            const int c0 = (t % num_n) * BN + col_half * HALF;
+            if (r >= p.m || c0 >= p.n) return;
+            const int cols = min(HALF, p.n - c0);
+            prefetch_l2_bulk(res_base + (r * p.ldr + c0) * ESZ, static_cast<uint32_t>(cols * ESZ));
         };
         // one 128-B residual step of this thread's row into registers
         auto load_residual = [&](int64_t r, int col0, uint4 (&dst)[8]) {
@@ -231,37 +261,36 @@ __global__ void __launch_bounds__(192, 1)
         prefetch_tile_residual(blockIdx.x);
         int acc = 0;
         uint32_t acc_phase = 0;
-        int chunk_count = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             prefetch_tile_residual(tile + gridDim.x);
             const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::BM;
-            const int n0 = (tile % num_n) * BN;
+            const int c_begin = (tile % num_n) * BN + col_half * HALF;
             const int64_t row0 = m0 + 32 * q;
             const int64_t row = row0 + lane;
             const bool use_res = res_base != nullptr && row < p.m;
-            const int nsteps = min(BN, p.n - n0 + CW - 1) / CW;  // steps with at least one valid column
+            const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
+            const int nsteps = valid > 0 ? (valid + CW - 1) / CW : 0;
             uint4 rnext[8];
-            if (use_res) load_residual(row, n0, rnext);
+            if (use_res && nsteps > 0) load_residual(row, c_begin, rnext);
             if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
             tc_fence_after();
-            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                                   static_cast<uint32_t>(acc * BN + col_half * HALF);
 #pragma unroll 1
             for (int c = 0; c < nsteps; ++c) {
-                const int col0 = n0 + c * CW;
+                const int col0 = c_begin + c * CW;
                 uint4 rcur[8];
 #pragma unroll
                 for (int g = 0; g < 8; ++g) rcur[g] = rnext[g];
                 if (use_res && c + 1 < nsteps) load_residual(row, col0 + CW, rnext);
+                uint32_t r[CW];
+#pragma unroll
+                for (int h = 0; h < CW / 32; ++h)
+                    tmem_ld_32x32b_x32(t_row + c * CW + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
+                tmem_ld_wait();
                 float v[CW];
-                {
-                    uint32_t r[CW];
 #pragma unroll
-                    for (int h = 0; h < CW / 32; ++h)
-                        tmem_ld_32x32b_x32(t_row + c * CW + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(r[j]);
-                }
+                for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(r[j]);
                 if (p.bias != nullptr) {
 #pragma unroll
                     for (int g = 0; g < CW / 8; ++g) {
@@ -300,10 +329,9 @@ __global__ void __launch_bounds__(192, 1)
                         }
                     }
                 }
-                // staging buffer (double-buffered per warp): wait until the TMA
-                // store that last read it has finished reading shared memory.
-                uint8_t* buf = stage_buf + (chunk_count & 1) * C::EPI_BUF_BYTES;
-                if (lane == 0) bulk_wait_group_read<1>();
+                // single staging buffer per warp: wait until the previous TMA
+                // store from it has finished reading shared memory
+                if (lane == 0) bulk_wait_group_read<0>();
                 __syncwarp();
 #pragma unroll
                 for (int g = 0; g < 8; ++g) {  // eight 16-B granules per 128-B row
@@ -328,11 +356,10 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0 && row0 < p.m) {
-                    tma_store_2d(&tm_y, buf, col0, static_cast<int32_t>(row0));
+                if (lane == 0) {
+                    if (row0 < p.m) tma_store_2d(&tm_y, buf, col0, static_cast<int32_t>(row0));
+                    bulk_commit_group();
                 }
-                if (lane == 0) bulk_commit_group();
-                ++chunk_count;
             }
             tc_fence_before();
             __syncwarp();

@@ -94,7 +94,6 @@ int device_state(DeviceState** out) {
         e = cudaGetSymbolAddress(&addr, g_device_error);
         if (e == cudaSuccess) e = configure_gemm<256>();
         if (e == cudaSuccess) e = configure_gemm<128>();
-        if (e == cudaSuccess) e = configure_gemm<64>();
         if (e != cudaSuccess) {
             st.status = RPFQ_ERR_CUDA;
             st.error = std::string("device set-up: ") + cudaGetErrorString(e);
@@ -181,13 +180,13 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
 
 int pick_block_n(int64_t m, int n, int sm_count) {
     // Estimated time ~ waves of the persistent grid x tile width / relative
-    // per-tile efficiency (measured on B200: 128-wide tiles run at ~0.78 and
-    // 64-wide at ~0.42 of the flop rate of 256-wide tiles).
+    // per-tile efficiency (measured on B200: 128-wide tiles run at ~0.78 of
+    // the flop rate of 256-wide tiles).
     const int64_t mt = (m + 127) / 128;
     int best = 256;
     double best_cost = -1.0;
-    for (int bn : {256, 128, 64}) {
-        const double eff = bn == 256 ? 1.0 : (bn == 128 ? 0.78 : 0.42);
+    for (int bn : {256, 128}) {
+        const double eff = bn == 256 ? 1.0 : 0.78;
         const int64_t ntiles = (n + bn - 1) / bn;
         const int64_t waves = (mt * ntiles + sm_count - 1) / sm_count;
         const double cost = static_cast<double>(waves) * bn / eff;
@@ -228,8 +227,7 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     switch (bn) {
         case 256: return f32 ? launch_gemm<256, true>(a, st, stream) : launch_gemm<256, false>(a, st, stream);
         case 128: return f32 ? launch_gemm<128, true>(a, st, stream) : launch_gemm<128, false>(a, st, stream);
-        case 64: return f32 ? launch_gemm<64, true>(a, st, stream) : launch_gemm<64, false>(a, st, stream);
-        default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 64, 128 or 256 (got %d)", bn);
+        default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 128 or 256 (got %d)", bn);
     }
 }
 

@@ -94,7 +94,7 @@ GEMM_SHAPES = [
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
-@pytest.mark.parametrize("block_n", [0, 64, 128, 256])
+@pytest.mark.parametrize("block_n", [0, 128, 256])
 def test_gemm_matches_fp64(cuda, m, n, k, block_n):
     g = torch.Generator().manual_seed(m + n + k)
     x = torch.randn(m, k, generator=g).half()
