@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--gemm", default=None, help="M,N,K: time one packed layer instead of the model")
     ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
+    ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
+                    help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
     ap.add_argument("--gemm-breakdown", action="store_true", help="print per-GEMM event times (stderr)")
     return ap.parse_args()
 
@@ -445,13 +447,17 @@ def run_gemm(args):
     # two input / output sets, alternated, so that consecutive launches do not
     # find their operands in L2 when the set is larger than L2
     xs = [torch.randn(m, k, device=dev, generator=g).half() for _ in range(2)]
-    ys = [torch.empty(m, n, device=dev, dtype=torch.float16) for _ in range(2)]
+    out_dtype = torch.float32 if args.epilogue == "residual_f32" else torch.float16
+    ys = [torch.randn(m, n, device=dev, generator=g).to(out_dtype) for _ in range(2)]
     from rpfq_review_b200 import ops
     packed = mod.packed()
+    act = "gelu" if args.epilogue == "gelu" else "none"
 
     def step(i):
-        if args.block_n:
-            ops.gemm(xs[i & 1], mod.dense, mod.bias, block_n=args.block_n, out=ys[i & 1])
+        res = ys[i & 1] if args.epilogue == "residual_f32" else None
+        if args.block_n or args.epilogue != "none":
+            ops.gemm(xs[i & 1], mod.dense, mod.bias, residual=res, activation=act, block_n=args.block_n,
+                     out=ys[i & 1])
         else:
             ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1])
 
@@ -482,7 +488,10 @@ def run_gemm(args):
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     tf = flops / (ms / 1000) / 1e12
     hbm_bytes = 2 * m * k + 2 * m * n + n * k // 4 + 2 * n
+    if args.epilogue == "residual_f32":
+        hbm_bytes += 6 * m * n
     print(json.dumps({"metric": "complex-GEMM TFLOP/s", "value": tf, "unit": "TFLOP/s", "shape": [m, n, k],
+                      "epilogue": args.epilogue,
                       "us_per_launch": ms * 1000, "act_bits": args.act_bits,
                       "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                                    "frac": tf / peak, "peak_source": f"{src} bf16_tflops (burst)"},
