@@ -148,6 +148,19 @@ typedef struct RpfqWideLinearArgs {
 } RpfqWideLinearArgs;
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
 
+/* Allocation-free variant of rpfq_wide_linear_sm100 — no counterpart in the
+ * reference. For callers that cannot allocate device memory when they run a
+ * layer (code recorded into a CUDA graph, request paths that must not call the
+ * synchronising cudaMalloc / cudaFree, hosts that give a library no allocator):
+ * with act_bits > 0 the quantized activations go to an 8 MiB scratch array
+ * built into the library (m * 2 k_c fp16 values at most; larger m is rejected
+ * with RPFQ_ERR_INVALID), args->scratch is ignored, and nothing is allocated.
+ * Every GPU that loads the library holds the array until the process exits.
+ * The first call on a device looks up the array's device address (set-up,
+ * once per device); make that first call before any stream capture. All calls
+ * share the array: calls that overlap on the GPU race on it. */
+int rpfq_wide_linear_noalloc_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
+
 /* Message of the last failed call on this host thread ("" if none). */
 const char* rpfq_last_error(void);
 

@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_act_quant_sm100",
     "rpfq_layernorm_sm100",
     "rpfq_wide_linear_sm100",
+    "rpfq_wide_linear_noalloc_sm100",
     "rpfq_last_error",
     "rpfq_device_error",
     "rpfq_version",
@@ -106,10 +107,12 @@ def lib() -> ctypes.CDLL:
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_wide_linear_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
+        L.rpfq_wide_linear_noalloc_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_last_error.restype = ctypes.c_char_p
         L.rpfq_device_error.argtypes = [ctypes.POINTER(I32)]
         for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
-                     "rpfq_wide_linear_sm100", "rpfq_device_error", "rpfq_version"):
+                     "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_device_error",
+                     "rpfq_version"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
         return L

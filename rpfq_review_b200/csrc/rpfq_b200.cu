@@ -434,3 +434,79 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the whole-layer entry point.
+//
+// Some callers cannot allocate device memory at the moment they run a layer:
+// code recorded into a CUDA graph (allocation calls are not capturable),
+// inference servers whose request path must not call cudaMalloc / cudaFree
+// because those calls can synchronise the device and stall every other
+// stream, and embedded or plugin hosts that own a fixed device budget and give
+// a kernel library no allocator at all. With activation quantization on, the
+// layer needs a scratch buffer for the quantized activations; this variant
+// takes it from a fixed array compiled into the library instead of from the
+// caller.
+//
+// The array is a file-scope static __device__ array of
+// kNoAllocScratchBytes (8 MiB). Every GPU that loads this library holds it
+// until the process exits. All calls share it and it keeps the last call's
+// contents; nothing in it needs to start at zero, because the quantization
+// kernel writes every element the GEMM then reads. Calls that overlap on the
+// GPU (for example on two streams at once) race on it.
+namespace rpfq {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) uint16_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(uint16_t)];
+
+struct NoAllocState {
+    std::once_flag once;
+    cudaError_t status = cudaSuccess;
+    uint16_t* ptr = nullptr;  // device address of g_noalloc_scratch on this device
+};
+NoAllocState g_noalloc[kMaxDevices];
+
+// In host code the array's name is only a host-side stand-in, so its device
+// address is looked up once per device, with that device current.
+int noalloc_scratch(uint16_t** out) {
+    int dev = 0;
+    RPFQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(RPFQ_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    NoAllocState& st = g_noalloc[dev];
+    std::call_once(st.once, [&st]() {
+        void* p = nullptr;
+        st.status = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        st.ptr = static_cast<uint16_t*>(p);
+    });
+    if (st.status != cudaSuccess || st.ptr == nullptr)
+        return fail(RPFQ_ERR_CUDA, "cudaGetSymbolAddress of the no-alloc scratch failed: %s",
+                    cudaGetErrorString(st.status));
+    *out = st.ptr;
+    return RPFQ_OK;
+}
+
+}  // namespace
+}  // namespace rpfq
+
+extern "C" int rpfq_wide_linear_noalloc_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
+    if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_wide_linear_noalloc_sm100: null args");
+    int rc = check_layer(a->layer, "rpfq_wide_linear_noalloc_sm100");
+    if (rc) return rc;
+    if (a->m < 0) return fail(RPFQ_ERR_INVALID, "rpfq_wide_linear_noalloc_sm100: negative m");
+    RpfqWideLinearArgs local = *a;
+    local.scratch = nullptr;
+    if (a->act_bits != 0) {
+        const size_t need = static_cast<size_t>(a->m) * 2 * static_cast<size_t>(a->layer->k_c) * sizeof(uint16_t);
+        if (need > kNoAllocScratchBytes)
+            return fail(RPFQ_ERR_INVALID,
+                        "rpfq_wide_linear_noalloc_sm100: the quantized activations need %zu bytes (m=%lld x %d fp16) "
+                        "but the built-in scratch holds %zu; use rpfq_wide_linear_sm100 with a caller buffer",
+                        need, (long long)a->m, 2 * a->layer->k_c, kNoAllocScratchBytes);
+        uint16_t* scratch = nullptr;
+        rc = noalloc_scratch(&scratch);
+        if (rc) return rc;
+        local.scratch = scratch;
+    }
+    return rpfq_wide_linear_sm100(&local, stream);
+}
