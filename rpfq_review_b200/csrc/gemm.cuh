@@ -23,9 +23,10 @@
 //   WG2  warps 8..11  epilogue, tile columns [BN/2, BN)   (232 registers: setmaxnreg.inc)
 //        Each epilogue warp owns the 32 TMEM lanes (tile rows) of quarter
 //        warp % 4 and walks its column half in steps of 128 bytes of output
-//        per row: tcgen05.ld, bias, GELU, residual (prefetched into L2 one
-//        tile ahead, into registers one step ahead), pack, 128-B-swizzled
-//        smem staging, TMA store of a [32 rows x 128 B] box.
+//        per row: tcgen05.ld, bias, GELU, residual (prefetched into L2 by WG0
+//        warp 2 with TMA box prefetches two tiles ahead, then into registers
+//        two steps ahead), pack, 128-B-swizzled smem staging, TMA store of a
+//        [32 rows x 128 B] box.
 // Register split: 128 x 40 + 256 x 232 = 64512 = 384 threads x 168 at launch.
 #pragma once
 
@@ -71,17 +72,33 @@ struct GemmCfg {
 };
 
 // GELU(v) = v/2 (1 + erf(v / sqrt 2)) with erf from Abramowitz & Stegun
-// 7.1.26 (Hastings): erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^{-z^2},
-// t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7. For v < 0 the result is
-// v/2 * (1 - erf(|v|/sqrt 2)), computed directly from the tail term.
-__device__ __forceinline__ float gelu_erf(float v) {
-    const float z = fabsf(v) * 0.70710678118654752f;
-    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-    const float poly =
-        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f),
-                 0.254829592f);
-    const float tail = poly * __expf(-z * z);  // = 1 - erf(z)
-    return 0.5f * v * (v >= 0.0f ? 2.0f - tail : tail);
+// 7.1.26 (Hastings): for z = |v| / sqrt 2,
+//   1 - erf(z) = tail = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^{-z^2},  t = 1 / (1 + p z),
+// |error of erf| <= 1.5e-7. Since erf(v / sqrt 2) = sign(v) (1 - tail),
+//   GELU(v) = (v + |v|) / 2 - |v| tail / 2,
+// evaluated on pairs of values with the packed fp32x2 instructions of sm_100
+// (one reciprocal and one exponential per value on the special-function unit).
+__device__ __forceinline__ void gelu_erf_pair(float& v0, float& v1) {
+    constexpr float kP = 0.3275911f * 0.70710678118654752f;  // p / sqrt 2 (acts on |v|)
+    constexpr float kE = -0.5f * 1.4426950408889634f;        // -z^2 = -v^2 / 2, in base 2
+    const uint64_t v = f2_pack(v0, v1);
+    const uint64_t a = v & 0x7fffffff7fffffffull;  // |v| of both lanes
+    const uint64_t den = f2_fma(f2_pack(kP, kP), a, f2_pack(1.0f, 1.0f));
+    float d0, d1;
+    f2_unpack(den, d0, d1);
+    const uint64_t t = f2_pack(rcp_approx(d0), rcp_approx(d1));
+    uint64_t poly = f2_fma(t, f2_pack(1.061405429f, 1.061405429f), f2_pack(-1.453152027f, -1.453152027f));
+    poly = f2_fma(t, poly, f2_pack(1.421413741f, 1.421413741f));
+    poly = f2_fma(t, poly, f2_pack(-0.284496736f, -0.284496736f));
+    poly = f2_fma(t, poly, f2_pack(0.254829592f, 0.254829592f));
+    poly = f2_mul(t, poly);
+    const uint64_t q = f2_mul(f2_mul(v, v), f2_pack(kE, kE));
+    float q0, q1;
+    f2_unpack(q, q0, q1);
+    const uint64_t tail = f2_mul(poly, f2_pack(ex2_approx(q0), ex2_approx(q1)));
+    const uint64_t half_a = f2_mul(a, f2_pack(-0.5f, -0.5f));
+    const uint64_t pos = f2_mul(f2_add(v, a), f2_pack(0.5f, 0.5f));
+    f2_unpack(f2_fma(half_a, tail, pos), v0, v1);
 }
 
 __device__ __forceinline__ void setmaxnreg_dec40() {
@@ -94,7 +111,8 @@ __device__ __forceinline__ void setmaxnreg_inc232() {
 template <int BN, bool OUT_F32>
 __global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                          const __grid_constant__ CUtensorMap tm_y, const GemmParams p) {
+                          const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
+                          const GemmParams p) {
     using C = GemmCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -132,6 +150,7 @@ __global__ void __launch_bounds__(384, 1)
         prefetch_tmap(&tm_x);
         prefetch_tmap(&tm_w);
         prefetch_tmap(&tm_y);
+        if (p.residual != nullptr) prefetch_tmap(&tm_r);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -225,6 +244,30 @@ __global__ void __launch_bounds__(384, 1)
             umma_commit(drain_bar);
             volatile int no_abort = 0;
             wait_bar(drain_bar, 0, &no_abort, p.err, 203);
+        } else if (warp == 2 && lane == 0 && p.residual != nullptr) {
+            // -------------------------------------------------------- residual prefetcher
+            // The residual of this CTA's tile i+2 is prefetched into L2 (one TMA
+            // box per column half) when tile i's accumulator is complete, i.e.
+            // about two main loops before the epilogue reads it.
+            auto prefetch_tile = [&](int t) {
+                if (t >= num_tiles) return;
+                const int r0 = (t / num_n) * C::BM;
+                const int c0 = (t % num_n) * BN;
+                tma_prefetch_l2_2d(&tm_r, c0, r0);
+                if (c0 + BN / 2 < p.n) tma_prefetch_l2_2d(&tm_r, c0 + BN / 2, r0);
+            };
+            prefetch_tile(blockIdx.x);
+            prefetch_tile(blockIdx.x + gridDim.x);
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 401)) break;
+                prefetch_tile(tile + 2 * gridDim.x);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
         }
     } else {
         setmaxnreg_inc232();
@@ -238,15 +281,6 @@ __global__ void __launch_bounds__(384, 1)
         const int col_half = (warp - 4) >> 2;  // 0: columns [0, BN/2), 1: [BN/2, BN)
         uint8_t* buf = epi_base + (warp - 4) * C::EPI_BUF_BYTES;
         const uint8_t* res_base = static_cast<const uint8_t*>(p.residual);
-        // residual row segment (this warp's half of a tile, this thread's row) into L2
-        auto prefetch_tile_residual = [&](int t) {
-            if (res_base == nullptr || t >= num_tiles) return;
-            const int64_t r = static_cast<int64_t>(t / num_n) * C::BM + 32 * q + lane;
-            const int c0 = (t % num_n) * BN + col_half * HALF;
-            if (r >= p.m || c0 >= p.n) return;
-            const int cols = min(HALF, p.n - c0);
-            prefetch_l2_bulk(res_base + (r * p.ldr + c0) * ESZ, static_cast<uint32_t>(cols * ESZ));
-        };
         // one 128-B residual step of this thread's row into registers
         auto load_residual = [&](int64_t r, int col0, uint4 (&dst)[8]) {
             const uint4* src = reinterpret_cast<const uint4*>(res_base + (r * p.ldr + col0) * ESZ);
@@ -258,11 +292,9 @@ __global__ void __launch_bounds__(384, 1)
                     dst[g] = make_uint4(0u, 0u, 0u, 0u);
             }
         };
-        prefetch_tile_residual(blockIdx.x);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            prefetch_tile_residual(tile + gridDim.x);
             const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::BM;
             const int c_begin = (tile % num_n) * BN + col_half * HALF;
             const int64_t row0 = m0 + 32 * q;
@@ -270,8 +302,10 @@ __global__ void __launch_bounds__(384, 1)
             const bool use_res = res_base != nullptr && row < p.m;
             const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
             const int nsteps = valid > 0 ? (valid + CW - 1) / CW : 0;
-            uint4 rnext[8];
-            if (use_res && nsteps > 0) load_residual(row, c_begin, rnext);
+            // residual steps c+1 and c+2 are in flight in registers while step c runs
+            uint4 rn1[8], rn2[8];
+            if (use_res && nsteps > 0) load_residual(row, c_begin, rn1);
+            if (use_res && nsteps > 1) load_residual(row, c_begin + CW, rn2);
             if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
@@ -281,8 +315,11 @@ __global__ void __launch_bounds__(384, 1)
                 const int col0 = c_begin + c * CW;
                 uint4 rcur[8];
 #pragma unroll
-                for (int g = 0; g < 8; ++g) rcur[g] = rnext[g];
-                if (use_res && c + 1 < nsteps) load_residual(row, col0 + CW, rnext);
+                for (int g = 0; g < 8; ++g) {
+                    rcur[g] = rn1[g];
+                    rn1[g] = rn2[g];
+                }
+                if (use_res && c + 2 < nsteps) load_residual(row, col0 + 2 * CW, rn2);
                 uint32_t r[CW];
 #pragma unroll
                 for (int h = 0; h < CW / 32; ++h)
@@ -308,7 +345,7 @@ __global__ void __launch_bounds__(384, 1)
                 }
                 if (p.activation == kActGelu) {
 #pragma unroll
-                    for (int j = 0; j < CW; ++j) v[j] = gelu_erf(v[j]);
+                    for (int j = 0; j < CW; j += 2) gelu_erf_pair(v[j], v[j + 1]);
                 }
                 if (use_res) {
 #pragma unroll

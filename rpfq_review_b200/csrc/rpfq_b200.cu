@@ -133,7 +133,7 @@ int encode_fn(EncodeTiledFn* out) {
 // Row-major matrix [rows, cols] of fp16 (esize 2) or fp32 (esize 4), row
 // stride ld elements, box [box_rows, box_cols], 128-B swizzle.
 int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-                  int box_cols, int esize = 2) {
+                  int box_cols, int esize = 2, bool swizzle = true) {
     EncodeTiledFn fn;
     int rc = encode_fn(&fn);
     if (rc) return rc;
@@ -143,7 +143,8 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
     cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a [%lld x %lld] matrix", (int)r,
@@ -157,11 +158,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 template <int BN, bool OUT_F32>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     using C = GemmCfg<BN>;
-    CUtensorMap tx, tw, ty;
+    CUtensorMap tx, tw, ty, tr;
     int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
     if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, BN, C::BK);
     if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, OUT_F32 ? 32 : 64, OUT_F32 ? 4 : 2);
+    // residual: only L2 prefetches of [128 rows x BN/2 columns] boxes, no swizzle
+    if (!rc && a->residual)
+        rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, C::BM, BN / 2, OUT_F32 ? 4 : 2, false);
     if (rc) return rc;
+    if (!a->residual) tr = ty;
     GemmParams p;
     p.bias = reinterpret_cast<const __half*>(a->bias);
     p.residual = a->residual;
@@ -173,7 +178,7 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     p.err = st->err_word;
     const int64_t tiles = ((a->m + C::BM - 1) / C::BM) * ((a->n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
-    gemm_f16_sm100_kernel<BN, OUT_F32><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, p);
+    gemm_f16_sm100_kernel<BN, OUT_F32><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, tr, p);
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }
