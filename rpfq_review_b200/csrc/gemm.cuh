@@ -23,10 +23,11 @@
 //   WG2  warps 8..11  epilogue, tile columns [BN/2, BN)   (232 registers: setmaxnreg.inc)
 //        Each epilogue warp owns the 32 TMEM lanes (tile rows) of quarter
 //        warp % 4 and walks its column half in steps of 128 bytes of output
-//        per row: tcgen05.ld, bias, GELU, residual (prefetched into L2 by WG0
-//        warp 2 with TMA box prefetches two tiles ahead, then into registers
-//        two steps ahead), pack, 128-B-swizzled smem staging, TMA store of a
-//        [32 rows x 128 B] box.
+//        per row: tcgen05.ld, bias, GELU, residual, pack, 128-B-swizzled smem
+//        staging, TMA store of a [32 rows x 128 B] box. The residual step is
+//        TMA-loaded into the warp's staging slot one step ahead (two slots
+//        per warp) and the output is written over it; WG0 warp 2 prefetches
+//        each tile's residual into L2 two tiles ahead.
 // Register split: 128 x 40 + 256 x 232 = 64512 = 384 threads x 168 at launch.
 #pragma once
 
@@ -46,20 +47,24 @@ struct GemmParams {
     int* err;                // device error word
 };
 
-template <int BN>
+template <int BN, bool RES>
 struct GemmCfg {
     static_assert(BN == 128 || BN == 256, "tile width");
     static constexpr int BM = 128;
     static constexpr int BK = 64;  // 64 fp16 = 128 B = one swizzle row
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    // With a residual, each epilogue warp double-buffers its staging slot (the
+    // residual lands there by TMA and the output is written over it), which
+    // costs one main-loop stage.
+    static constexpr int STAGES = BN == 256 ? (RES ? 3 : 4) : (RES ? 5 : 6);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_WARPS = 8;
-    static constexpr int EPI_BUF_BYTES = 32 * 128;  // 32 rows x 128 B, one per epilogue warp
-    static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF_BYTES;
+    static constexpr int EPI_SLOTS = RES ? 2 : 1;   // staging slots per epilogue warp
+    static constexpr int EPI_BUF_BYTES = 32 * 128;  // one slot: 32 rows x 128 B
+    static constexpr int EPI_BYTES = EPI_WARPS * EPI_SLOTS * EPI_BUF_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
-    static constexpr int BAR_BYTES = 256;
+    static constexpr int BAR_BYTES = 512;
     static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
     static constexpr int THREADS = 384;
     static constexpr int LAUNCH_REGS = 168;  // 65536 / 384, rounded down to the allocation granule
@@ -108,12 +113,12 @@ __device__ __forceinline__ void setmaxnreg_inc232() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
 }
 
-template <int BN, bool OUT_F32>
+template <int BN, bool OUT_F32, bool RES>
 __global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
                           const GemmParams p) {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, RES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
@@ -124,7 +129,8 @@ __global__ void __launch_bounds__(384, 1)
     uint64_t* tfull_bar = bars + 2 * C::STAGES;      // [2]
     uint64_t* tempty_bar = bars + 2 * C::STAGES + 2; // [2]
     uint64_t* drain_bar = bars + 2 * C::STAGES + 4;  // [1] teardown drain of MMAs
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5);
+    uint64_t* res_bar = bars + 2 * C::STAGES + 5;    // [EPI_WARPS * 2] residual slot landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5 + 2 * C::EPI_WARPS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -145,6 +151,7 @@ __global__ void __launch_bounds__(384, 1)
             mbar_init(&tempty_bar[b], C::EPI_WARPS);
         }
         mbar_init(drain_bar, 1);
+        for (int b = 0; b < 2 * C::EPI_WARPS; ++b) mbar_init(&res_bar[b], 1);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&tm_x);
@@ -249,12 +256,13 @@ __global__ void __launch_bounds__(384, 1)
             // The residual of this CTA's tile i+2 is prefetched into L2 (one TMA
             // box per column half) when tile i's accumulator is complete, i.e.
             // about two main loops before the epilogue reads it.
+            constexpr int PCW = OUT_F32 ? 32 : 64;  // residual box: 32 rows x 128 B
             auto prefetch_tile = [&](int t) {
                 if (t >= num_tiles) return;
                 const int r0 = (t / num_n) * C::BM;
                 const int c0 = (t % num_n) * BN;
-                tma_prefetch_l2_2d(&tm_r, c0, r0);
-                if (c0 + BN / 2 < p.n) tma_prefetch_l2_2d(&tm_r, c0 + BN / 2, r0);
+                for (int c = c0; c < c0 + BN && c < p.n; c += PCW)
+                    for (int r = r0; r < r0 + C::BM && r < p.m; r += 32) tma_prefetch_l2_2d(&tm_r, c, r);
             };
             prefetch_tile(blockIdx.x);
             prefetch_tile(blockIdx.x + gridDim.x);
@@ -274,52 +282,50 @@ __global__ void __launch_bounds__(384, 1)
         // ------------------------------------------------------------ epilogue
         // CW output columns per step = 128 bytes per row (64 fp16 or 32 fp32).
         constexpr int CW = OUT_F32 ? 32 : 64;
-        constexpr int ESZ = OUT_F32 ? 4 : 2;
         constexpr int HALF = BN / 2;
         static_assert(HALF % CW == 0, "column half must hold whole steps");
         const int q = warp & 3;                // TMEM lane quarter accessible to this warp
         const int col_half = (warp - 4) >> 2;  // 0: columns [0, BN/2), 1: [BN/2, BN)
-        uint8_t* buf = epi_base + (warp - 4) * C::EPI_BUF_BYTES;
-        const uint8_t* res_base = static_cast<const uint8_t*>(p.residual);
-        // one 128-B residual step of this thread's row into registers
-        auto load_residual = [&](int64_t r, int col0, uint4 (&dst)[8]) {
-            const uint4* src = reinterpret_cast<const uint4*>(res_base + (r * p.ldr + col0) * ESZ);
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                if (col0 + g * (16 / ESZ) < p.n)
-                    dst[g] = __ldcs(src + g);  // streamed: read once
-                else
-                    dst[g] = make_uint4(0u, 0u, 0u, 0u);
-            }
+        const int ew = warp - 4;               // epilogue warp index 0..7
+        uint8_t* slots = epi_base + ew * C::EPI_SLOTS * C::EPI_BUF_BYTES;
+        // TMA load of residual step (row0, col0) into slot s of this warp
+        auto load_residual = [&](int s, int col0, int64_t row0) {
+            mbar_arrive_expect_tx(&res_bar[2 * ew + s], C::EPI_BUF_BYTES);
+            tma_load_2d(slots + s * C::EPI_BUF_BYTES, &tm_r, &res_bar[2 * ew + s], col0,
+                        static_cast<int32_t>(row0));
         };
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t j = 0;  // running step counter of this warp (slot = j & 1 with a residual)
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::BM;
             const int c_begin = (tile % num_n) * BN + col_half * HALF;
             const int64_t row0 = m0 + 32 * q;
-            const int64_t row = row0 + lane;
-            const bool use_res = res_base != nullptr && row < p.m;
             const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
-            const int nsteps = valid > 0 ? (valid + CW - 1) / CW : 0;
-            // residual steps c+1 and c+2 are in flight in registers while step c runs
-            uint4 rn1[8], rn2[8];
-            if (use_res && nsteps > 0) load_residual(row, c_begin, rn1);
-            if (use_res && nsteps > 1) load_residual(row, c_begin + CW, rn2);
+            const int nsteps = (valid > 0 && row0 < p.m) ? (valid + CW - 1) / CW : 0;
+            if constexpr (RES) {
+                // first residual step of the tile lands while the main loop runs
+                if (lane == 0 && nsteps > 0) {
+                    bulk_wait_group_read<0>();
+                    load_residual(j & 1, c_begin, row0);
+                }
+            }
             if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
                                    static_cast<uint32_t>(acc * BN + col_half * HALF);
+            bool ok = true;
 #pragma unroll 1
-            for (int c = 0; c < nsteps; ++c) {
+            for (int c = 0; c < nsteps; ++c, ++j) {
                 const int col0 = c_begin + c * CW;
-                uint4 rcur[8];
-#pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    rcur[g] = rn1[g];
-                    rn1[g] = rn2[g];
+                if constexpr (RES) {
+                    // next residual step into the other slot, once that slot's
+                    // previous store has been read out
+                    if (lane == 0 && c + 1 < nsteps) {
+                        bulk_wait_group_read<0>();
+                        load_residual((j + 1) & 1, col0 + CW, row0);
+                    }
                 }
-                if (use_res && c + 2 < nsteps) load_residual(row, col0 + 2 * CW, rn2);
                 uint32_t r[CW];
 #pragma unroll
                 for (int h = 0; h < CW / 32; ++h)
@@ -327,7 +333,7 @@ __global__ void __launch_bounds__(384, 1)
                 tmem_ld_wait();
                 float v[CW];
 #pragma unroll
-                for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(r[j]);
+                for (int jj = 0; jj < CW; ++jj) v[jj] = __uint_as_float(r[jj]);
                 if (p.bias != nullptr) {
 #pragma unroll
                     for (int g = 0; g < CW / 8; ++g) {
@@ -345,18 +351,25 @@ __global__ void __launch_bounds__(384, 1)
                 }
                 if (p.activation == kActGelu) {
 #pragma unroll
-                    for (int j = 0; j < CW; j += 2) gelu_erf_pair(v[j], v[j + 1]);
+                    for (int jj = 0; jj < CW; jj += 2) gelu_erf_pair(v[jj], v[jj + 1]);
                 }
-                if (use_res) {
+                uint8_t* buf = slots + (RES ? (j & 1) : 0) * C::EPI_BUF_BYTES;
+                if constexpr (RES) {
+                    if (!wait_bar(&res_bar[2 * ew + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 302)) {
+                        ok = false;
+                        break;
+                    }
+                    // this thread's row of the residual step (128-B swizzle)
 #pragma unroll
                     for (int g = 0; g < 8; ++g) {
+                        const uint4 rv = *reinterpret_cast<const uint4*>(buf + lane * 128 + ((g ^ (lane & 7)) << 4));
                         if constexpr (OUT_F32) {
-                            v[4 * g + 0] += __uint_as_float(rcur[g].x);
-                            v[4 * g + 1] += __uint_as_float(rcur[g].y);
-                            v[4 * g + 2] += __uint_as_float(rcur[g].z);
-                            v[4 * g + 3] += __uint_as_float(rcur[g].w);
+                            v[4 * g + 0] += __uint_as_float(rv.x);
+                            v[4 * g + 1] += __uint_as_float(rv.y);
+                            v[4 * g + 2] += __uint_as_float(rv.z);
+                            v[4 * g + 3] += __uint_as_float(rv.w);
                         } else {
-                            const __half2* rh = reinterpret_cast<const __half2*>(&rcur[g]);
+                            const __half2* rh = reinterpret_cast<const __half2*>(&rv);
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
                                 const float2 f = __half22float2(rh[e]);
@@ -365,11 +378,12 @@ __global__ void __launch_bounds__(384, 1)
                             }
                         }
                     }
+                    __syncwarp();  // every lane has read its row before any lane overwrites the slot
+                } else {
+                    // single slot: wait until the previous TMA store has read it
+                    if (lane == 0) bulk_wait_group_read<0>();
+                    __syncwarp();
                 }
-                // single staging buffer per warp: wait until the previous TMA
-                // store from it has finished reading shared memory
-                if (lane == 0) bulk_wait_group_read<0>();
-                __syncwarp();
 #pragma unroll
                 for (int g = 0; g < 8; ++g) {  // eight 16-B granules per 128-B row
                     uint4 pk;
@@ -394,10 +408,11 @@ __global__ void __launch_bounds__(384, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    if (row0 < p.m) tma_store_2d(&tm_y, buf, col0, static_cast<int32_t>(row0));
+                    tma_store_2d(&tm_y, buf, col0, static_cast<int32_t>(row0));
                     bulk_commit_group();
                 }
             }
+            if (!ok) break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);

@@ -59,13 +59,19 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
+template <int BN, bool OUT_F32, bool RES>
+cudaError_t configure_one() {
+    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, OUT_F32, RES>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, RES>::SMEM_BYTES);
+}
+
 template <int BN>
 cudaError_t configure_gemm() {
-    cudaError_t e = cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                GemmCfg<BN>::SMEM_BYTES);
+    cudaError_t e = configure_one<BN, false, false>();
+    if (e == cudaSuccess) e = configure_one<BN, true, false>();
+    if (e == cudaSuccess) e = configure_one<BN, false, true>();
+    if (e == cudaSuccess) e = configure_one<BN, true, true>();
+    return e;
 }
 
 // Per-device set-up, done once with that device current: SM count, device
@@ -155,18 +161,19 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // ---------------------------------------------------------------- GEMM launch
-template <int BN, bool OUT_F32>
+template <int BN, bool OUT_F32, bool RES>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, RES>;
+    constexpr int CW = OUT_F32 ? 32 : 64;   // output / residual columns per 128-B step
+    constexpr int ESZ = OUT_F32 ? 4 : 2;
     CUtensorMap tx, tw, ty, tr;
     int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
     if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, BN, C::BK);
-    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, OUT_F32 ? 32 : 64, OUT_F32 ? 4 : 2);
-    // residual: only L2 prefetches of [128 rows x BN/2 columns] boxes, no swizzle
-    if (!rc && a->residual)
-        rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, C::BM, BN / 2, OUT_F32 ? 4 : 2, false);
+    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, CW, ESZ);
+    // residual: same [32 rows x 128 B] boxes as the output (TMA loads + L2 prefetches)
+    if (!rc && RES) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
     if (rc) return rc;
-    if (!a->residual) tr = ty;
+    if (!RES) tr = ty;
     GemmParams p;
     p.bias = reinterpret_cast<const __half*>(a->bias);
     p.residual = a->residual;
@@ -178,9 +185,17 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     p.err = st->err_word;
     const int64_t tiles = ((a->m + C::BM - 1) / C::BM) * ((a->n + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
-    gemm_f16_sm100_kernel<BN, OUT_F32><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, tr, p);
+    gemm_f16_sm100_kernel<BN, OUT_F32, RES><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, tr, p);
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
+}
+
+template <int BN>
+int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
+    const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
+    const bool res = a->residual != nullptr;
+    if (f32) return res ? launch_gemm<BN, true, true>(a, st, stream) : launch_gemm<BN, true, false>(a, st, stream);
+    return res ? launch_gemm<BN, false, true>(a, st, stream) : launch_gemm<BN, false, false>(a, st, stream);
 }
 
 int pick_block_n(int64_t m, int n, int sm_count) {
@@ -228,10 +243,9 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     int rc = device_state(&st);
     if (rc) return rc;
     int bn = a->block_n ? a->block_n : pick_block_n(a->m, a->n, st->sm_count);
-    const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
     switch (bn) {
-        case 256: return f32 ? launch_gemm<256, true>(a, st, stream) : launch_gemm<256, false>(a, st, stream);
-        case 128: return f32 ? launch_gemm<128, true>(a, st, stream) : launch_gemm<128, false>(a, st, stream);
+        case 256: return launch_gemm_bn<256>(a, st, stream);
+        case 128: return launch_gemm_bn<128>(a, st, stream);
         default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 128 or 256 (got %d)", bn);
     }
 }
