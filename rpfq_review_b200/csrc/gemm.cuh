@@ -47,20 +47,23 @@ struct GemmParams {
     int* err;                // device error word
 };
 
-template <int BN, bool RES>
+// RES = residual slots per epilogue warp: 0 (no residual), 1 (the residual
+// step lands in the single staging slot just before it is used: fine when a
+// long main loop hides the epilogue), 2 (the next step's residual lands in the
+// second slot while this step runs: for short main loops, at the price of one
+// main-loop stage of shared memory).
+template <int BN, int RES>
 struct GemmCfg {
     static_assert(BN == 128 || BN == 256, "tile width");
+    static_assert(RES >= 0 && RES <= 2, "residual slots");
     static constexpr int BM = 128;
     static constexpr int BK = 64;  // 64 fp16 = 128 B = one swizzle row
-    // With a residual, each epilogue warp double-buffers its staging slot (the
-    // residual lands there by TMA and the output is written over it), which
-    // costs one main-loop stage.
-    static constexpr int STAGES = BN == 256 ? (RES ? 3 : 4) : (RES ? 5 : 6);
+    static constexpr int STAGES = BN == 256 ? (RES == 2 ? 3 : 4) : (RES == 2 ? 5 : 6);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_WARPS = 8;
-    static constexpr int EPI_SLOTS = RES ? 2 : 1;   // staging slots per epilogue warp
+    static constexpr int EPI_SLOTS = RES == 2 ? 2 : 1;  // staging slots per epilogue warp
     static constexpr int EPI_BUF_BYTES = 32 * 128;  // one slot: 32 rows x 128 B
     static constexpr int EPI_BYTES = EPI_WARPS * EPI_SLOTS * EPI_BUF_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
@@ -113,7 +116,7 @@ __device__ __forceinline__ void setmaxnreg_inc232() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
 }
 
-template <int BN, bool OUT_F32, bool RES>
+template <int BN, bool OUT_F32, int RES>
 __global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
@@ -303,11 +306,11 @@ __global__ void __launch_bounds__(384, 1)
             const int64_t row0 = m0 + 32 * q;
             const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
             const int nsteps = (valid > 0 && row0 < p.m) ? (valid + CW - 1) / CW : 0;
-            if constexpr (RES) {
+            if constexpr (RES > 0) {
                 // first residual step of the tile lands while the main loop runs
                 if (lane == 0 && nsteps > 0) {
                     bulk_wait_group_read<0>();
-                    load_residual(j & 1, c_begin, row0);
+                    load_residual(RES == 2 ? (j & 1) : 0, c_begin, row0);
                 }
             }
             if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
@@ -318,12 +321,19 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll 1
             for (int c = 0; c < nsteps; ++c, ++j) {
                 const int col0 = c_begin + c * CW;
-                if constexpr (RES) {
+                if constexpr (RES == 2) {
                     // next residual step into the other slot, once that slot's
                     // previous store has been read out
                     if (lane == 0 && c + 1 < nsteps) {
                         bulk_wait_group_read<0>();
                         load_residual((j + 1) & 1, col0 + CW, row0);
+                    }
+                } else if constexpr (RES == 1) {
+                    // single slot: this step's residual (the first one of the tile
+                    // was issued before the accumulator wait)
+                    if (lane == 0 && c > 0) {
+                        bulk_wait_group_read<0>();
+                        load_residual(0, col0, row0);
                     }
                 }
                 uint32_t r[CW];
@@ -353,9 +363,12 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                     for (int jj = 0; jj < CW; jj += 2) gelu_erf_pair(v[jj], v[jj + 1]);
                 }
-                uint8_t* buf = slots + (RES ? (j & 1) : 0) * C::EPI_BUF_BYTES;
-                if constexpr (RES) {
-                    if (!wait_bar(&res_bar[2 * ew + (j & 1)], (j >> 1) & 1, abort_flag, p.err, 302)) {
+                const uint32_t slot = RES == 2 ? (j & 1) : 0;
+                uint8_t* buf = slots + slot * C::EPI_BUF_BYTES;
+                if constexpr (RES > 0) {
+                    // uses of this slot so far: j / 2 (two slots) or j (one slot)
+                    const uint32_t parity = RES == 2 ? ((j >> 1) & 1) : (j & 1);
+                    if (!wait_bar(&res_bar[2 * ew + slot], parity, abort_flag, p.err, 302)) {
                         ok = false;
                         break;
                     }

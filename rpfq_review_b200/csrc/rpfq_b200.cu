@@ -59,7 +59,7 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-template <int BN, bool OUT_F32, bool RES>
+template <int BN, bool OUT_F32, int RES>
 cudaError_t configure_one() {
     return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, OUT_F32, RES>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, RES>::SMEM_BYTES);
@@ -67,10 +67,10 @@ cudaError_t configure_one() {
 
 template <int BN>
 cudaError_t configure_gemm() {
-    cudaError_t e = configure_one<BN, false, false>();
-    if (e == cudaSuccess) e = configure_one<BN, true, false>();
-    if (e == cudaSuccess) e = configure_one<BN, false, true>();
-    if (e == cudaSuccess) e = configure_one<BN, true, true>();
+    cudaError_t e = cudaSuccess;
+    for (cudaError_t r : {configure_one<BN, false, 0>(), configure_one<BN, true, 0>(), configure_one<BN, false, 1>(),
+                          configure_one<BN, true, 1>(), configure_one<BN, false, 2>(), configure_one<BN, true, 2>()})
+        if (e == cudaSuccess) e = r;
     return e;
 }
 
@@ -161,7 +161,7 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // ---------------------------------------------------------------- GEMM launch
-template <int BN, bool OUT_F32, bool RES>
+template <int BN, bool OUT_F32, int RES>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     using C = GemmCfg<BN, RES>;
     constexpr int CW = OUT_F32 ? 32 : 64;   // output / residual columns per 128-B step
@@ -171,9 +171,9 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, BN, C::BK);
     if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, CW, ESZ);
     // residual: same [32 rows x 128 B] boxes as the output (TMA loads + L2 prefetches)
-    if (!rc && RES) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
+    if (!rc && RES > 0) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
     if (rc) return rc;
-    if (!RES) tr = ty;
+    if (RES == 0) tr = ty;
     GemmParams p;
     p.bias = reinterpret_cast<const __half*>(a->bias);
     p.residual = a->residual;
@@ -190,12 +190,20 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     return RPFQ_OK;
 }
 
+// Residual slots: two (one main-loop stage less) when the main loop is short
+// and the epilogue must hide the residual latency itself; one otherwise.
 template <int BN>
 int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
-    const bool res = a->residual != nullptr;
-    if (f32) return res ? launch_gemm<BN, true, true>(a, st, stream) : launch_gemm<BN, true, false>(a, st, stream);
-    return res ? launch_gemm<BN, false, true>(a, st, stream) : launch_gemm<BN, false, false>(a, st, stream);
+    const int res = a->residual == nullptr ? 0 : (a->k <= 1024 ? 2 : 1);
+    if (f32) {
+        if (res == 2) return launch_gemm<BN, true, 2>(a, st, stream);
+        if (res == 1) return launch_gemm<BN, true, 1>(a, st, stream);
+        return launch_gemm<BN, true, 0>(a, st, stream);
+    }
+    if (res == 2) return launch_gemm<BN, false, 2>(a, st, stream);
+    if (res == 1) return launch_gemm<BN, false, 1>(a, st, stream);
+    return launch_gemm<BN, false, 0>(a, st, stream);
 }
 
 int pick_block_n(int64_t m, int n, int sm_count) {

@@ -108,9 +108,9 @@ def test_gemm_matches_fp64(cuda, m, n, k, block_n):
     assert torch.all(err <= ref.abs() * 2.0 ** -10 + 1e-3 * ref.abs().max())
 
 
-def test_gemm_epilogue_gelu_residual(cuda):
+@pytest.mark.parametrize("m,n,k", [(777, 3072, 768), (390, 768, 3072)])
+def test_gemm_epilogue_gelu_residual(cuda, m, n, k):
     g = torch.Generator().manual_seed(3)
-    m, n, k = 777, 3072, 768
     x = torch.randn(m, k, generator=g).half()
     w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
     b = (torch.randn(n, generator=g) * 0.1).half()
@@ -133,7 +133,8 @@ def test_gemm_strided_rows(cuda):
     assert torch.all(out[:, :128] == 0) and torch.all(out[:, 384:] == 0)
 
 
-@pytest.mark.parametrize("m,n,k", [(1576, 768, 768), (300, 1000, 768), (129, 96, 96)])
+@pytest.mark.parametrize("m,n,k", [(1576, 768, 768), (300, 1000, 768), (129, 96, 96), (700, 768, 3072),
+                                   (257, 384, 1536)])
 def test_gemm_fp32_output_and_residual(cuda, m, n, k):
     """fp32 output with an fp32 residual added in place (the model's residual stream)."""
     g = torch.Generator().manual_seed(m + n)
