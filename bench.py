@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--gemm", default=None, help="M,N,K: time one packed layer instead of the model")
     ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
+    ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
     ap.add_argument("--gemm-breakdown", action="store_true", help="print per-GEMM event times (stderr)")
@@ -455,9 +456,9 @@ def run_gemm(args):
 
     def step(i):
         res = ys[i & 1] if args.epilogue == "residual_f32" else None
-        if args.block_n or args.epilogue != "none":
+        if args.block_n or args.cta_pair or args.epilogue != "none":
             ops.gemm(xs[i & 1], mod.dense, mod.bias, residual=res, activation=act, block_n=args.block_n,
-                     out=ys[i & 1])
+                     out=ys[i & 1], cta_pair=args.cta_pair)
         else:
             ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1])
 

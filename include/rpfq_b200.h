@@ -102,7 +102,7 @@ typedef struct RpfqGemmArgs {
     int32_t activation;       /* RPFQ_ACT_NONE or RPFQ_ACT_GELU (erf)                   */
     int32_t block_n;          /* 0 = automatic; else 128 or 256                         */
     int32_t flags;            /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32             */
-    int32_t reserved;
+    int32_t cta_pair;         /* 0 = automatic; 1 = one CTA per tile; 2 = CTA pairs      */
 } RpfqGemmArgs;
 int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
 

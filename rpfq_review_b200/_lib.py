@@ -63,7 +63,7 @@ class RpfqGemmArgs(ctypes.Structure):
         ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
         ("m", ctypes.c_int64), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
         ("activation", ctypes.c_int32), ("block_n", ctypes.c_int32),
-        ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32), ("cta_pair", ctypes.c_int32),
     ]
 
 

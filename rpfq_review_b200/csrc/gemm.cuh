@@ -52,15 +52,21 @@ struct GemmParams {
 // long main loop hides the epilogue), 2 (the next step's residual lands in the
 // second slot while this step runs: for short main loops, at the price of one
 // main-loop stage of shared memory).
-template <int BN, int RES>
+// PAIR: a cluster of two CTAs computes a 256 x BN tile with cta_group::2
+// MMAs; each CTA loads its 128 rows of x and half (BN/2 rows) of w, so the
+// operand bytes each SM streams per flop drop by a third.
+template <int BN, int RES, bool PAIR = false>
 struct GemmCfg {
     static_assert(BN == 128 || BN == 256, "tile width");
     static_assert(RES >= 0 && RES <= 2, "residual slots");
-    static constexpr int BM = 128;
+    static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
+    static constexpr int BM = 128;      // rows per CTA (TMEM lanes)
+    static constexpr int TILE_M = PAIR ? 256 : 128;
     static constexpr int BK = 64;  // 64 fp16 = 128 B = one swizzle row
-    static constexpr int STAGES = BN == 256 ? (RES == 2 ? 3 : 4) : (RES == 2 ? 5 : 6);
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of w per CTA and stage
+    static constexpr int STAGES = PAIR ? (RES == 2 ? 5 : 6) : (BN == 256 ? (RES == 2 ? 3 : 4) : (RES == 2 ? 5 : 6));
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_WARPS = 8;
     static constexpr int EPI_SLOTS = RES == 2 ? 2 : 1;  // staging slots per epilogue warp
@@ -116,12 +122,12 @@ __device__ __forceinline__ void setmaxnreg_inc232() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
 }
 
-template <int BN, bool OUT_F32, int RES>
+template <int BN, bool OUT_F32, int RES, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
                           const GemmParams p) {
-    using C = GemmCfg<BN, RES>;
+    using C = GemmCfg<BN, RES, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
@@ -138,8 +144,12 @@ __global__ void __launch_bounds__(384, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // CTA pairs: rank 0 (leader) issues the MMAs; tiles are scheduled per pair.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
-    const int num_m = static_cast<int>((p.m + C::BM - 1) / C::BM);
+    const int num_m = static_cast<int>((p.m + C::TILE_M - 1) / C::TILE_M);
     const int num_n = (p.n + BN - 1) / BN;
     const int num_k = (p.k + C::BK - 1) / C::BK;
     const int num_tiles = num_m * num_n;
@@ -151,7 +161,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull_bar[b], 1);
-            mbar_init(&tempty_bar[b], C::EPI_WARPS);
+            mbar_init(&tempty_bar[b], PAIR ? 2 * C::EPI_WARPS : C::EPI_WARPS);
         }
         mbar_init(drain_bar, 1);
         for (int b = 0; b < 2 * C::EPI_WARPS; ++b) mbar_init(&res_bar[b], 1);
@@ -163,11 +173,17 @@ __global__ void __launch_bounds__(384, 1)
         if (p.residual != nullptr) prefetch_tmap(&tm_r);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -179,18 +195,26 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / num_n) * C::BM;
-                const int n0 = (tile % num_n) * BN;
+            for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+                const int m0 = (tile / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
+                const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * C::B_ROWS;
                 for (int kb = 0; kb < num_k; ++kb) {
                     if (!wait_bar(&empty_bar[stage], phase ^ 1, abort_flag, p.err, 101)) {
                         ok = false;
                         break;
                     }
                     uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
-                    tma_load_2d(sa, &tm_x, &full_bar[stage], kb * C::BK, m0);
-                    tma_load_2d(sa + C::A_BYTES, &tm_w, &full_bar[stage], kb * C::BK, n0);
+                    if constexpr (PAIR) {
+                        // both CTAs' bytes complete on the leader's full barrier
+                        if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+                        const uint32_t leader_full = mapa_shared(smem_u32(&full_bar[stage]), 0);
+                        tma_load_2d_pair(sa, &tm_x, leader_full, kb * C::BK, m0);
+                        tma_load_2d_pair(sa + C::A_BYTES, &tm_w, leader_full, kb * C::BK, n0);
+                    } else {
+                        mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+                        tma_load_2d(sa, &tm_x, &full_bar[stage], kb * C::BK, m0);
+                        tma_load_2d(sa + C::A_BYTES, &tm_w, &full_bar[stage], kb * C::BK, n0);
+                    }
                     ++issued;
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -199,8 +223,10 @@ __global__ void __launch_bounds__(384, 1)
                 }
             }
             // Drain: every load issued into the ring must have landed before the
-            // CTA may exit (normally already consumed by the MMA warp).
-            const int pending = issued < C::STAGES ? issued : C::STAGES;
+            // CTA may exit (normally already consumed by the MMA warp). With CTA
+            // pairs the peer's bytes complete on the leader's barriers, so the
+            // leader drains for both (the peer waits at the final cluster barrier).
+            const int pending = (PAIR && rank != 0) ? 0 : (issued < C::STAGES ? issued : C::STAGES);
             for (int i = 1; i <= pending; ++i) {
                 int s = stage - i;
                 uint32_t ph = phase;
@@ -211,16 +237,26 @@ __global__ void __launch_bounds__(384, 1)
                 volatile int no_abort = 0;
                 wait_bar(&full_bar[s], ph, &no_abort, p.err, 102);
             }
-        } else if (warp == 1 && lane == 0) {
+        } else if (warp == 1 && lane == 0 && rank == 0) {
             // -------------------------------------------------------- MMA issuer
-            constexpr uint32_t idesc = umma_idesc_f16(C::BM, BN);
+            constexpr uint32_t idesc = umma_idesc_f16(C::TILE_M, BN);
+            // commits go to this CTA's barrier and, for pairs, to the peer's as well
+            auto commit_both = [&](uint64_t* bar) {
+                if constexpr (PAIR) {
+                    const uint32_t a = smem_u32(bar);
+                    umma_commit_pair(a);
+                    umma_commit_pair(mapa_shared(a, 1));
+                } else {
+                    umma_commit(bar);
+                }
+            };
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                if (!wait_bar(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, 201)) break;
+            for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+                if (!wait_bar<PAIR>(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, 201)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
                 for (int kb = 0; kb < num_k; ++kb) {
@@ -235,23 +271,29 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                     for (int kk = 0; kk < C::BK / 16; ++kk) {
                         // +32 B per K step of 16 fp16 inside the 128-B swizzle row
-                        umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                        if constexpr (PAIR)
+                            umma_f16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                        else
+                            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
                     }
-                    umma_commit(&empty_bar[stage]);
+                    commit_both(&empty_bar[stage]);
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
-                umma_commit(&tfull_bar[acc]);
+                commit_both(&tfull_bar[acc]);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1;
                 }
             }
             // Teardown: make sure no MMA is still writing TMEM before it is freed.
-            umma_commit(drain_bar);
+            if constexpr (PAIR)
+                umma_commit_pair(smem_u32(drain_bar));
+            else
+                umma_commit(drain_bar);
             volatile int no_abort = 0;
             wait_bar(drain_bar, 0, &no_abort, p.err, 203);
         } else if (warp == 2 && lane == 0 && p.residual != nullptr) {
@@ -262,18 +304,18 @@ __global__ void __launch_bounds__(384, 1)
             constexpr int PCW = OUT_F32 ? 32 : 64;  // residual box: 32 rows x 128 B
             auto prefetch_tile = [&](int t) {
                 if (t >= num_tiles) return;
-                const int r0 = (t / num_n) * C::BM;
+                const int r0 = (t / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
                 const int c0 = (t % num_n) * BN;
                 for (int c = c0; c < c0 + BN && c < p.n; c += PCW)
                     for (int r = r0; r < r0 + C::BM && r < p.m; r += 32) tma_prefetch_l2_2d(&tm_r, c, r);
             };
-            prefetch_tile(blockIdx.x);
-            prefetch_tile(blockIdx.x + gridDim.x);
+            prefetch_tile(first_tile);
+            prefetch_tile(first_tile + tile_step);
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
                 if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 401)) break;
-                prefetch_tile(tile + 2 * gridDim.x);
+                prefetch_tile(tile + 2 * tile_step);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1;
@@ -300,8 +342,11 @@ __global__ void __launch_bounds__(384, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t j = 0;  // running step counter of this warp (slot = j & 1 with a residual)
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::BM;
+        // the accumulator is released to the leader's MMA warp (both CTAs' warps)
+        const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+        const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+        for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+            const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::TILE_M + static_cast<int64_t>(rank) * C::BM;
             const int c_begin = (tile % num_n) * BN + col_half * HALF;
             const int64_t row0 = m0 + 32 * q;
             const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
@@ -428,7 +473,12 @@ __global__ void __launch_bounds__(384, 1)
             if (!ok) break;
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (lane == 0) {
+                if constexpr (PAIR)
+                    mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+                else
+                    mbar_arrive(&tempty_bar[acc]);
+            }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
@@ -440,8 +490,14 @@ __global__ void __launch_bounds__(384, 1)
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer is done with TMEM and with our barriers
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (warp == 1) {
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
 }
 
 }  // namespace rpfq

@@ -59,10 +59,10 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-template <int BN, bool OUT_F32, int RES>
+template <int BN, bool OUT_F32, int RES, bool PAIR = false>
 cudaError_t configure_one() {
-    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, OUT_F32, RES>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, RES>::SMEM_BYTES);
+    return cudaFuncSetAttribute(gemm_f16_sm100_kernel<BN, OUT_F32, RES, PAIR>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, RES, PAIR>::SMEM_BYTES);
 }
 
 template <int BN>
@@ -71,6 +71,12 @@ cudaError_t configure_gemm() {
     for (cudaError_t r : {configure_one<BN, false, 0>(), configure_one<BN, true, 0>(), configure_one<BN, false, 1>(),
                           configure_one<BN, true, 1>(), configure_one<BN, false, 2>(), configure_one<BN, true, 2>()})
         if (e == cudaSuccess) e = r;
+    if constexpr (BN == 256) {
+        for (cudaError_t r :
+             {configure_one<BN, false, 0, true>(), configure_one<BN, true, 0, true>(), configure_one<BN, false, 1, true>(),
+              configure_one<BN, true, 1, true>(), configure_one<BN, false, 2, true>(), configure_one<BN, true, 2, true>()})
+            if (e == cudaSuccess) e = r;
+    }
     return e;
 }
 
@@ -161,14 +167,14 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // ---------------------------------------------------------------- GEMM launch
-template <int BN, bool OUT_F32, int RES>
+template <int BN, bool OUT_F32, int RES, bool PAIR>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
-    using C = GemmCfg<BN, RES>;
+    using C = GemmCfg<BN, RES, PAIR>;
     constexpr int CW = OUT_F32 ? 32 : 64;   // output / residual columns per 128-B step
     constexpr int ESZ = OUT_F32 ? 4 : 2;
     CUtensorMap tx, tw, ty, tr;
     int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
-    if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, BN, C::BK);
+    if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, C::B_ROWS, C::BK);
     if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, CW, ESZ);
     // residual: same [32 rows x 128 B] boxes as the output (TMA loads + L2 prefetches)
     if (!rc && RES > 0) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
@@ -183,27 +189,64 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     p.k = a->k;
     p.activation = a->activation;
     p.err = st->err_word;
-    const int64_t tiles = ((a->m + C::BM - 1) / C::BM) * ((a->n + BN - 1) / BN);
-    const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
-    gemm_f16_sm100_kernel<BN, OUT_F32, RES><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, tr, p);
-    RPFQ_CUDA(cudaGetLastError());
+    const int64_t tiles = ((a->m + C::TILE_M - 1) / C::TILE_M) * ((a->n + BN - 1) / BN);
+    if constexpr (PAIR) {
+        // as many CTA pairs as can be resident at once (queried once per device)
+        static int max_pairs[kMaxDevices] = {};
+        int dev = 0;
+        RPFQ_CUDA(cudaGetDevice(&dev));
+        cudaLaunchConfig_t cfg = {};
+        if (max_pairs[dev] == 0) {
+            cudaLaunchConfig_t q = {};
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = 2;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.gridDim = dim3(st->sm_count);
+            q.blockDim = dim3(C::THREADS);
+            q.dynamicSmemBytes = C::SMEM_BYTES;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int n = 0;
+            RPFQ_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, &q));
+            max_pairs[dev] = n > 0 ? n : 1;
+        }
+        const int pairs = static_cast<int>(tiles < max_pairs[dev] ? tiles : max_pairs[dev]);
+        cfg.gridDim = dim3(2 * pairs);
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM_BYTES;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        RPFQ_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, tx, tw, ty, tr, p));
+    } else {
+        const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
+        gemm_f16_sm100_kernel<BN, OUT_F32, RES, false><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, tr, p);
+        RPFQ_CUDA(cudaGetLastError());
+    }
     return RPFQ_OK;
 }
 
 // Residual slots: two (one main-loop stage less) when the main loop is short
 // and the epilogue must hide the residual latency itself; one otherwise.
-template <int BN>
+template <int BN, bool PAIR>
 int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
     const int res = a->residual == nullptr ? 0 : (a->k <= 1024 ? 2 : 1);
     if (f32) {
-        if (res == 2) return launch_gemm<BN, true, 2>(a, st, stream);
-        if (res == 1) return launch_gemm<BN, true, 1>(a, st, stream);
-        return launch_gemm<BN, true, 0>(a, st, stream);
+        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream);
+        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream);
+        return launch_gemm<BN, true, 0, PAIR>(a, st, stream);
     }
-    if (res == 2) return launch_gemm<BN, false, 2>(a, st, stream);
-    if (res == 1) return launch_gemm<BN, false, 1>(a, st, stream);
-    return launch_gemm<BN, false, 0>(a, st, stream);
+    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream);
+    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream);
+    return launch_gemm<BN, false, 0, PAIR>(a, st, stream);
 }
 
 int pick_block_n(int64_t m, int n, int sm_count) {
@@ -251,9 +294,15 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     int rc = device_state(&st);
     if (rc) return rc;
     int bn = a->block_n ? a->block_n : pick_block_n(a->m, a->n, st->sm_count);
+    // CTA pairs (256 x 256 tiles over two SMs) when the 256-wide tile is chosen
+    // and there are enough row pairs to fill the GPU; cta_pair forces either way.
+    const int64_t pair_tiles = ((a->m + 255) / 256) * ((a->n + 255) / 256);
+    const bool pair = bn == 256 && (a->cta_pair == 2 || (a->cta_pair == 0 && pair_tiles >= st->sm_count / 2));
+    if (a->cta_pair < 0 || a->cta_pair > 2)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: cta_pair must be 0, 1 or 2 (got %d)", a->cta_pair);
     switch (bn) {
-        case 256: return launch_gemm_bn<256>(a, st, stream);
-        case 128: return launch_gemm_bn<128>(a, st, stream);
+        case 256: return pair ? launch_gemm_bn<256, true>(a, st, stream) : launch_gemm_bn<256, false>(a, st, stream);
+        case 128: return launch_gemm_bn<128, false>(a, st, stream);
         default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 128 or 256 (got %d)", bn);
     }
 }

@@ -118,7 +118,7 @@ def _flags(out: torch.Tensor, residual: torch.Tensor | None) -> int:
 
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, activation="none", block_n: int = 0,
-         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16, cta_pair: int = 0) -> torch.Tensor:
     """K2: ``act(x @ w.T + bias) + residual`` with fp16 operands, fp32
     accumulation; ``residual`` and ``out`` may be fp16 or fp32 (and may be the
     same tensor for an in-place residual add)."""
@@ -146,7 +146,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
         raise ValueError("out must be a row-major view with unit column stride")
     a = _lib.RpfqGemmArgs(x=x2.data_ptr(), ldx=ldx, w=w.data_ptr(), bias=_p(bias), residual=_p(r2), ldr=ldr,
                           y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n,
-                          flags=_flags(out, r2))
+                          flags=_flags(out, r2), cta_pair=cta_pair)
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:

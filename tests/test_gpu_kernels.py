@@ -94,13 +94,13 @@ GEMM_SHAPES = [
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
-@pytest.mark.parametrize("block_n", [0, 128, 256])
-def test_gemm_matches_fp64(cuda, m, n, k, block_n):
+@pytest.mark.parametrize("block_n,cta_pair", [(0, 0), (128, 0), (256, 1), (256, 2)])
+def test_gemm_matches_fp64(cuda, m, n, k, block_n, cta_pair):
     g = torch.Generator().manual_seed(m + n + k)
     x = torch.randn(m, k, generator=g).half()
     w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
     b = (torch.randn(n, generator=g) * 0.1).half()
-    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), block_n=block_n).cpu()
+    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), block_n=block_n, cta_pair=cta_pair).cpu()
     ref = x.double() @ w.double().T + b.double()
     assert rel_err(y.numpy(), ref.numpy()) < TOL
     # fp32 accumulation: every element within its fp16 output rounding + accumulation slack
@@ -109,13 +109,15 @@ def test_gemm_matches_fp64(cuda, m, n, k, block_n):
 
 
 @pytest.mark.parametrize("m,n,k", [(777, 3072, 768), (390, 768, 3072)])
-def test_gemm_epilogue_gelu_residual(cuda, m, n, k):
+@pytest.mark.parametrize("cta_pair", [1, 2])
+def test_gemm_epilogue_gelu_residual(cuda, m, n, k, cta_pair):
     g = torch.Generator().manual_seed(3)
     x = torch.randn(m, k, generator=g).half()
     w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
     b = (torch.randn(n, generator=g) * 0.1).half()
     r = torch.randn(m, n, generator=g).half()
-    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=r.to(cuda), activation="gelu").cpu()
+    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=r.to(cuda), activation="gelu", block_n=256,
+                    cta_pair=cta_pair).cpu()
     lin = x.double() @ w.double().T + b.double()
     ref = torch.nn.functional.gelu(lin) + r.double()
     assert rel_err(y.numpy(), ref.numpy()) < TOL
@@ -135,7 +137,8 @@ def test_gemm_strided_rows(cuda):
 
 @pytest.mark.parametrize("m,n,k", [(1576, 768, 768), (300, 1000, 768), (129, 96, 96), (700, 768, 3072),
                                    (257, 384, 1536)])
-def test_gemm_fp32_output_and_residual(cuda, m, n, k):
+@pytest.mark.parametrize("cta_pair", [1, 2])
+def test_gemm_fp32_output_and_residual(cuda, m, n, k, cta_pair):
     """fp32 output with an fp32 residual added in place (the model's residual stream)."""
     g = torch.Generator().manual_seed(m + n)
     x = torch.randn(m, k, generator=g).half()
@@ -143,14 +146,15 @@ def test_gemm_fp32_output_and_residual(cuda, m, n, k):
     b = (torch.randn(n, generator=g) * 0.1).half()
     r = torch.randn(m, n, generator=g) * 3.0
     res = r.to(cuda)
-    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=res, out=res)
+    y = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=res, out=res, block_n=256, cta_pair=cta_pair)
     assert y.data_ptr() == res.data_ptr() and y.dtype == torch.float32
     ref = x.double() @ w.double().T + b.double() + r.double()
     err = (y.cpu().double() - ref).abs()
     # fp32 output: only accumulation-order error remains
     assert float(err.max()) < 1e-5 * float(ref.abs().max()) * k ** 0.5
-    y16 = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=r.to(cuda), out_dtype=torch.float32)
-    assert torch.equal(y16, y)
+    y2 = _ops().gemm(x.to(cuda), w.to(cuda), b.to(cuda), residual=r.to(cuda), out_dtype=torch.float32, block_n=256,
+                     cta_pair=cta_pair)
+    assert torch.equal(y2, y)
 
 
 @pytest.mark.parametrize("d", [384, 768, 1024])
