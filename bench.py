@@ -65,6 +65,11 @@ def parse():
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
     ap.add_argument("--gemm-breakdown", action="store_true", help="print per-GEMM event times (stderr)")
+    ap.add_argument("--weights", default="random_init", choices=["random_init", "synthetic"],
+                    help="model weights: exporter packing of random init, or synthetic codes + lognormal scales")
+    ap.add_argument("--code-bits", type=int, default=2, help="phase code width b (3, 4 need --weights synthetic)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="configs[4] standalone complex-GEMM sweep: M in 256..65536 x K = N in 768/1024/3072/4096")
     return ap.parse_args()
 
 
@@ -263,7 +268,7 @@ def run_b200(args):
 
     cfg = CONFIGS[args.model]
     B = args.batch
-    model = PackedViT(cfg, dev, seed=0, act_bits=args.act_bits)
+    model = PackedViT(cfg, dev, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     images = torch.randn(B, 3, cfg.img, cfg.img, device=dev, generator=g).half()
     gathered = torch.empty((world * B, cfg.classes), dtype=torch.float32, device=dev) if world > 1 else None
@@ -404,11 +409,14 @@ def run_b200(args):
         "dtype": "f16",
         "data": "synthetic: N(0,1) images (seeded per rank), random-init weights packed to 2-bit phase codes",
         "config": {
-            "workload": f"{cfg.name} inference, packed 2-bit complex-phase linears (2 residual stages), "
-                        f"batch {B} per GPU",
+            "workload": f"{cfg.name} inference, packed {args.code_bits}-bit complex-phase linears (2 residual "
+                        f"stages, {args.weights} weights), batch {B} per GPU",
+            "code_bits": args.code_bits, "weights": args.weights,
             "batch_per_gpu": B, "global_batch": world * B, "tokens": cfg.tokens, "act_bits": args.act_bits,
             "parallelism": f"dp{world} (weight replica per rank, NCCL all-gather of logits)",
-            "l2": "per-step working set (activations of 49 GEMMs, >= 77 MB each) far larger than the 126 MB L2",
+            "l2": ("per-step working set (activations of the GEMMs, >= 77 MB each) far larger than the 126 MB L2"
+                   if B * cfg.tokens * cfg.dim * 2 >= 64e6 else
+                   "small batch: activations and packed weights are L2-resident across steps (latency-bound regime)"),
             "cuda_graph": use_graph,
         },
         "gemm": {"tflops": achieved, "flops_per_image": flops_img,
@@ -504,6 +512,12 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        for k in (768, 1024, 3072, 4096):
+            for m in (256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536):
+                args.gemm = f"{m},{k},{k}"
+                run_gemm(args)
+        return 0
     if args.gemm:
         return run_gemm(args)
     return run_b200(args)
