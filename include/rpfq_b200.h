@@ -126,12 +126,15 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
  * (RPFQ-ViT-main/quant_models/quant_i.py:513-554; Android wideLinear,
  * phase_linear.cpp:279-326): optional activation quantization, then the
  * tcgen05 GEMM over the dense coefficients `dense` (from rpfq_prepack_sm100),
- * bias and optional GELU / residual in the epilogue.
+ * bias and optional GELU / residual in the epilogue. With dense == NULL and
+ * m <= 256 (2-bit codes, n_c and k_c multiples of 8) the layer runs the fused
+ * decode path instead: the packed codes are TMA-staged and unpacked in shared
+ * memory into the MMA operand tiles, so only the packed weights are read.
  * When act_bits > 0, `scratch` must hold m * 2 k_c fp16 values (the quantized
  * activations); otherwise it may be NULL. */
 typedef struct RpfqWideLinearArgs {
-    const RpfqPackedLinear* layer; /* shapes (n_c, k_c); planes unused when dense != NULL */
-    const uint16_t* dense;         /* fp16 [2 n_c, 2 k_c] from rpfq_prepack_sm100 */
+    const RpfqPackedLinear* layer; /* shapes; the planes are read when dense == NULL */
+    const uint16_t* dense;         /* fp16 [2 n_c, 2 k_c] from rpfq_prepack_sm100, or NULL (m <= 256) */
     const uint16_t* x;             /* fp16 [m, 2 k_c], row stride ldx */
     int64_t ldx;
     const uint16_t* bias;          /* fp16 [2 n_c] or NULL */

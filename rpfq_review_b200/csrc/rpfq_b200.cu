@@ -11,12 +11,14 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "../../include/rpfq_b200.h"
 #include "actquant.cuh"
+#include "decode_gemm.cuh"
 #include "gemm.cuh"
 #include "layernorm.cuh"
 #include "prepack.cuh"
@@ -166,6 +168,38 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// x [m][2][k_c] view of the fp16 activations (Re half, Im half), box {64, 1, 128}, 128-B swizzle.
+int make_tmap_x_halves(CUtensorMap* m, const void* base, int64_t rows, int32_t k_c, int64_t ld) {
+    EncodeTiledFn fn;
+    int rc = encode_fn(&fn);
+    if (rc) return rc;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(k_c), 2, static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(k_c) * 2, static_cast<cuuint64_t>(ld) * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for the x halves view", (int)r);
+    return RPFQ_OK;
+}
+
+// packed codes [rows][bytes_per_row] uint8, box {16 bytes, box_rows}, no swizzle.
+int make_tmap_codes(CUtensorMap* m, const void* base, int64_t rows, int64_t bytes_per_row, int box_rows) {
+    EncodeTiledFn fn;
+    int rc = encode_fn(&fn);
+    if (rc) return rc;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(bytes_per_row), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(bytes_per_row)};
+    cuuint32_t box[2] = {16, static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for packed codes", (int)r);
+    return RPFQ_OK;
+}
+
 // ---------------------------------------------------------------- GEMM launch
 template <int BN, bool OUT_F32, int RES, bool PAIR>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
@@ -247,6 +281,99 @@ int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) 
     if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream);
     if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream);
     return launch_gemm<BN, false, 0, PAIR>(a, st, stream);
+}
+
+// ---------------------------------------------------------------- K3 fused decode launch
+constexpr int64_t kDecodeMaxRows = 256;
+
+template <int RB>
+int launch_decode(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx, DeviceState* st, cudaStream_t stream) {
+    using C = DecodeCfg<RB>;
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr_status[kMaxDevices];
+    int dev = 0;
+    RPFQ_CUDA(cudaGetDevice(&dev));
+    std::call_once(once[dev], [dev]() {
+        attr_status[dev] = cudaFuncSetAttribute(decode_gemm_sm100_kernel<RB>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
+    RPFQ_CUDA(attr_status[dev]);
+    const RpfqPackedLinear* L = a->layer;
+    CUtensorMap tx;
+    DecodeCodeMaps cm;
+    std::memset(&cm, 0, sizeof(cm));
+    int rc = make_tmap_x_halves(&tx, xin, a->m, L->k_c, ldx);
+    DecodeGemmParams p;
+    std::memset(&p, 0, sizeof(p));
+    for (int s = 0; s < L->stages && !rc; ++s) {
+        rc = make_tmap_codes(&cm.plane[s], L->u[s].codes, L->n_cp, L->k_cp / 4, RB);
+        if (!rc) rc = make_tmap_codes(&cm.plane[L->stages + s], L->w[s].codes, L->n_cp, L->k_cp / 4, RB);
+        p.gamma_re[s] = reinterpret_cast<const __half*>(L->u[s].gamma_real);
+        p.gamma_im[s] = reinterpret_cast<const __half*>(L->u[s].gamma_imag);
+        p.gamma_re[L->stages + s] = reinterpret_cast<const __half*>(L->w[s].gamma_real);
+        p.gamma_im[L->stages + s] = reinterpret_cast<const __half*>(L->w[s].gamma_imag);
+    }
+    if (rc) return rc;
+    p.stages = L->stages;
+    p.n_c = L->n_c;
+    p.k_c = L->k_c;
+    p.n_cp = L->n_cp;
+    p.k_cp = L->k_cp;
+    p.rows_per_item = RB;
+    p.bias = reinterpret_cast<const __half*>(a->bias);
+    p.residual = a->residual;
+    p.ldr = a->ldr;
+    p.y = a->y;
+    p.ldy = a->ldy;
+    p.m = a->m;
+    p.activation = a->activation;
+    p.out_f32 = (a->flags & RPFQ_GEMM_OUT_F32) ? 1 : 0;
+    p.err = st->err_word;
+    const int items = (L->n_c + RB - 1) / RB;
+    const int grid = items < st->sm_count ? items : st->sm_count;
+    decode_gemm_sm100_kernel<RB><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, cm, p);
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+int decode_path(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx, cudaStream_t stream) {
+    const RpfqPackedLinear* L = a->layer;
+    if (L->code_bits != 2)
+        return fail(RPFQ_ERR_UNSUPPORTED, "fused decode path: 2-bit codes only (decode 3/4-bit layers with rpfq_prepack_sm100)");
+    if (a->m > kDecodeMaxRows)
+        return fail(RPFQ_ERR_UNSUPPORTED, "fused decode path: m <= %lld rows (got %lld); prepack for larger m",
+                    (long long)kDecodeMaxRows, (long long)a->m);
+    if (L->k_c % 8 || L->n_c % 8)
+        return fail(RPFQ_ERR_UNSUPPORTED, "fused decode path: n_c and k_c must be multiples of 8");
+    if (ldx % 8 || a->ldy % 8 || (a->residual && a->ldr % 8) || !aligned16(xin) || !aligned16(a->y) ||
+        (a->bias && !aligned16(a->bias)) || (a->residual && !aligned16(a->residual)))
+        return fail(RPFQ_ERR_INVALID, "fused decode path: 16-byte aligned pointers and strides required");
+    if (a->residual && (((a->flags & RPFQ_GEMM_RESIDUAL_F32) != 0) != ((a->flags & RPFQ_GEMM_OUT_F32) != 0)))
+        return fail(RPFQ_ERR_UNSUPPORTED, "fused decode path: the residual must have the output's dtype");
+    for (int s = 0; s < L->stages; ++s) {
+        const RpfqPhasePlane* ps[2] = {&L->u[s], &L->w[s]};
+        for (const RpfqPhasePlane* pl : ps)
+            if (!pl->codes || !pl->gamma_real || !pl->gamma_imag || !aligned16(pl->codes))
+                return fail(RPFQ_ERR_INVALID, "fused decode path: stage %d needs 16-byte aligned codes and gammas", s);
+    }
+    if (a->m == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    // Row block: the smallest block that still fills the SMs (more x reuse per
+    // weight tile with larger blocks, more CTAs with smaller ones).
+    static const int forced_rows = [] {
+        const char* e = std::getenv("RPFQ_DECODE_ROWS");
+        return e ? std::atoi(e) : 0;
+    }();
+    int rb = forced_rows;
+    if (rb != 16 && rb != 32 && rb != 64) {
+        const int64_t n_c = L->n_c;
+        rb = (n_c + 63) / 64 >= st->sm_count ? 64 : ((n_c + 31) / 32 >= st->sm_count ? 32 : 16);
+    }
+    if (rb == 64) return launch_decode<64>(a, xin, ldx, st, stream);
+    if (rb == 32) return launch_decode<32>(a, xin, ldx, st, stream);
+    return launch_decode<16>(a, xin, ldx, st, stream);
 }
 
 int pick_block_n(int64_t m, int n, int sm_count) {
@@ -476,9 +603,10 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
     if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_wide_linear_sm100: null args");
     int rc = check_layer(a->layer, "rpfq_wide_linear_sm100");
     if (rc) return rc;
-    if (!a->dense)
+    if (!a->dense && a->m > kDecodeMaxRows)
         return fail(RPFQ_ERR_INVALID,
-                    "rpfq_wide_linear_sm100: dense coefficients are required (decode them once with rpfq_prepack_sm100)");
+                    "rpfq_wide_linear_sm100: for m > %lld the dense coefficients are required (decode them once with "
+                    "rpfq_prepack_sm100)", (long long)kDecodeMaxRows);
     const int32_t K = 2 * a->layer->k_c;
     const int32_t N = 2 * a->layer->n_c;
     const uint16_t* xin = a->x;
@@ -491,6 +619,7 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
         xin = a->scratch;
         ldx = K;
     }
+    if (!a->dense) return decode_path(a, xin, ldx, static_cast<cudaStream_t>(stream));
     RpfqGemmArgs g;
     std::memset(&g, 0, sizeof(g));
     g.x = xin;

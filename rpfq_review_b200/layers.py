@@ -38,13 +38,17 @@ class PackedPhaseLinear(nn.Module):
 
     ``forward(x[..., in_features]) -> y[..., out_features]`` computes
     ``act(U x + W conj(x) + bias)`` (+ ``residual``) with optional activation
-    quantization of x (``act_num_bits``). The dense fp16 coefficients are
-    decoded once on the GPU (K1) and kept as a non-persistent buffer.
+    quantization of x (``act_num_bits``). With ``cache_dense=True`` (the
+    default; the reference runtime's fused fp16 cache) the dense fp16
+    coefficients are decoded once on the GPU and kept as a non-persistent
+    buffer. With ``cache_dense=False`` only the packed planes stay resident:
+    calls of at most ``ops.FUSED_DECODE_MAX_ROWS`` rows decode the codes inside
+    the GEMM, larger calls decode into a temporary dense matrix first.
     """
 
     def __init__(self, in_features: int, out_features: int, stages: int = 2, code_bits: int = 2,
                  enable_act_quant: bool = False, act_num_bits: int = 4, activation: str = "none",
-                 rounding: str = "rne", device=None):
+                 rounding: str = "rne", cache_dense: bool = True, device=None):
         super().__init__()
         if in_features % 2 or out_features % 2:
             raise ValueError("Complex-phase QAT requires even in/out features.")
@@ -54,6 +58,7 @@ class PackedPhaseLinear(nn.Module):
         self.act_bits = act_num_bits if enable_act_quant else 0
         self.activation = activation
         self.rounding = rounding
+        self.cache_dense = cache_dense
         n_cp, k_cp = round_up(self.n_c, BLOCK_SIZE), round_up(self.k_c, BLOCK_SIZE)
         for tag in ("u", "w"):
             for s in range(stages):
@@ -99,16 +104,24 @@ class PackedPhaseLinear(nn.Module):
         # The TMA path needs 16-byte row strides: real K and N multiples of 8.
         return self.in_features % 8 == 0 and self.out_features % 8 == 0
 
-    def prepack(self) -> torch.Tensor:
-        """Decode the packed planes once (K1). Layers whose real dims are not
-        multiples of 8 keep a zero-padded copy ``[N8, K8]`` for the GEMM."""
+    @property
+    def _fused_decode_ok(self) -> bool:
+        # the fused decode path stores 8 complex columns per vector
+        return self.code_bits == 2 and self.n_c % 8 == 0 and self.k_c % 8 == 0
+
+    def _decode_dense(self) -> torch.Tensor:
         dense = ops.prepack(self.packed(), self.rounding)
         if not self._aligned:
             n8, k8 = round_up(self.out_features, 8), round_up(self.in_features, 8)
             padded = torch.zeros((n8, k8), dtype=torch.float16, device=dense.device)
             padded[: self.out_features, : self.in_features] = dense
             dense = padded
-        self.dense = dense
+        return dense
+
+    def prepack(self) -> torch.Tensor:
+        """Decode the packed planes once (K1). Layers whose real dims are not
+        multiples of 8 keep a zero-padded copy ``[N8, K8]`` for the GEMM."""
+        self.dense = self._decode_dense()
         return self.dense
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
@@ -121,28 +134,36 @@ class PackedPhaseLinear(nn.Module):
         the epilogue and may be ``out`` itself. ``prequantized=True`` skips the
         activation quantization (already applied by the producer, e.g. the
         fused LayerNorm kernel)."""
-        if self.dense is None or self.dense.device != x.device:
-            self.prepack()
         if out_dtype is None:
             out_dtype = out.dtype if out is not None else (x.dtype if x.dtype in (torch.float16, torch.float32)
                                                            else torch.float16)
         x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
         act_bits = 0 if prequantized else self.act_bits
-        if self._aligned:
-            return ops.wide_linear(x16, self.packed(), self.dense, act_bits, self.activation, residual, out=out,
+        rows = x.numel() // self.in_features if self.in_features else 0
+        if not self.cache_dense and self._fused_decode_ok and rows <= ops.FUSED_DECODE_MAX_ROWS:
+            return ops.wide_linear(x16, self.packed(), None, act_bits, self.activation, residual, out=out,
                                    out_dtype=out_dtype)
-        y = self._forward_padded(x16, residual, act_bits, out_dtype)
+        if self.cache_dense:
+            if self.dense is None or self.dense.device != x.device:
+                self.prepack()
+            dense = self.dense
+        else:
+            dense = self._decode_dense()
+        if self._aligned:
+            return ops.wide_linear(x16, self.packed(), dense, act_bits, self.activation, residual, out=out,
+                                   out_dtype=out_dtype)
+        y = self._forward_padded(x16, dense, residual, act_bits, out_dtype)
         if out is not None:
             out.copy_(y)
             return out
         return y
 
-    def _forward_padded(self, x16: torch.Tensor, residual: torch.Tensor | None, act_bits: int,
-                        out_dtype: torch.dtype) -> torch.Tensor:
+    def _forward_padded(self, x16: torch.Tensor, dense: torch.Tensor, residual: torch.Tensor | None,
+                        act_bits: int, out_dtype: torch.dtype) -> torch.Tensor:
         """Layers whose K or N is not a multiple of 8: run the GEMM on
         zero-padded copies (x, bias, residual) and crop the output."""
         K, N = self.in_features, self.out_features
-        n8, k8 = self.dense.shape
+        n8, k8 = dense.shape
         lead = x16.shape[:-1]
         x2 = x16.reshape(-1, K)
         if act_bits:
@@ -155,7 +176,7 @@ class PackedPhaseLinear(nn.Module):
         if residual is not None:
             rp = torch.zeros((x2.shape[0], n8), dtype=residual.dtype, device=x16.device)
             rp[:, :N] = residual.reshape(-1, N)
-        y = ops.gemm(xp, self.dense, bias, rp, self.activation, out_dtype=out_dtype)
+        y = ops.gemm(xp, dense, bias, rp, self.activation, out_dtype=out_dtype)
         return y[:, :N].contiguous().reshape(*lead, N)
 
     def extra_repr(self) -> str:

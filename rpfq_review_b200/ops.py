@@ -55,6 +55,11 @@ def _count_launch(n: int = 1) -> None:
         _timer.launches += n
 
 
+# Largest row count of the fused decode path (``dense=None``); the C ABI
+# rejects more.
+FUSED_DECODE_MAX_ROWS = 256
+
+
 def _p(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
 
@@ -200,15 +205,20 @@ def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -
     return out.reshape(x.shape)
 
 
-def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor, act_bits: int = 0,
+def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None, act_bits: int = 0,
                 activation="none", residual: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
     """Whole layer through ``rpfq_wide_linear_sm100``: optional activation
     quantization, then the GEMM over the prepacked coefficients with bias and
     epilogue. ``x`` is fp16 ``[..., 2 k_c]``; ``residual`` / ``out`` fp16 or
-    fp32 (``out`` may be ``residual`` for an in-place residual add)."""
+    fp32 (``out`` may be ``residual`` for an in-place residual add).
+
+    ``dense=None`` selects the fused decode path (at most ``FUSED_DECODE_MAX_ROWS``
+    rows, 2-bit codes, ``n_c`` and ``k_c`` multiples of 8): the packed planes
+    are decoded inside the GEMM and no dense matrix exists anywhere."""
     _require(x, "x")
-    _require(dense, "dense")
+    if dense is not None:
+        _require(dense, "dense")
     K, N = 2 * layer.k_c, 2 * layer.n_c
     x2, ldx = _rows(x, K, "x")
     m = x2.shape[0]
@@ -224,7 +234,7 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor, act_bi
         raise ValueError("out must be a row-major view with unit column stride")
     scratch = torch.empty((m, K), dtype=torch.float16, device=x.device) if act_bits else None
     s = layer_struct(layer)
-    a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=dense.data_ptr(), x=x2.data_ptr(), ldx=ldx,
+    a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=_p(dense), x=x2.data_ptr(), ldx=ldx,
                                 bias=_p(layer.bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
                                 act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch),
                                 flags=_flags(out, r2))
