@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
+    ap.add_argument("--fused-decode", action="store_true",
+                    help="--gemm: the fused decode path (packed planes only, M <= 256), rotating over enough "
+                         "layer copies that the packed weights stream from HBM")
     ap.add_argument("--gemm-breakdown", action="store_true", help="print per-GEMM event times (stderr)")
     ap.add_argument("--weights", default="random_init", choices=["random_init", "synthetic"],
                     help="model weights: exporter packing of random init, or synthetic codes + lognormal scales")
@@ -395,6 +398,7 @@ def run_b200(args):
             cpu = {"value": None, "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
                    "sample": f"failed: {type(e).__name__}: {e}"}
 
+    traffic = _gemm_traffic(cfg, B, args)
     line = {
         "metric": METRIC,
         "value": value,
@@ -422,9 +426,11 @@ def run_b200(args):
         "gemm": {"tflops": achieved, "flops_per_image": flops_img,
                  "ms_per_step": gemm_ms, "share_of_step": (gemm_ms / (max_ms / args.steps)) if gemm_ms else None},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "frac": (achieved / peak) if achieved else None,
+                     "traffic": traffic["bytes_per_launch"] if traffic else None,
+                     "traffic_detail": traffic,
                      "peak_source": f"{peak_src} bf16_tflops_sustained (cuBLAS, power-capped loop)",
-                     "kernel": "gemm_f16_sm100_kernel (tcgen05, 128x256 tiles)"},
+                     "kernel": "gemm_f16_sm100_kernel (tcgen05, 256x256 tiles on CTA pairs)"},
         "e2e": {"value": e2e_value, "unit": "images/s",
                 "h2d_bytes_per_step": int(host_imgs.numel() * host_imgs.element_size()),
                 "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size())},
@@ -435,6 +441,26 @@ def run_b200(args):
     }
     print(json.dumps(line))
     return 0
+
+
+# DRAM bytes (read + write) per launch of the four per-layer GEMMs of the
+# ViT-B/16 batch-256 step, from one `ncu --set full` capture of each at that
+# exact shape (files profiles/gemm_f16_sm100_{qkv,proj_residual,fc1_gelu,
+# fc2_residual}_50432x*.md), with the algorithmic bytes 2MK + 2NK + 2N + e*MN
+# of each (e = 2 for fp16 out, 8 for fp32 out + fp32 residual read).
+_VITB256_GEMM_TRAFFIC = {"qkv": (258.6e6, 313.4e6), "proj_residual": (417.1e6, 388.5e6),
+                         "fc1_gelu": (334.6e6, 392.0e6), "fc2_residual": (760.1e6, 624.4e6)}
+
+
+def _gemm_traffic(cfg, batch, args):
+    """Measured DRAM traffic per GEMM launch (mean over the layer's four
+    GEMMs) for the configuration those captures cover; None otherwise."""
+    if cfg.name != "vit_base_patch16_224" or batch != 256 or args.code_bits != 2 or args.act_bits:
+        return None
+    meas = sum(v[0] for v in _VITB256_GEMM_TRAFFIC.values()) / 4
+    alg = sum(v[1] for v in _VITB256_GEMM_TRAFFIC.values()) / 4
+    return {"bytes_per_launch": meas, "algorithmic_bytes_per_launch": alg, "ratio": meas / alg,
+            "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture per GEMM shape"}
 
 
 def run_gemm(args):
@@ -450,8 +476,20 @@ def run_gemm(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     layer = random_packed(n // 2, k // 2, seed=0, device=dev)
-    mod = PackedPhaseLinear.from_packed(layer, enable_act_quant=args.act_bits > 0, act_num_bits=args.act_bits or 4)
-    mod.prepack()
+    mod = PackedPhaseLinear.from_packed(layer, enable_act_quant=args.act_bits > 0, act_num_bits=args.act_bits or 4,
+                                        cache_dense=not args.fused_decode)
+    packed_bytes = sum(t.numel() * t.element_size() for v in layer.planes.values() for t in v)
+    copies = 1
+    if args.fused_decode:
+        from rpfq_review_b200.packing import PackedLayer
+        # enough distinct copies of the packed planes that one pass over them
+        # exceeds 3x the 126 MB L2: each launch reads its weights from HBM
+        copies = min(4096, max(2, -(-3 * 126_000_000 // packed_bytes)))
+        packs = [PackedLayer(layer.n_c, layer.k_c, layer.stages, layer.code_bits,
+                             {kk: tuple(t.clone() for t in v) for kk, v in layer.planes.items()}, layer.bias)
+                 for _ in range(copies)]
+    else:
+        mod.prepack()
     g = torch.Generator(device=dev).manual_seed(1)
     # two input / output sets, alternated, so that consecutive launches do not
     # find their operands in L2 when the set is larger than L2
@@ -464,7 +502,10 @@ def run_gemm(args):
 
     def step(i):
         res = ys[i & 1] if args.epilogue == "residual_f32" else None
-        if args.block_n or args.cta_pair or args.epilogue != "none":
+        if args.fused_decode:
+            ops.wide_linear(xs[i & 1], packs[i % copies], None, mod.act_bits, activation=act, residual=res,
+                            out=ys[i & 1])
+        elif args.block_n or args.cta_pair or args.epilogue != "none":
             ops.gemm(xs[i & 1], mod.dense, mod.bias, residual=res, activation=act, block_n=args.block_n,
                      out=ys[i & 1], cta_pair=args.cta_pair)
         else:
@@ -481,8 +522,9 @@ def run_gemm(args):
     with torch.cuda.stream(side):
         step(0)
     torch.cuda.current_stream(dev).wait_stream(side)
+    launches = max(args.steps, copies)
     with torch.cuda.graph(graph):
-        for i in range(args.steps):
+        for i in range(launches):
             step(i)
     graph.replay()
     torch.cuda.synchronize()
@@ -491,7 +533,7 @@ def run_gemm(args):
     graph.replay()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / launches
     flops = 2 * m * n * k
     peaks, src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
@@ -501,6 +543,8 @@ def run_gemm(args):
         hbm_bytes += 6 * m * n
     print(json.dumps({"metric": "complex-GEMM TFLOP/s", "value": tf, "unit": "TFLOP/s", "shape": [m, n, k],
                       "epilogue": args.epilogue,
+                      "path": "fused_decode" if args.fused_decode else "prepacked",
+                      "weight_copies": copies, "packed_weight_bytes": packed_bytes,
                       "us_per_launch": ms * 1000, "act_bits": args.act_bits,
                       "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                                    "frac": tf / peak, "peak_source": f"{src} bf16_tflops (burst)"},

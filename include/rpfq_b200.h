@@ -16,6 +16,7 @@
  *   - wideLinear / wideLinearReference        RPFQ-ViTAndroid/app/src/main/cpp/ops/phase_linear.h:59-68
  *   - buildFusedWideLinearCache               RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.h:30-31
  *   - ActivationQuantSTE.forward              RPFQ-ViT-main/quant_models/quant_i.py:442-455
+ *   - save_quantized_linear (exporter packing) RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py:384-423
  *
  * Layout conventions (unchanged from the reference):
  *   real Linear(in = K, out = N) = complex map k_c = K/2 -> n_c = N/2;
@@ -150,6 +151,32 @@ typedef struct RpfqWideLinearArgs {
     int32_t reserved;
 } RpfqWideLinearArgs;
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
+
+/* Output buffers of one residual stage of U or W for rpfq_pack_linear_sm100:
+ * codes uint8 [n_cp, k_cp/4], gammas fp16 [n_cp, k_cp/256]. */
+typedef struct RpfqPhasePlaneOut {
+    uint8_t* codes;
+    uint16_t* gamma_real;
+    uint16_t* gamma_imag;
+} RpfqPhasePlaneOut;
+
+/* Device memory rpfq_pack_linear_sm100 needs as workspace for a layer with
+ * complex dims (n_c, k_c): the four fp32 residual planes plus the partial
+ * sums of the scale reductions. 0 for non-positive dims. */
+uint64_t rpfq_pack_workspace_bytes(int32_t n_c, int32_t k_c);
+
+/* The exporter's packing on the device: float weight [2 n_c, 2 k_c] (fp32,
+ * row stride ldw elements) -> `stages` residual stages of 2-bit axial codes and
+ * fp16 gammas for U and for W (u_out[0..stages), w_out[0..stages)), padding
+ * included, bit-identical to the reference exporter: save_quantized_linear /
+ * quantize_complex_weight / phase_quantize_axis,
+ * RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py:189-224,257-289,317-333,384-423.
+ * The bias is not touched (the exporter stores fp16(bias)). The scale of each
+ * axis is a mean over the whole matrix, reduced on the device: no host sync.
+ * workspace: rpfq_pack_workspace_bytes(n_c, k_c) bytes, 16-byte aligned. */
+int rpfq_pack_linear_sm100(const float* weight, int64_t ldw, int32_t n_c, int32_t k_c, int32_t stages,
+                           const RpfqPhasePlaneOut* u_out, const RpfqPhasePlaneOut* w_out, void* workspace,
+                           uint64_t workspace_bytes, rpfq_stream_t stream);
 
 /* Allocation-free variant of rpfq_wide_linear_sm100 — no counterpart in the
  * reference. For callers that cannot allocate device memory when they run a

@@ -35,6 +35,8 @@ EXPORTED_SYMBOLS = (
     "rpfq_layernorm_sm100",
     "rpfq_wide_linear_sm100",
     "rpfq_wide_linear_noalloc_sm100",
+    "rpfq_pack_workspace_bytes",
+    "rpfq_pack_linear_sm100",
     "rpfq_last_error",
     "rpfq_device_error",
     "rpfq_version",
@@ -42,6 +44,10 @@ EXPORTED_SYMBOLS = (
 
 
 class RpfqPhasePlane(ctypes.Structure):
+    _fields_ = [("codes", ctypes.c_void_p), ("gamma_real", ctypes.c_void_p), ("gamma_imag", ctypes.c_void_p)]
+
+
+class RpfqPhasePlaneOut(ctypes.Structure):
     _fields_ = [("codes", ctypes.c_void_p), ("gamma_real", ctypes.c_void_p), ("gamma_imag", ctypes.c_void_p)]
 
 
@@ -108,10 +114,15 @@ def lib() -> ctypes.CDLL:
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_wide_linear_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_wide_linear_noalloc_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
+        L.rpfq_pack_workspace_bytes.argtypes = [I32, I32]
+        L.rpfq_pack_workspace_bytes.restype = ctypes.c_uint64
+        L.rpfq_pack_linear_sm100.argtypes = [P, I64, I32, I32, I32, ctypes.POINTER(RpfqPhasePlaneOut),
+                                             ctypes.POINTER(RpfqPhasePlaneOut), P, ctypes.c_uint64, P]
         L.rpfq_last_error.restype = ctypes.c_char_p
         L.rpfq_device_error.argtypes = [ctypes.POINTER(I32)]
         for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
-                     "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_device_error",
+                     "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_pack_linear_sm100",
+                     "rpfq_device_error",
                      "rpfq_version"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L

@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -21,6 +22,7 @@
 #include "decode_gemm.cuh"
 #include "gemm.cuh"
 #include "layernorm.cuh"
+#include "pack.cuh"
 #include "prepack.cuh"
 
 namespace rpfq {
@@ -596,6 +598,71 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
         default: return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: row length %d (supported: 384, 768, 1024)", d);
     }
     RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+uint64_t rpfq_pack_workspace_bytes(int32_t n_c, int32_t k_c) {
+    if (n_c <= 0 || k_c <= 0) return 0;
+    return 16ull * static_cast<uint64_t>(n_c) * static_cast<uint64_t>(k_c) +
+           static_cast<uint64_t>(kPackMaxStatsCtas) * kPackPartials * sizeof(double);
+}
+
+int rpfq_pack_linear_sm100(const float* weight, int64_t ldw, int32_t n_c, int32_t k_c, int32_t stages,
+                           const RpfqPhasePlaneOut* u_out, const RpfqPhasePlaneOut* w_out, void* workspace,
+                           uint64_t workspace_bytes, rpfq_stream_t stream) {
+    if (!weight || !u_out || !w_out || !workspace) return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: null pointer");
+    if (n_c <= 0 || k_c <= 0)
+        return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: complex dims must be positive (got %d, %d)", n_c, k_c);
+    if (stages < 1 || stages > 4)
+        return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: stages must be 1..4 (got %d)", stages);
+    if (ldw < 2 * static_cast<int64_t>(k_c))
+        return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: ldw %lld < 2 k_c", (long long)ldw);
+    if ((reinterpret_cast<uintptr_t>(weight) & 3) || !aligned16(workspace))
+        return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: weight must be 4-byte, workspace 16-byte aligned");
+    if (workspace_bytes < rpfq_pack_workspace_bytes(n_c, k_c))
+        return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: workspace of %llu bytes, need %llu",
+                    (unsigned long long)workspace_bytes, (unsigned long long)rpfq_pack_workspace_bytes(n_c, k_c));
+    for (int s = 0; s < stages; ++s)
+        for (const RpfqPhasePlaneOut* o : {&u_out[s], &w_out[s]})
+            if (!o->codes || !o->gamma_real || !o->gamma_imag || (reinterpret_cast<uintptr_t>(o->gamma_real) & 1) ||
+                (reinterpret_cast<uintptr_t>(o->gamma_imag) & 1))
+                return fail(RPFQ_ERR_INVALID, "rpfq_pack_linear_sm100: stage %d output buffers missing or misaligned", s);
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    PackParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.weight = weight;
+    p.ldw = ldw;
+    p.n_c = n_c;
+    p.k_c = k_c;
+    p.n_cp = (n_c + 255) / 256 * 256;
+    p.k_cp = (k_c + 255) / 256 * 256;
+    p.res = static_cast<float*>(workspace);
+    p.partials = reinterpret_cast<double*>(static_cast<uint8_t*>(workspace) +
+                                           16ull * static_cast<uint64_t>(n_c) * static_cast<uint64_t>(k_c));
+    const int64_t elems = static_cast<int64_t>(n_c) * k_c;
+    int64_t sc = (elems + kPackThreads - 1) / kPackThreads;
+    const int stats_ctas = static_cast<int>(std::min<int64_t>(sc, std::min(kPackMaxStatsCtas, 4 * st->sm_count)));
+    const int64_t bytes = static_cast<int64_t>(p.n_cp) * (p.k_cp / 4);
+    const int code_ctas =
+        static_cast<int>(std::min<int64_t>((bytes + kPackThreads - 1) / kPackThreads, 16 * st->sm_count));
+    p.stats_ctas = stats_ctas;
+    for (int s = 0; s < stages; ++s) {
+        p.first = s == 0;
+        p.write_res = s + 1 < stages;
+        p.codes[0] = u_out[s].codes;
+        p.codes[1] = w_out[s].codes;
+        p.gre[0] = u_out[s].gamma_real;
+        p.gim[0] = u_out[s].gamma_imag;
+        p.gre[1] = w_out[s].gamma_real;
+        p.gim[1] = w_out[s].gamma_imag;
+        pack_stats_kernel<<<stats_ctas, kPackThreads, 0, strm>>>(p);
+        RPFQ_CUDA(cudaGetLastError());
+        pack_codes_kernel<<<code_ctas, kPackThreads, 0, strm>>>(p);
+        RPFQ_CUDA(cudaGetLastError());
+    }
     return RPFQ_OK;
 }
 

@@ -107,6 +107,43 @@ def prepack(layer: PackedLayer, rounding: str = "rne") -> torch.Tensor:
     return out
 
 
+def pack_linear(weight: torch.Tensor, bias: torch.Tensor | None = None, stages: int = 2) -> PackedLayer:
+    """The exporter's packing on the GPU (``save_quantized_linear``,
+    export_rpfq_vit_to_mlx.py:384-423) through ``rpfq_pack_linear_sm100``:
+    float ``[N, K]`` weight -> ``stages`` residual stages of 2-bit axial codes
+    and fp16 gammas for U and W, bit-identical to the exporter; bias -> fp16."""
+    if not weight.is_cuda:
+        raise ValueError("weight must be a CUDA tensor (rpfq_pack_linear_sm100 packs on the GPU)")
+    n, k = weight.shape
+    if n % 2 or k % 2:
+        raise ValueError(f"Complex decomposition requires even dims, got {tuple(weight.shape)}")
+    from .packing import BLOCK_SIZE, round_up
+    w = weight.detach().to(torch.float32)
+    if w.stride(1) != 1 or w.data_ptr() % 4:
+        w = w.contiguous()
+    dev = w.device
+    n_c, k_c = n // 2, k // 2
+    n_cp, k_cp = round_up(n_c, BLOCK_SIZE), round_up(k_c, BLOCK_SIZE)
+    outs = {"u": (_lib.RpfqPhasePlaneOut * stages)(), "w": (_lib.RpfqPhasePlaneOut * stages)()}
+    planes = {}
+    for tag in ("u", "w"):
+        for i in range(stages):
+            codes = torch.empty((n_cp, k_cp // 4), dtype=torch.uint8, device=dev)
+            gr = torch.empty((n_cp, k_cp // BLOCK_SIZE), dtype=torch.float16, device=dev)
+            gi = torch.empty_like(gr)
+            outs[tag][i].codes, outs[tag][i].gamma_real, outs[tag][i].gamma_imag = (
+                codes.data_ptr(), gr.data_ptr(), gi.data_ptr())
+            planes[f"{tag}_s{i}"] = (codes, gr, gi)
+    L = _lib.lib()
+    ws_bytes = int(L.rpfq_pack_workspace_bytes(n_c, k_c))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.rpfq_pack_linear_sm100(w.data_ptr(), w.stride(0), n_c, k_c, stages, outs["u"], outs["w"],
+                                            ws.data_ptr(), ws_bytes, _stream(dev)), "rpfq_pack_linear_sm100")
+    b = torch.zeros(n, device=dev) if bias is None else bias.detach()
+    return PackedLayer(n_c, k_c, stages, 2, planes, b.to(device=dev, dtype=torch.float16).contiguous())
+
+
 def _flags(out: torch.Tensor, residual: torch.Tensor | None) -> int:
     f = 0
     if out.dtype == torch.float32:

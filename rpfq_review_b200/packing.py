@@ -197,7 +197,19 @@ def pack_linear(weight: torch.Tensor, bias: torch.Tensor | None, stages: int = 2
     """Float ``[N, K]`` weight -> packed layer, the exporter's
     ``save_quantized_linear`` (export…py:384-423): widely-linear decomposition
     (export…py:317-333), then ``stages`` residual axial quantization steps
-    (export…py:257-289) for U and for W."""
+    (export…py:257-289) for U and for W.
+
+    CUDA weights are packed by the GPU packer (``ops.pack_linear``, two
+    kernels per stage, no host sync); CPU weights by the same algorithm in
+    torch, the offline exporter's setting."""
+    if weight.is_cuda:
+        from . import ops
+        return ops.pack_linear(weight, bias, stages)
+    return pack_linear_torch(weight, bias, stages)
+
+
+def pack_linear_torch(weight: torch.Tensor, bias: torch.Tensor | None, stages: int = 2) -> PackedLayer:
+    """:func:`pack_linear` as torch tensor ops on the weight's device."""
     n, k = weight.shape
     if n % 2 or k % 2:
         raise ValueError(f"Complex decomposition requires even dims, got {tuple(weight.shape)}")
