@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--model", default="vit_base_patch16_224")
     ap.add_argument("--batch", type=int, default=256, help="images per GPU")
     ap.add_argument("--act-bits", type=int, default=0)
+    ap.add_argument("--vision-quant", action="store_true",
+                    help="every packed linear uses the vision-aware (token-saliency, int8) activation quantizer")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-sample", type=int, default=1, help="images per CPU-baseline step")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline in the GPU arm")
@@ -271,7 +273,10 @@ def run_b200(args):
 
     cfg = CONFIGS[args.model]
     B = args.batch
-    model = PackedViT(cfg, dev, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits)
+    vq = dict(salient_token_ratio=0.25, background_clip_ratio=0.75, energy_score_weight=0.5,
+              protect_cls_token=True) if args.vision_quant else None
+    model = PackedViT(cfg, dev, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits,
+                      vision_quant=vq)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     images = torch.randn(B, 3, cfg.img, cfg.img, device=dev, generator=g).half()
     gathered = torch.empty((world * B, cfg.classes), dtype=torch.float32, device=dev) if world > 1 else None
@@ -417,6 +422,8 @@ def run_b200(args):
                         f"stages, {args.weights} weights), batch {B} per GPU",
             "code_bits": args.code_bits, "weights": args.weights,
             "batch_per_gpu": B, "global_batch": world * B, "tokens": cfg.tokens, "act_bits": args.act_bits,
+            "act_quantizer": "vision-aware int8 (token saliency)" if args.vision_quant else
+                             (f"ActivationQuantSTE {args.act_bits}-bit" if args.act_bits else "none"),
             "parallelism": f"dp{world} (weight replica per rank, NCCL all-gather of logits)",
             "l2": ("per-step working set (activations of the GEMMs, >= 77 MB each) far larger than the 126 MB L2"
                    if B * cfg.tokens * cfg.dim * 2 >= 64e6 else

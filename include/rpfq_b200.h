@@ -17,6 +17,7 @@
  *   - buildFusedWideLinearCache               RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.h:30-31
  *   - ActivationQuantSTE.forward              RPFQ-ViT-main/quant_models/quant_i.py:442-455
  *   - save_quantized_linear (exporter packing) RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py:384-423
+ *   - VisionAwareActivationQuantizer.forward  RPFQ-ViT-main/quant_models/quant_rpfq_vit_vision.py:26-171
  *
  * Layout conventions (unchanged from the reference):
  *   real Linear(in = K, out = N) = complex map k_c = K/2 -> n_c = N/2;
@@ -151,6 +152,27 @@ typedef struct RpfqWideLinearArgs {
     int32_t reserved;
 } RpfqWideLinearArgs;
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
+
+/* Vision-aware activation quantization of `images` x `tokens` rows of fp16
+ * x[row] = [Re | Im] (k = 2 k_c columns, k_c a multiple of 8) into xq (may
+ * alias x): the reference's VisionAwareActivationQuantizer.forward
+ * (RPFQ-ViT-main/quant_models/quant_rpfq_vit_vision.py:26-171). With
+ * tokens = 1 + g*g the ceil(g*g * salient_ratio) most salient patch tokens per
+ * image (energy and 4-neighbour contrast score) and, if protect_cls_token,
+ * the CLS token keep per-token int8 scales; the other tokens share one
+ * per-image scale from their amax times background_clip_ratio. Any other
+ * token count quantizes every row with its own int8 scale, like the
+ * reference's fallback. mask_out (optional, [images * tokens]) receives 1 for
+ * salient rows. The ratios are doubles as in the reference (Python floats);
+ * saliency grids up to 128 x 128 patches. With a saliency grid the call
+ * needs `workspace`: rpfq_vision_workspace_bytes(images, tokens) bytes of
+ * device memory, 16-byte aligned (per-token statistics and scales); it may be
+ * NULL otherwise. */
+uint64_t rpfq_vision_workspace_bytes(int64_t images, int32_t tokens);
+int rpfq_vision_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t images,
+                                int32_t tokens, int32_t k, double salient_ratio, double background_clip_ratio,
+                                double energy_score_weight, int32_t protect_cls_token, uint8_t* mask_out,
+                                void* workspace, uint64_t workspace_bytes, rpfq_stream_t stream);
 
 /* Output buffers of one residual stage of U or W for rpfq_pack_linear_sm100:
  * codes uint8 [n_cp, k_cp/4], gammas fp16 [n_cp, k_cp/256]. */

@@ -23,6 +23,7 @@
 #include "gemm.cuh"
 #include "layernorm.cuh"
 #include "pack.cuh"
+#include "vision_quant.cuh"
 #include "prepack.cuh"
 
 namespace rpfq {
@@ -597,6 +598,95 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
         case 1024: layernorm_f32_f16_kernel<1024><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
         default: return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: row length %d (supported: 384, 768, 1024)", d);
     }
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+uint64_t rpfq_vision_workspace_bytes(int64_t images, int32_t tokens) {
+    if (images <= 0 || tokens <= 0) return 0;
+    return 24ull * static_cast<uint64_t>(images) * static_cast<uint64_t>(tokens);
+}
+
+int rpfq_vision_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t images,
+                                int32_t tokens, int32_t k, double salient_ratio, double background_clip_ratio,
+                                double energy_score_weight, int32_t protect_cls_token, uint8_t* mask_out,
+                                void* workspace, uint64_t workspace_bytes, rpfq_stream_t stream) {
+    if (!x || !xq) return fail(RPFQ_ERR_INVALID, "rpfq_vision_act_quant_sm100: null pointer");
+    if (images < 0 || tokens <= 0 || k <= 0 || k % 16)
+        return fail(RPFQ_ERR_INVALID, "rpfq_vision_act_quant_sm100: need images >= 0, tokens > 0, k a multiple of 16");
+    if (ldx < k || ldq < k || ldx % 8 || ldq % 8 || !aligned16(x) || !aligned16(xq))
+        return fail(RPFQ_ERR_INVALID, "rpfq_vision_act_quant_sm100: rows must be 16-byte aligned (strides % 8)");
+    if (!(salient_ratio >= 0.0 && salient_ratio <= 1.0))
+        return fail(RPFQ_ERR_INVALID, "salient_token_ratio must be in [0, 1].");
+    if (!(background_clip_ratio > 0.0)) return fail(RPFQ_ERR_INVALID, "background_clip_ratio must be > 0.");
+    if (!(energy_score_weight >= 0.0 && energy_score_weight <= 1.0))
+        return fail(RPFQ_ERR_INVALID, "energy_score_weight must be in [0, 1].");
+    if (images == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    VisionQuantParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.x = reinterpret_cast<const __half*>(x);
+    p.ldx = ldx;
+    p.y = reinterpret_cast<__half*>(xq);
+    p.ldy = ldq;
+    p.tokens = tokens;
+    p.k_c = k / 2;
+    p.protect_cls = protect_cls_token ? 1 : 0;
+    p.clip = static_cast<float>(background_clip_ratio);
+    p.w_energy = static_cast<float>(energy_score_weight);
+    p.w_contrast = static_cast<float>(1.0 - energy_score_weight);
+    p.mask_out = mask_out;
+    const int patches = tokens - 1;
+    int g = 0;
+    if (patches > 0) {
+        g = static_cast<int>(std::sqrt(static_cast<double>(patches)));
+        while (g * g > patches) --g;
+        while ((g + 1) * (g + 1) <= patches) ++g;
+        if (g * g != patches) g = 0;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (g == 0) {
+        p.grid = 0;
+        const int64_t rows = images * tokens;
+        const int64_t ctas = std::min<int64_t>((rows + 15) / 16, 8 * st->sm_count);
+        vision_quant_tokenwise_kernel<<<static_cast<unsigned>(ctas), kVisionThreads, 0, s>>>(p, rows);
+        RPFQ_CUDA(cudaGetLastError());
+        return RPFQ_OK;
+    }
+    if (tokens > kVisionMaxTokens)
+        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_vision_act_quant_sm100: saliency grid of %d patches (max %d)", patches,
+                    kVisionMaxTokens - 1);
+    if (images > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_vision_act_quant_sm100: too many images");
+    p.grid = g;
+    // the reference: max(1, ceil(P * ratio)) capped at P, 0 when the ratio is 0 (Python floats)
+    p.num_salient = salient_ratio <= 0.0
+                        ? 0
+                        : static_cast<int>(std::min<double>(patches, std::max(1.0, std::ceil(patches * salient_ratio))));
+    if (!workspace || workspace_bytes < rpfq_vision_workspace_bytes(images, tokens) || !aligned16(workspace))
+        return fail(RPFQ_ERR_INVALID,
+                    "rpfq_vision_act_quant_sm100: a 16-byte aligned workspace of rpfq_vision_workspace_bytes() bytes "
+                    "is required for a saliency grid");
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr[kMaxDevices];
+    int dev = 0;
+    RPFQ_CUDA(cudaGetDevice(&dev));
+    const int max_smem = 2 * (kVisionMaxTokens - 1) * 4 + kVisionMaxTokens + 16;
+    std::call_once(once[dev], [dev, max_smem]() {
+        attr[dev] = cudaFuncSetAttribute(vision_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    });
+    RPFQ_CUDA(attr[dev]);
+    const int64_t rows = images * tokens;
+    VisionTokenStats* stats = static_cast<VisionTokenStats*>(workspace);
+    float2* scales = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + 16 * rows);
+    const int64_t stat_ctas = std::min<int64_t>((rows + 15) / 16, 16 * st->sm_count);
+    vision_stats_kernel<<<static_cast<unsigned>(stat_ctas), kVisionThreads, 0, s>>>(p, rows, stats);
+    RPFQ_CUDA(cudaGetLastError());
+    const int smem = 2 * patches * 4 + tokens;
+    vision_select_kernel<<<static_cast<unsigned>(images), kVisionThreads, smem, s>>>(p, stats, scales);
+    RPFQ_CUDA(cudaGetLastError());
+    vision_apply_kernel<<<static_cast<unsigned>(stat_ctas), kVisionThreads, 0, s>>>(p, rows, scales);
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }

@@ -48,7 +48,7 @@ class PackedPhaseLinear(nn.Module):
 
     def __init__(self, in_features: int, out_features: int, stages: int = 2, code_bits: int = 2,
                  enable_act_quant: bool = False, act_num_bits: int = 4, activation: str = "none",
-                 rounding: str = "rne", cache_dense: bool = True, device=None):
+                 rounding: str = "rne", cache_dense: bool = True, vision_quant: dict | None = None, device=None):
         super().__init__()
         if in_features % 2 or out_features % 2:
             raise ValueError("Complex-phase QAT requires even in/out features.")
@@ -59,6 +59,10 @@ class PackedPhaseLinear(nn.Module):
         self.activation = activation
         self.rounding = rounding
         self.cache_dense = cache_dense
+        # vision-aware activation quantizer (quant_rpfq_vit_vision.py:26-171) in
+        # place of ActivationQuantSTE: {salient_token_ratio, background_clip_ratio,
+        # energy_score_weight, protect_cls_token}
+        self.vision_quant = dict(vision_quant) if (vision_quant is not None and enable_act_quant) else None
         n_cp, k_cp = round_up(self.n_c, BLOCK_SIZE), round_up(self.k_c, BLOCK_SIZE)
         for tag in ("u", "w"):
             for s in range(stages):
@@ -139,6 +143,10 @@ class PackedPhaseLinear(nn.Module):
                                                            else torch.float16)
         x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
         act_bits = 0 if prequantized else self.act_bits
+        if self.vision_quant is not None and not prequantized:
+            # token saliency needs the [B, T, K] structure of the input
+            x16 = ops.vision_act_quant(x16, **self.vision_quant)
+            act_bits = 0
         rows = x.numel() // self.in_features if self.in_features else 0
         if not self.cache_dense and self._fused_decode_ok and rows <= ops.FUSED_DECODE_MAX_ROWS:
             return ops.wide_linear(x16, self.packed(), None, act_bits, self.activation, residual, out=out,
@@ -181,7 +189,8 @@ class PackedPhaseLinear(nn.Module):
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, stages={self.stages}, "
-                f"code_bits={self.code_bits}, act_bits={self.act_bits}, activation={self.activation}")
+                f"code_bits={self.code_bits}, act_bits={self.act_bits}, activation={self.activation}"
+                + (f", vision_quant={self.vision_quant}" if self.vision_quant else ""))
 
 
 class QATLinearComplexPhase(nn.Linear):
@@ -235,12 +244,50 @@ class QATLinearComplexPhase(nn.Linear):
             with torch.no_grad():
                 layer = pack_linear(self.weight, self.bias, self.stages)
             self._packed = PackedPhaseLinear.from_packed(layer, enable_act_quant=self.enable_act_quant,
-                                                         act_num_bits=self.act_num_bits)
+                                                         act_num_bits=self.act_num_bits,
+                                                         vision_quant=self._vision_quant())
             self._packed.prepack()
             self._cache_key = key
         return self._packed
+
+    def _vision_quant(self) -> dict | None:
+        return None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not x.is_cuda:
             raise RuntimeError("QATLinearComplexPhase (B200) runs on CUDA tensors only")
         return self.packed_module()(x)
+
+
+class VisionAwareQATLinearComplexPhase(QATLinearComplexPhase):
+    """Drop-in for the reference ``VisionAwareQATLinearComplexPhase``
+    (quant_rpfq_vit_vision.py:174-207): the complex-phase layer whose
+    activation quantizer is the token-saliency one
+    (``VisionAwareActivationQuantizer``, :26-171) — salient patch tokens (and
+    CLS) keep per-token int8 scales, the rest share a clipped per-image scale.
+    Inputs ``[B, 1 + g*g, K]`` get the saliency split, other shapes per-token
+    int8 scales, as in the reference. Same constructor; ``enable_rotation``
+    must be False (see :class:`QATLinearComplexPhase`)."""
+
+    def __init__(self, quant_method_u: str = "complex_phase_v1", quant_method_w: str = "complex_phase_v1",
+                 enable_act_quant: bool = True, act_num_bits: int = 4, enable_rotation: bool = False,
+                 quant_group_size: int = 32, salient_token_ratio: float = 0.25, background_clip_ratio: float = 0.75,
+                 energy_score_weight: float = 0.5, protect_cls_token: bool = True, *args, **kwargs):
+        super().__init__(quant_method_u, quant_method_w, enable_act_quant, act_num_bits, enable_rotation,
+                         quant_group_size, *args, **kwargs)
+        if not 0.0 <= salient_token_ratio <= 1.0:
+            raise ValueError("salient_token_ratio must be in [0, 1].")
+        if background_clip_ratio <= 0.0:
+            raise ValueError("background_clip_ratio must be > 0.")
+        if not 0.0 <= energy_score_weight <= 1.0:
+            raise ValueError("energy_score_weight must be in [0, 1].")
+        self.salient_token_ratio = salient_token_ratio
+        self.background_clip_ratio = background_clip_ratio
+        self.energy_score_weight = energy_score_weight
+        self.protect_cls_token = protect_cls_token
+
+    def _vision_quant(self) -> dict | None:
+        if not self.enable_act_quant:
+            return None
+        return dict(salient_token_ratio=self.salient_token_ratio, background_clip_ratio=self.background_clip_ratio,
+                    energy_score_weight=self.energy_score_weight, protect_cls_token=self.protect_cls_token)

@@ -12,6 +12,7 @@ a missing library raises — there is no fallback path.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -105,6 +106,40 @@ def prepack(layer: PackedLayer, rounding: str = "rne") -> torch.Tensor:
         _lib.check(_lib.lib().rpfq_prepack_sm100(ctypes.byref(s), out.data_ptr(), _ROUND[rounding], _stream(dev)),
                    "rpfq_prepack_sm100")
     return out
+
+
+def vision_act_quant(x: torch.Tensor, salient_token_ratio: float = 0.25, background_clip_ratio: float = 0.75,
+                     energy_score_weight: float = 0.5, protect_cls_token: bool = True,
+                     out: torch.Tensor | None = None, return_mask: bool = False):
+    """Vision-aware activation quantization (``VisionAwareActivationQuantizer``,
+    quant_rpfq_vit_vision.py:26-171) of fp16 ``x`` through
+    ``rpfq_vision_act_quant_sm100``. ``x`` is ``[B, T, K]`` (saliency over each
+    image's T tokens when T = 1 + g*g) or ``[M, K]`` (per-token int8 scales,
+    the reference's fallback for inputs that are not 3-D). ``out`` may be ``x``."""
+    _require(x, "x")
+    if x.dim() == 3:
+        images, tokens, K = x.shape
+    elif x.dim() == 2:
+        images, tokens, K = x.shape[0], 1, x.shape[1]
+    else:
+        raise ValueError(f"x must be [B, T, K] or [M, K], got {tuple(x.shape)}")
+    x2, ldx = _rows(x, K, "x")
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    y2, ldy = _rows(out, K, "out")
+    mask = torch.empty(x.shape[:-1], dtype=torch.uint8, device=x.device) if return_mask else None
+    L = _lib.lib()
+    ws_bytes = int(L.rpfq_vision_workspace_bytes(images, tokens))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    with torch.cuda.device(x.device):
+        _lib.check(L.rpfq_vision_act_quant_sm100(
+            x2.data_ptr(), ldx, y2.data_ptr(), ldy, images, tokens, K, float(salient_token_ratio),
+            float(background_clip_ratio), float(energy_score_weight), int(bool(protect_cls_token)), _p(mask),
+            _p(ws), ws_bytes, _stream(x.device)), "rpfq_vision_act_quant_sm100")
+    if images:
+        g = math.isqrt(tokens - 1) if tokens > 1 else 0
+        _count_launch(3 if g and g * g == tokens - 1 else 1)
+    return (out, mask.bool()) if return_mask else out
 
 
 def pack_linear(weight: torch.Tensor, bias: torch.Tensor | None = None, stages: int = 2) -> PackedLayer:

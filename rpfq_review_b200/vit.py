@@ -85,9 +85,15 @@ class PackedViT(nn.Module):
     """
 
     def __init__(self, cfg: ViTConfig, device, seed: int = 0, act_bits: int = 0, weights: str = "random_init",
-                 code_bits: int = 2, prepack: bool = True):
+                 code_bits: int = 2, prepack: bool = True, vision_quant: dict | None = None):
         super().__init__()
         self.cfg = cfg
+        # vision_quant: the reference's VisionAwareComplexVisionTransformer
+        # (quant_rpfq_vit_vision.py:210-301): every packed linear quantizes its
+        # input with the token-saliency quantizer (int8) instead of act_bits
+        self.vision_quant = dict(vision_quant) if vision_quant is not None else None
+        if self.vision_quant is not None:
+            act_bits = 0
         self.act_bits = act_bits
         dev = torch.device(device)
         d = cfg.dim
@@ -114,8 +120,9 @@ class PackedViT(nn.Module):
                 layer.planes = planes
             else:
                 raise ValueError(f"unknown weights mode {weights!r}")
-            return PackedPhaseLinear.from_packed(layer, enable_act_quant=act_bits > 0, act_num_bits=act_bits or 4,
-                                                 activation=activation)
+            return PackedPhaseLinear.from_packed(layer, enable_act_quant=act_bits > 0 or vision_quant is not None,
+                                                 act_num_bits=act_bits or 4, activation=activation,
+                                                 vision_quant=vision_quant)
 
         self.blocks = nn.ModuleList()
         for i in range(cfg.depth):
@@ -161,12 +168,15 @@ class PackedViT(nn.Module):
         The residual stream is kept in fp32: LayerNorm reads it and writes the
         fp16 GEMM input (with the activation quantization fused in when
         enabled); proj and fc2 add their output to it in place in the GEMM
-        epilogue. GEMM operands are fp16 with fp32 accumulation."""
+        epilogue. GEMM operands are fp16 with fp32 accumulation. With the
+        vision-aware quantizer each packed linear quantizes its own
+        ``[B, tokens, K]`` input (the saliency split needs the whole image)."""
         cfg = self.cfg
         B = images.shape[0]
         d, H = cfg.dim, cfg.heads
         hd = d // H
         ab = self.act_bits
+        pre = self.vision_quant is None  # LayerNorm applied the quantizer
         patches = self.patchify(images.to(torch.float16))
         emb = ops.gemm(patches, self.patch_w, self.patch_b, out_dtype=torch.float32)
         ntok = cfg.tokens - patches.shape[1]
@@ -175,14 +185,14 @@ class PackedViT(nn.Module):
         L = cfg.tokens
         for blk in self.blocks:
             h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab)
-            qkv = blk.qkv(h, prequantized=True).view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
+            qkv = blk.qkv(h, prequantized=pre).view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
             a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2])
             a = a.transpose(1, 2).reshape(B, L, d)
             blk.proj(a, residual=x, out=x)
             h = ops.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab)
-            blk.fc2(blk.fc1(h, prequantized=True), residual=x, out=x)
+            blk.fc2(blk.fc1(h, prequantized=pre), residual=x, out=x)
         cls = ops.layernorm(x[:, :ntok], self.norm_w, self.norm_b, cfg.eps, ab)
-        logits = self.head(cls[:, 0], out_dtype=torch.float32, prequantized=True)
+        logits = self.head(cls[:, 0], out_dtype=torch.float32, prequantized=pre)
         if self.head_dist is not None:
-            logits = (logits + self.head_dist(cls[:, 1], out_dtype=torch.float32, prequantized=True)) / 2
+            logits = (logits + self.head_dist(cls[:, 1], out_dtype=torch.float32, prequantized=pre)) / 2
         return logits

@@ -18,6 +18,14 @@ tests never need the reference at run time. Fixtures:
 * ``golden_refcpp.npz`` — the reference's C++ runtime built from its sources
   (oracle/_ref): ``wideLinearReference`` output and the fp16 coefficient
   planes of ``buildFusedWideLinearCache`` for a seeded synthetic packed layer.
+* ``golden_vision.npz`` — ``VisionAwareActivationQuantizer.forward``
+  (RPFQ-ViT-main/quant_models/quant_rpfq_vit_vision.py:26-171) on seeded
+  token batches: the saliency mask and the quantized Re / Im halves. The
+  module imports timm at its top, which this container lacks, so the class
+  definition (and ``EPS``) is taken out of the file with ``ast`` and executed
+  alone, unchanged.
+
+``--only NAME`` regenerates one fixture (exporter, actquant, qat, refcpp, vision).
 """
 
 from __future__ import annotations
@@ -37,7 +45,11 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default=None, choices=["exporter", "actquant", "qat", "refcpp", "vision"])
     args = ap.parse_args()
+    if args.only == "vision":
+        make_vision(args.ref)
+        return
     sys.path.insert(0, os.path.join(args.ref, "RPFQ-ViTApple", "scripts"))
     sys.path.insert(0, os.path.join(args.ref, "RPFQ-ViT-main", "quant_models"))
     sys.path.insert(0, REPO)
@@ -123,7 +135,63 @@ def main() -> None:
     for key, val in ref_lib.coefficient_planes(packed, n_c, k_c).items():
         rc[f"plane.{key}"] = val
     np.savez_compressed(os.path.join(HERE, "golden_refcpp.npz"), **rc)
+    make_vision(args.ref)
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+
+
+def _reference_vision_quantizer(ref: str):
+    """The reference's VisionAwareActivationQuantizer class, executed from its
+    own source without the module's timm imports."""
+    import ast
+    import math
+    path = os.path.join(ref, "RPFQ-ViT-main", "quant_models", "quant_rpfq_vit_vision.py")
+    tree = ast.parse(open(path).read(), path)
+    keep = [n for n in tree.body
+            if (isinstance(n, ast.ClassDef) and n.name == "VisionAwareActivationQuantizer")
+            or (isinstance(n, ast.Assign) and any(getattr(t, "id", None) == "EPS" for t in n.targets))]
+    ns = {"torch": torch, "nn": torch.nn, "math": math}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), path, "exec"), ns)
+    return ns["VisionAwareActivationQuantizer"]
+
+
+def make_vision(ref: str) -> None:
+    VAQ = _reference_vision_quantizer(ref)
+    # name: (batch, tokens, k_c, salient_ratio, clip_ratio, energy_weight, protect_cls, two_d)
+    cases = {
+        "vitb": (2, 197, 16, 0.25, 0.75, 0.5, True, False),
+        "nocls": (2, 197, 16, 0.1, 0.5, 0.3, False, False),
+        "all_salient": (1, 197, 16, 1.0, 0.75, 0.5, True, False),
+        "no_salient": (1, 197, 16, 0.0, 0.75, 0.5, True, False),
+        "grid4": (3, 17, 8, 0.25, 0.75, 1.0, True, False),
+        "zero_token": (1, 50, 24, 0.3, 0.9, 0.0, True, False),
+        "fallback_tokens": (2, 198, 16, 0.25, 0.75, 0.5, True, False),
+        "fallback_2d": (1, 40, 16, 0.25, 0.75, 0.5, True, True),
+    }
+    out: dict[str, np.ndarray] = {}
+    for i, (name, (b, t, k, ratio, clip, wgt, cls, two_d)) in enumerate(cases.items()):
+        g = torch.Generator().manual_seed(5000 + i)
+        # per-token magnitudes vary so that token scales and saliency differ
+        mag = torch.exp(torch.randn(b, t, 1, generator=g) * 0.7)
+        xr = (torch.randn(b, t, k, generator=g) * mag).half().float()
+        xi = (torch.randn(b, t, k, generator=g) * mag).half().float()
+        if name == "zero_token":
+            xr[:, 7] = 0.0
+            xi[:, 7] = 0.0
+        q = VAQ(salient_token_ratio=ratio, background_clip_ratio=clip, energy_score_weight=wgt,
+                protect_cls_token=cls)
+        if two_d:
+            xr, xi = xr.reshape(b * t, k), xi.reshape(b * t, k)
+        with torch.no_grad():
+            mask = q._build_saliency_mask(xr, xi)
+            qr, qi = q(xr, xi)
+        out[f"{name}.params"] = np.array([ratio, clip, wgt, float(cls)], np.float64)
+        out[f"{name}.x_real"] = xr.numpy().astype(np.float16)
+        out[f"{name}.x_imag"] = xi.numpy().astype(np.float16)
+        out[f"{name}.q_real"] = qr.numpy()
+        out[f"{name}.q_imag"] = qi.numpy()
+        out[f"{name}.mask"] = (np.ones(xr.shape[:-1], bool) if mask is None
+                               else mask.squeeze(-1).numpy()).astype(np.uint8)
+    np.savez_compressed(os.path.join(HERE, "golden_vision.npz"), **out)
 
 
 if __name__ == "__main__":

