@@ -161,18 +161,25 @@ def cpu_forward_factory(cfg, model, threads: int):
         else:
             dense = torch.from_numpy(pr.dense_weight_from_packed(np_layer, mod.n_c, mod.k_c))
             linears[name] = (dense, torch.from_numpy(np_layer["bias"].astype(np.float32)))
-    small = {k: getattr(model, k).float().cpu() for k in ("patch_w", "patch_b", "cls_tokens", "pos_embed",
-                                                          "norm_w", "norm_b")}
-    norms = [{n: getattr(b, n).detach().float().cpu() for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b")}
-             for b in model.blocks]
 
     def lin(name, t):
         shape = t.shape
         if kind == "reference":
-            y = linears[name].run(t.reshape(-1, shape[-1]).numpy(), threads)
+            y = linears[name].run(t.reshape(-1, shape[-1]).contiguous().numpy(), threads)
             return torch.from_numpy(y).reshape(*shape[:-1], -1)
         W, b = linears[name]
         return F.linear(t, W, b)
+
+    from rpfq_review_b200.swin import SwinConfig
+    if isinstance(cfg, SwinConfig):
+        from oracle import swin_ref
+        w_rest = swin_ref.extract_weights(model, torch.float32, linears=False)
+        return (lambda images: swin_ref.swin_forward(w_rest, cfg, images, lin=lin)), kind
+
+    small = {k: getattr(model, k).float().cpu() for k in ("patch_w", "patch_b", "cls_tokens", "pos_embed",
+                                                          "norm_w", "norm_b")}
+    norms = [{n: getattr(b, n).detach().float().cpu() for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b")}
+             for b in model.blocks]
 
     def forward(images):
         x = images.float()
@@ -216,6 +223,30 @@ def time_cpu(forward, images, steps: int, warmup: int, budget_s: float | None = 
 
 
 # ----------------------------------------------------------------------------- main arms
+def model_config(name: str):
+    from rpfq_review_b200.swin import SWIN_CONFIGS
+    from rpfq_review_b200.vit import CONFIGS
+    if name in CONFIGS:
+        return CONFIGS[name]
+    if name in SWIN_CONFIGS:
+        return SWIN_CONFIGS[name]
+    raise SystemExit(f"unknown --model {name!r}; choose from {sorted(CONFIGS) + sorted(SWIN_CONFIGS)}")
+
+
+def build_model(cfg, device, args, prepack: bool = True):
+    """The packed model of ``cfg`` with the seeded weights every arm shares."""
+    from rpfq_review_b200.swin import PackedSwin, SwinConfig
+    from rpfq_review_b200.vit import PackedViT
+    if isinstance(cfg, SwinConfig):
+        if args.weights != "random_init" or args.code_bits != 2 or args.vision_quant:
+            raise SystemExit("Swin runs random-init 2-bit weights with the standard activation path only")
+        return PackedSwin(cfg, device, seed=0, act_bits=args.act_bits, prepack=prepack)
+    vq = dict(salient_token_ratio=0.25, background_clip_ratio=0.75, energy_score_weight=0.5,
+              protect_cls_token=True) if args.vision_quant else None
+    return PackedViT(cfg, device, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits,
+                     prepack=prepack, vision_quant=vq)
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU implementation on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -223,12 +254,10 @@ def run_reference(args):
         return 0
     import torch
 
-    from rpfq_review_b200.vit import CONFIGS, PackedViT
-
-    cfg = CONFIGS[args.model]
+    cfg = model_config(args.model)
     threads = os.cpu_count() or 1
     # Same seeded weights as the GPU arm, packed on the CPU (no CUDA involved).
-    model = PackedViT(cfg, "cpu", seed=0, act_bits=args.act_bits, prepack=False)
+    model = build_model(cfg, "cpu", args, prepack=False)
     forward, kind = cpu_forward_factory(cfg, model, threads)
     g = torch.Generator().manual_seed(1234)
     images = torch.randn(args.cpu_sample, 3, cfg.img, cfg.img, generator=g).half()
@@ -258,7 +287,6 @@ def run_b200(args):
     import torch.distributed as dist
 
     from rpfq_review_b200 import ops
-    from rpfq_review_b200.vit import CONFIGS, PackedViT
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -271,12 +299,9 @@ def run_b200(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    cfg = CONFIGS[args.model]
+    cfg = model_config(args.model)
     B = args.batch
-    vq = dict(salient_token_ratio=0.25, background_clip_ratio=0.75, energy_score_weight=0.5,
-              protect_cls_token=True) if args.vision_quant else None
-    model = PackedViT(cfg, dev, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits,
-                      vision_quant=vq)
+    model = build_model(cfg, dev, args)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     images = torch.randn(B, 3, cfg.img, cfg.img, device=dev, generator=g).half()
     gathered = torch.empty((world * B, cfg.classes), dtype=torch.float32, device=dev) if world > 1 else None
@@ -505,18 +530,19 @@ def run_gemm(args):
     ys = [torch.randn(m, n, device=dev, generator=g).to(out_dtype) for _ in range(2)]
     from rpfq_review_b200 import ops
     packed = mod.packed()
+    bias32 = mod._bias_f32()  # what the layer hands the epilogue
     act = "gelu" if args.epilogue == "gelu" else "none"
 
     def step(i):
         res = ys[i & 1] if args.epilogue == "residual_f32" else None
         if args.fused_decode:
             ops.wide_linear(xs[i & 1], packs[i % copies], None, mod.act_bits, activation=act, residual=res,
-                            out=ys[i & 1])
+                            out=ys[i & 1], bias=bias32)
         elif args.block_n or args.cta_pair or args.epilogue != "none":
-            ops.gemm(xs[i & 1], mod.dense, mod.bias, residual=res, activation=act, block_n=args.block_n,
+            ops.gemm(xs[i & 1], mod.dense, bias32, residual=res, activation=act, block_n=args.block_n,
                      out=ys[i & 1], cta_pair=args.cta_pair)
         else:
-            ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1])
+            ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1], bias=bias32)
 
     for i in range(args.warmup):
         step(i)

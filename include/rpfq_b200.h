@@ -50,7 +50,10 @@ enum {
 };
 
 enum { RPFQ_ACT_NONE = 0, RPFQ_ACT_GELU = 1 };               /* epilogue activation */
-enum { RPFQ_GEMM_OUT_F32 = 1, RPFQ_GEMM_RESIDUAL_F32 = 2 };  /* RpfqGemmArgs.flags */
+/* RpfqGemmArgs.flags / RpfqWideLinearArgs.flags: fp32 output, fp32 residual,
+ * fp32 bias (the same bias values widened once by the caller: the epilogue
+ * then adds them without a conversion per element). */
+enum { RPFQ_GEMM_OUT_F32 = 1, RPFQ_GEMM_RESIDUAL_F32 = 2, RPFQ_GEMM_BIAS_F32 = 4 };
 enum { RPFQ_ROUND_NEAREST_EVEN = 0, RPFQ_ROUND_TIES_AWAY = 1 }; /* fp32 -> fp16 of K1 */
 
 /* One residual stage of U or W. Replaces PhaseLinearParams
@@ -94,7 +97,7 @@ typedef struct RpfqGemmArgs {
     const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements)                */
     int64_t ldx;
     const uint16_t* w;        /* fp16 [n, k], contiguous                                */
-    const uint16_t* bias;     /* fp16 [n] or NULL                                       */
+    const void* bias;         /* fp16 [n] (fp32 with RPFQ_GEMM_BIAS_F32) or NULL         */
     const void* residual;     /* [m, n] fp16 (fp32 with RPFQ_GEMM_RESIDUAL_F32) or NULL */
     int64_t ldr;
     void* y;                  /* [m, n] fp16 (fp32 with RPFQ_GEMM_OUT_F32), stride ldy  */
@@ -103,7 +106,7 @@ typedef struct RpfqGemmArgs {
     int32_t n, k;
     int32_t activation;       /* RPFQ_ACT_NONE or RPFQ_ACT_GELU (erf)                   */
     int32_t block_n;          /* 0 = automatic; else 128 or 256                         */
-    int32_t flags;            /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32             */
+    int32_t flags;            /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32 | RPFQ_GEMM_BIAS_F32 */
     int32_t cta_pair;         /* 0 = automatic; 1 = one CTA per tile; 2 = CTA pairs      */
 } RpfqGemmArgs;
 int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
@@ -115,7 +118,8 @@ int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
 int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t m, int32_t k,
                          int32_t num_bits, rpfq_stream_t stream);
 
-/* LayerNorm of an fp32 residual stream row (d = 384, 768 or 1024) into the
+/* LayerNorm of an fp32 residual stream row (d = 96, 192, 384, 768, 1024, 1536
+ * or 3072: the ViT / DeiT / Swin widths and Swin's patch-merging 4C) into the
  * fp16 input of the next packed GEMM; with act_bits > 0 the activation
  * quantization of that GEMM's complex input (ActivationQuantSTE,
  * RPFQ-ViT-main/quant_models/quant_i.py:442-455) is applied in the same pass.
@@ -139,7 +143,7 @@ typedef struct RpfqWideLinearArgs {
     const uint16_t* dense;         /* fp16 [2 n_c, 2 k_c] from rpfq_prepack_sm100, or NULL (m <= 256) */
     const uint16_t* x;             /* fp16 [m, 2 k_c], row stride ldx */
     int64_t ldx;
-    const uint16_t* bias;          /* fp16 [2 n_c] or NULL */
+    const void* bias;              /* fp16 [2 n_c] (fp32 with RPFQ_GEMM_BIAS_F32) or NULL */
     const void* residual;          /* [m, 2 n_c] or NULL, row stride ldr (fp32 with RPFQ_GEMM_RESIDUAL_F32) */
     int64_t ldr;
     void* y;                       /* [m, 2 n_c], row stride ldy (fp32 with RPFQ_GEMM_OUT_F32) */

@@ -24,6 +24,7 @@ ACT_NONE = 0
 ACT_GELU = 1
 GEMM_OUT_F32 = 1
 GEMM_RESIDUAL_F32 = 2
+GEMM_BIAS_F32 = 4
 ROUND_NEAREST_EVEN = 0
 ROUND_TIES_AWAY = 1
 

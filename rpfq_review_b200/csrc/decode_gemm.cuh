@@ -32,7 +32,8 @@ struct DecodeGemmParams {
     int32_t stages;
     int32_t n_c, k_c, n_cp, k_cp;
     int32_t rows_per_item;  // RB (16, 32 or 64)
-    const __half* bias;     // [2 n_c] or nullptr
+    const void* bias;       // [2 n_c] fp16 (fp32 with bias_f32) or nullptr
+    int32_t bias_f32;
     const void* residual;   // [m, 2 n_c] (y's dtype) or nullptr
     int64_t ldr;
     void* y;                // [m, 2 n_c]
@@ -359,8 +360,14 @@ __global__ void __launch_bounds__(320, 1)
                     float v[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[j0 + e]);
-                    if (p.bias != nullptr) {
-                        const uint4 bv = *reinterpret_cast<const uint4*>(p.bias + col0 + j0);
+                    if (p.bias != nullptr && p.bias_f32) {
+                        const float* bf = static_cast<const float*>(p.bias) + col0 + j0;
+                        const float4 b0 = *reinterpret_cast<const float4*>(bf);
+                        const float4 b1 = *reinterpret_cast<const float4*>(bf + 4);
+                        v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+                        v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+                    } else if (p.bias != nullptr) {
+                        const uint4 bv = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p.bias) + col0 + j0);
                         const __half2* bh = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {

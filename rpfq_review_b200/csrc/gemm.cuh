@@ -38,12 +38,13 @@ namespace rpfq {
 enum : int { kActNone = 0, kActGelu = 1 };
 
 struct GemmParams {
-    const __half* bias;      // [N] or nullptr
+    const void* bias;        // [N] fp16 (fp32 with bias_f32) or nullptr
     const void* residual;    // [M, N], same dtype as y (row stride ldr), or nullptr
     int64_t ldr;
     int64_t m;
     int32_t n, k;
     int32_t activation;
+    int32_t bias_f32;        // bias holds fp32 values (no per-element conversion in the epilogue)
     int* err;                // device error word
 };
 
@@ -389,11 +390,24 @@ __global__ void __launch_bounds__(384, 1)
                 float v[CW];
 #pragma unroll
                 for (int jj = 0; jj < CW; ++jj) v[jj] = __uint_as_float(r[jj]);
-                if (p.bias != nullptr) {
+                if (p.bias != nullptr && p.bias_f32) {
+                    // every lane reads the same 16 B: one broadcast transaction per load
+#pragma unroll
+                    for (int g = 0; g < CW / 4; ++g) {
+                        if (col0 + 4 * g < p.n) {
+                            const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias) + (col0 >> 2) + g);
+                            v[4 * g + 0] += b4.x;
+                            v[4 * g + 1] += b4.y;
+                            v[4 * g + 2] += b4.z;
+                            v[4 * g + 3] += b4.w;
+                        }
+                    }
+                } else if (p.bias != nullptr) {
 #pragma unroll
                     for (int g = 0; g < CW / 8; ++g) {
                         if (col0 + 8 * g < p.n) {
-                            const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + col0 + 8 * g));
+                            const uint4 bv =
+                                __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(p.bias) + col0 + 8 * g));
                             const __half2* bh = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {

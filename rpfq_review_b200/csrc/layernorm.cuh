@@ -8,7 +8,7 @@
 //   act_bits > 0:  per Re / Im half of h: s = fl(fl(1 / max(amax, 1e-5)) * qmax),
 //                  h' = fl(clamp(rint(fl(h * s)), qmin, qmax) / s)
 //
-// Loads: float4 per lane, element e of lane l at 4 l + 128 j (+ 0..3).
+// Loads: VW = 4, 2 or 1 consecutive floats per lane and step (by row length).
 #pragma once
 
 #include "ptx.cuh"
@@ -28,23 +28,37 @@ struct LayerNormParams {
 
 template <int D>
 __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormParams p) {
-    static_assert(D % 128 == 0, "row length must be a multiple of 128");
-    constexpr int J = D / 128;  // float4 per lane
+    static_assert(D % 32 == 0, "row length must be a multiple of 32");
+    // VW consecutive floats per lane and step: element e of step j of lane l
+    // sits at column 32 VW j + VW l + e (coalesced, 16-/8-/4-byte loads)
+    constexpr int VW = D % 128 == 0 ? 4 : (D % 64 == 0 ? 2 : 1);
+    constexpr int J = D / (32 * VW);
     const int warps = blockDim.x >> 5;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= p.m) return;
     const float* xr = p.x + row * p.ldx;
-    float v[J][4];
+    float v[J][VW];
     float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-        const float4 t = *reinterpret_cast<const float4*>(xr + 128 * j + 4 * lane);
-        v[j][0] = t.x;
-        v[j][1] = t.y;
-        v[j][2] = t.z;
-        v[j][3] = t.w;
-        sum += (t.x + t.y) + (t.z + t.w);
+        const int col = 32 * VW * j + VW * lane;
+        if constexpr (VW == 4) {
+            const float4 t = *reinterpret_cast<const float4*>(xr + col);
+            v[j][0] = t.x;
+            v[j][1] = t.y;
+            v[j][2] = t.z;
+            v[j][3] = t.w;
+            sum += (t.x + t.y) + (t.z + t.w);
+        } else if constexpr (VW == 2) {
+            const float2 t = *reinterpret_cast<const float2*>(xr + col);
+            v[j][0] = t.x;
+            v[j][1] = t.y;
+            sum += t.x + t.y;
+        } else {
+            v[j][0] = xr[col];
+            sum += v[j][0];
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -53,7 +67,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < VW; ++e) {
             const float dlt = v[j][e] - mean;
             sq += dlt * dlt;
         }
@@ -63,17 +77,26 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     float amax_re = 0.0f, amax_im = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-        const int col = 128 * j + 4 * lane;
-        const uint2 wv = *reinterpret_cast<const uint2*>(p.w + col);
-        const uint2 bv = *reinterpret_cast<const uint2*>(p.b + col);
-        const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-        const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
-        const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bv.x));
-        const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bv.y));
-        const float wf[4] = {w01.x, w01.y, w23.x, w23.y};
-        const float bf[4] = {b01.x, b01.y, b23.x, b23.y};
+        const int col = 32 * VW * j + VW * lane;
+        float wf[VW], bf[VW];
+        if constexpr (VW == 4) {
+            const uint2 wv = *reinterpret_cast<const uint2*>(p.w + col);
+            const uint2 bv = *reinterpret_cast<const uint2*>(p.b + col);
+            const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+            const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+            const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bv.x));
+            const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bv.y));
+            wf[0] = w01.x; wf[1] = w01.y; wf[2] = w23.x; wf[3] = w23.y;
+            bf[0] = b01.x; bf[1] = b01.y; bf[2] = b23.x; bf[3] = b23.y;
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+            for (int e = 0; e < VW; ++e) {
+                wf[e] = __half2float(p.w[col + e]);
+                bf[e] = __half2float(p.b[col + e]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
             v[j][e] = (v[j][e] - mean) * rstd * wf[e] + bf[e];
             const float a = fabsf(v[j][e]);
             if (col + e < D / 2)
@@ -98,10 +121,10 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     __half* yr = p.y + row * p.ldy;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-        const int col = 128 * j + 4 * lane;
-        float o[4];
+        const int col = 32 * VW * j + VW * lane;
+        float o[VW];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < VW; ++e) {
             o[e] = v[j][e];
             if (p.act_bits > 0) {
                 const float s = (col + e < D / 2) ? s_re : s_im;
@@ -110,12 +133,18 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
                 o[e] = __fdiv_rn(q, s);
             }
         }
-        __half2 h01 = __floats2half2_rn(o[0], o[1]);
-        __half2 h23 = __floats2half2_rn(o[2], o[3]);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&h01);
-        pk.y = *reinterpret_cast<uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(yr + col) = pk;
+        if constexpr (VW == 4) {
+            __half2 h01 = __floats2half2_rn(o[0], o[1]);
+            __half2 h23 = __floats2half2_rn(o[2], o[3]);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&h01);
+            pk.y = *reinterpret_cast<uint32_t*>(&h23);
+            *reinterpret_cast<uint2*>(yr + col) = pk;
+        } else if constexpr (VW == 2) {
+            *reinterpret_cast<__half2*>(yr + col) = __floats2half2_rn(o[0], o[1]);
+        } else {
+            yr[col] = __float2half_rn(o[0]);
+        }
     }
 }
 

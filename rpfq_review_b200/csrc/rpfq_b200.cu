@@ -218,7 +218,8 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     if (rc) return rc;
     if (RES == 0) tr = ty;
     GemmParams p;
-    p.bias = reinterpret_cast<const __half*>(a->bias);
+    p.bias = a->bias;
+    p.bias_f32 = (a->flags & RPFQ_GEMM_BIAS_F32) ? 1 : 0;
     p.residual = a->residual;
     p.ldr = a->ldr;
     p.m = a->m;
@@ -323,7 +324,8 @@ int launch_decode(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx,
     p.n_cp = L->n_cp;
     p.k_cp = L->k_cp;
     p.rows_per_item = RB;
-    p.bias = reinterpret_cast<const __half*>(a->bias);
+    p.bias = a->bias;
+    p.bias_f32 = (a->flags & RPFQ_GEMM_BIAS_F32) ? 1 : 0;
     p.residual = a->residual;
     p.ldr = a->ldr;
     p.y = a->y;
@@ -405,7 +407,7 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     if (a->m < 0 || a->n <= 0 || a->k <= 0) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: bad shape m=%lld n=%d k=%d", (long long)a->m, a->n, a->k);
     if (a->k % 8 || a->n % 8)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: k (%d) and n (%d) must be multiples of 8", a->k, a->n);
-    if (a->flags & ~(RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32))
+    if (a->flags & ~(RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32 | RPFQ_GEMM_BIAS_F32))
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: unknown flags 0x%x", a->flags);
     if (a->ldx < a->k || a->ldx % 8 || a->ldy < a->n || a->ldy % 8)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: row strides must be >= the row length and multiples of 8");
@@ -572,8 +574,7 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
         return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: x must be 16-byte and y, weight, bias 8-byte aligned");
     if (act_bits != 0 && (act_bits < 2 || act_bits > 8))
         return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: act_bits must be 0 or 2..8 (got %d)", act_bits);
-    if (act_bits != 0 && (d / 2) % 4)
-        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: act-quant fusion needs d/2 %% 4 == 0");
+    if (d % 2) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: odd row length %d", d);
     if (m == 0) return RPFQ_OK;
     DeviceState* st;
     int rc = device_state(&st);
@@ -592,11 +593,18 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
     const int64_t blocks = (m + warps - 1) / warps;
     if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: m too large");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned nb = static_cast<unsigned>(blocks);
     switch (d) {
-        case 384: layernorm_f32_f16_kernel<384><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
-        case 768: layernorm_f32_f16_kernel<768><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
-        case 1024: layernorm_f32_f16_kernel<1024><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(p); break;
-        default: return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: row length %d (supported: 384, 768, 1024)", d);
+        case 96: layernorm_f32_f16_kernel<96><<<nb, warps * 32, 0, s>>>(p); break;
+        case 192: layernorm_f32_f16_kernel<192><<<nb, warps * 32, 0, s>>>(p); break;
+        case 384: layernorm_f32_f16_kernel<384><<<nb, warps * 32, 0, s>>>(p); break;
+        case 768: layernorm_f32_f16_kernel<768><<<nb, warps * 32, 0, s>>>(p); break;
+        case 1024: layernorm_f32_f16_kernel<1024><<<nb, warps * 32, 0, s>>>(p); break;
+        case 1536: layernorm_f32_f16_kernel<1536><<<nb, warps * 32, 0, s>>>(p); break;
+        case 3072: layernorm_f32_f16_kernel<3072><<<nb, warps * 32, 0, s>>>(p); break;
+        default:
+            return fail(RPFQ_ERR_UNSUPPORTED,
+                        "rpfq_layernorm_sm100: row length %d (supported: 96, 192, 384, 768, 1024, 1536, 3072)", d);
     }
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;

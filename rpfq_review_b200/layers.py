@@ -69,6 +69,7 @@ class PackedPhaseLinear(nn.Module):
                 self.add_module(f"{tag}_s{s}", PhasePlane(n_cp, k_cp, code_bits, device))
         self.register_buffer("bias", torch.zeros(out_features, dtype=torch.float16, device=device))
         self.register_buffer("dense", None, persistent=False)
+        self._bias32 = None  # (version, fp32 copy of bias) for the epilogue
 
     # -- construction ---------------------------------------------------------
     @classmethod
@@ -107,6 +108,14 @@ class PackedPhaseLinear(nn.Module):
     def _aligned(self) -> bool:
         # The TMA path needs 16-byte row strides: real K and N multiples of 8.
         return self.in_features % 8 == 0 and self.out_features % 8 == 0
+
+    def _bias_f32(self) -> torch.Tensor:
+        """The fp16 bias widened to fp32 once (exact); refreshed when the
+        bias tensor changes."""
+        key = (self.bias.data_ptr(), self.bias._version, self.bias.device)
+        if self._bias32 is None or self._bias32[0] != key:
+            self._bias32 = (key, self.bias.float())
+        return self._bias32[1]
 
     @property
     def _fused_decode_ok(self) -> bool:
@@ -150,7 +159,7 @@ class PackedPhaseLinear(nn.Module):
         rows = x.numel() // self.in_features if self.in_features else 0
         if not self.cache_dense and self._fused_decode_ok and rows <= ops.FUSED_DECODE_MAX_ROWS:
             return ops.wide_linear(x16, self.packed(), None, act_bits, self.activation, residual, out=out,
-                                   out_dtype=out_dtype)
+                                   out_dtype=out_dtype, bias=self._bias_f32())
         if self.cache_dense:
             if self.dense is None or self.dense.device != x.device:
                 self.prepack()
@@ -159,7 +168,7 @@ class PackedPhaseLinear(nn.Module):
             dense = self._decode_dense()
         if self._aligned:
             return ops.wide_linear(x16, self.packed(), dense, act_bits, self.activation, residual, out=out,
-                                   out_dtype=out_dtype)
+                                   out_dtype=out_dtype, bias=self._bias_f32())
         y = self._forward_padded(x16, dense, residual, act_bits, out_dtype)
         if out is not None:
             out.copy_(y)

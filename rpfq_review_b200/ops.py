@@ -179,8 +179,13 @@ def pack_linear(weight: torch.Tensor, bias: torch.Tensor | None = None, stages: 
     return PackedLayer(n_c, k_c, stages, 2, planes, b.to(device=dev, dtype=torch.float16).contiguous())
 
 
-def _flags(out: torch.Tensor, residual: torch.Tensor | None) -> int:
+def _flags(out: torch.Tensor, residual: torch.Tensor | None, bias: torch.Tensor | None = None) -> int:
     f = 0
+    if bias is not None:
+        if bias.dtype == torch.float32:
+            f |= _lib.GEMM_BIAS_F32
+        elif bias.dtype != torch.float16:
+            raise ValueError(f"bias must be float16 or float32, got {bias.dtype}")
     if out.dtype == torch.float32:
         f |= _lib.GEMM_OUT_F32
     elif out.dtype != torch.float16:
@@ -207,7 +212,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     x2, ldx = _rows(x, k, "x")
     m = x2.shape[0]
     if bias is not None:
-        _require(bias, "bias")
+        _require(bias, "bias", bias.dtype)
         bias = bias.contiguous()
     r2, ldr = (None, 0)
     if residual is not None:
@@ -223,7 +228,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
         raise ValueError("out must be a row-major view with unit column stride")
     a = _lib.RpfqGemmArgs(x=x2.data_ptr(), ldx=ldx, w=w.data_ptr(), bias=_p(bias), residual=_p(r2), ldr=ldr,
                           y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n,
-                          flags=_flags(out, r2), cta_pair=cta_pair)
+                          flags=_flags(out, r2, bias), cta_pair=cta_pair)
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:
@@ -279,7 +284,8 @@ def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -
 
 def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None, act_bits: int = 0,
                 activation="none", residual: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16,
+                bias: torch.Tensor | None = None) -> torch.Tensor:
     """Whole layer through ``rpfq_wide_linear_sm100``: optional activation
     quantization, then the GEMM over the prepacked coefficients with bias and
     epilogue. ``x`` is fp16 ``[..., 2 k_c]``; ``residual`` / ``out`` fp16 or
@@ -287,10 +293,15 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
 
     ``dense=None`` selects the fused decode path (at most ``FUSED_DECODE_MAX_ROWS``
     rows, 2-bit codes, ``n_c`` and ``k_c`` multiples of 8): the packed planes
-    are decoded inside the GEMM and no dense matrix exists anywhere."""
+    are decoded inside the GEMM and no dense matrix exists anywhere.
+
+    ``bias`` (optional) replaces ``layer.bias`` for this call, e.g. the same
+    values widened to fp32 once, which the epilogue adds without converting."""
     _require(x, "x")
     if dense is not None:
         _require(dense, "dense")
+    if bias is None:
+        bias = layer.bias
     K, N = 2 * layer.k_c, 2 * layer.n_c
     x2, ldx = _rows(x, K, "x")
     m = x2.shape[0]
@@ -307,9 +318,9 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
     scratch = torch.empty((m, K), dtype=torch.float16, device=x.device) if act_bits else None
     s = layer_struct(layer)
     a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=_p(dense), x=x2.data_ptr(), ldx=ldx,
-                                bias=_p(layer.bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
+                                bias=_p(bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
                                 act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch),
-                                flags=_flags(out, r2))
+                                flags=_flags(out, r2, bias))
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:

@@ -157,7 +157,7 @@ def test_gemm_fp32_output_and_residual(cuda, m, n, k, cta_pair):
     assert torch.equal(y2, y)
 
 
-@pytest.mark.parametrize("d", [384, 768, 1024])
+@pytest.mark.parametrize("d", [96, 192, 384, 768, 1024, 1536, 3072])
 @pytest.mark.parametrize("act_bits", [0, 4])
 def test_layernorm_kernel(cuda, d, act_bits):
     """fp32 -> fp16 LayerNorm vs torch (fp16 rounding), and the fused
@@ -291,3 +291,18 @@ def test_no_device_errors_recorded(cuda):
     from rpfq_review_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_gemm_fp32_bias_matches_fp16_bias(cuda, out_dtype):
+    """RPFQ_GEMM_BIAS_F32: the same bias values widened to fp32 give
+    bit-identical outputs (the epilogue adds in fp32 either way)."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(300, 256, generator=g).half().to(cuda)
+    w = (torch.randn(512, 256, generator=g) * 0.05).half().to(cuda)
+    b16 = (torch.randn(512, generator=g) * 0.1).half().to(cuda)
+    for act in ("none", "gelu"):
+        y16 = ops.gemm(x, w, b16, activation=act, out_dtype=out_dtype)
+        y32 = ops.gemm(x, w, b16.float(), activation=act, out_dtype=out_dtype)
+        assert torch.equal(y16, y32)

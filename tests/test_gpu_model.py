@@ -88,3 +88,18 @@ def test_vision_quant_model_runs_and_stays_close(cuda):
     assert torch.isfinite(b).all()
     rel = float((a - b).abs().max() / a.abs().max())
     assert rel < 5e-2, rel
+
+
+def test_swin_t_logits_vs_cpu_reference(cuda):
+    """Swin-T (configs[3] model) with every linear on the packed path against
+    the float32 CPU restatement with export-reconstructed dense weights."""
+    from oracle import swin_ref
+    from rpfq_review_b200.swin import SWIN_T, PackedSwin
+    model = PackedSwin(SWIN_T, cuda, seed=0)
+    images = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(9)).half()
+    logits = model(images.to(cuda)).cpu()
+    ref = swin_ref.swin_forward(swin_ref.extract_weights(model), SWIN_T, images.float())
+    err = rel_err(logits.numpy(), ref.numpy())
+    print(f"swin_t: logits max rel err {err:.3e}")
+    assert err < 1e-3
+    assert torch.equal(logits.argmax(-1), ref.argmax(-1))
