@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--model", default="vit_base_patch16_224")
     ap.add_argument("--batch", type=int, default=256, help="images per GPU")
     ap.add_argument("--act-bits", type=int, default=0)
+    ap.add_argument("--attention", default="sdpa", choices=["sdpa", "rpfq"],
+                    help="ViT / DeiT attention: PyTorch SDPA (cuDNN) or the library's tcgen05 kernel")
     ap.add_argument("--vision-quant", action="store_true",
                     help="every packed linear uses the vision-aware (token-saliency, int8) activation quantizer")
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -244,7 +246,7 @@ def build_model(cfg, device, args, prepack: bool = True):
     vq = dict(salient_token_ratio=0.25, background_clip_ratio=0.75, energy_score_weight=0.5,
               protect_cls_token=True) if args.vision_quant else None
     return PackedViT(cfg, device, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits,
-                     prepack=prepack, vision_quant=vq)
+                     prepack=prepack, vision_quant=vq, attention=args.attention)
 
 
 def run_reference(args):

@@ -157,6 +157,17 @@ typedef struct RpfqWideLinearArgs {
 } RpfqWideLinearArgs;
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
 
+/* Multi-head self-attention for short sequences: qkv is the qkv GEMM output
+ * [images * tokens, 3 * heads * 64] fp16 (row = token: q heads, k heads,
+ * v heads), out[images * tokens, ldo] receives softmax(q k^T / 8) v with the
+ * heads concatenated (the proj GEMM's input). tokens <= 256 (all keys in one
+ * tensor-core tile), head_dim = 64. Replaces the attention of the timm blocks
+ * the reference models wrap (RPFQ-ViT-main/quant_models/quant_rpfq_vit.py,
+ * quant_rpfq_deit.py; runtime restatement
+ * RPFQ-ViTApple/scripts/audit_rpfq_vit_ios_parity.py:612-614). */
+int rpfq_attention_sm100(const uint16_t* qkv, int64_t images, int32_t tokens, int32_t heads, int32_t head_dim,
+                         uint16_t* out, int64_t ldo, rpfq_stream_t stream);
+
 /* Vision-aware activation quantization of `images` x `tokens` rows of fp16
  * x[row] = [Re | Im] (k = 2 k_c columns, k_c a multiple of 8) into xq (may
  * alias x): the reference's VisionAwareActivationQuantizer.forward

@@ -19,6 +19,7 @@
 
 #include "../../include/rpfq_b200.h"
 #include "actquant.cuh"
+#include "attention.cuh"
 #include "decode_gemm.cuh"
 #include "gemm.cuh"
 #include "layernorm.cuh"
@@ -606,6 +607,60 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
             return fail(RPFQ_ERR_UNSUPPORTED,
                         "rpfq_layernorm_sm100: row length %d (supported: 96, 192, 384, 768, 1024, 1536, 3072)", d);
     }
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
+int rpfq_attention_sm100(const uint16_t* qkv, int64_t images, int32_t tokens, int32_t heads, int32_t head_dim,
+                         uint16_t* out, int64_t ldo, rpfq_stream_t stream) {
+    if (!qkv || !out) return fail(RPFQ_ERR_INVALID, "rpfq_attention_sm100: null pointer");
+    if (images < 0 || tokens <= 0 || heads <= 0)
+        return fail(RPFQ_ERR_INVALID, "rpfq_attention_sm100: bad shape (images %lld, tokens %d, heads %d)",
+                    (long long)images, tokens, heads);
+    if (head_dim != 64) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_attention_sm100: head_dim %d (only 64)", head_dim);
+    if (tokens > AttnCfg::LK)
+        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_attention_sm100: %d tokens (at most %d keys in one tile)", tokens,
+                    AttnCfg::LK);
+    const int64_t d = static_cast<int64_t>(heads) * head_dim;
+    if (ldo < d || ldo % 8 || !aligned16(qkv) || !aligned16(out))
+        return fail(RPFQ_ERR_INVALID, "rpfq_attention_sm100: 16-byte aligned rows required (ldo >= d, ldo %% 8 == 0)");
+    if (images * heads * 2 > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_attention_sm100: grid too large");
+    if (images == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr[kMaxDevices];
+    int dev = 0;
+    RPFQ_CUDA(cudaGetDevice(&dev));
+    std::call_once(once[dev], [dev]() {
+        attr[dev] = cudaFuncSetAttribute(attn_short_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnCfg::SMEM_BYTES);
+    });
+    RPFQ_CUDA(attr[dev]);
+    EncodeTiledFn fn;
+    rc = encode_fn(&fn);
+    if (rc) return rc;
+    CUtensorMap tm;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(3 * d), static_cast<cuuint64_t>(tokens),
+                          static_cast<cuuint64_t>(images)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(3 * d * 2), static_cast<cuuint64_t>(3 * d * 2 * tokens)};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t*>(qkv), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RPFQ_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for qkv", (int)r);
+    AttnParams p;
+    p.out = reinterpret_cast<__half*>(out);
+    p.ldo = ldo;
+    p.L = tokens;
+    p.heads = heads;
+    p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
+    p.err = st->err_word;
+    const int64_t qtiles = (tokens + 127) / 128;
+    attn_short_sm100_kernel<<<static_cast<unsigned>(images * heads * qtiles), AttnCfg::THREADS, AttnCfg::SMEM_BYTES,
+                              static_cast<cudaStream_t>(stream)>>>(tm, p);
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }

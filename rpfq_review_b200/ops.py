@@ -108,6 +108,31 @@ def prepack(layer: PackedLayer, rounding: str = "rne") -> torch.Tensor:
     return out
 
 
+ATTENTION_MAX_TOKENS = 256
+
+
+def attention(qkv: torch.Tensor, heads: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Self-attention of the qkv GEMM output ``[B, L, 3 d]`` (fp16, head dim
+    64, L <= 256) through ``rpfq_attention_sm100`` -> ``[B, L, d]`` fp16:
+    softmax(q k^T / 8) v per head, heads concatenated."""
+    _require(qkv, "qkv")
+    if qkv.dim() != 3 or qkv.shape[-1] != 3 * 64 * heads:
+        raise ValueError(f"qkv must be [B, L, 3 * heads * 64], got {tuple(qkv.shape)} for {heads} heads")
+    if not qkv.is_contiguous():
+        qkv = qkv.contiguous()
+    B, L, _ = qkv.shape
+    d = 64 * heads
+    if out is None:
+        out = torch.empty((B, L, d), dtype=torch.float16, device=qkv.device)
+    o2, ldo = _rows(out, d, "out")
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.lib().rpfq_attention_sm100(qkv.data_ptr(), B, L, heads, 64, o2.data_ptr(), ldo,
+                                                   _stream(qkv.device)), "rpfq_attention_sm100")
+    if B:
+        _count_launch(1)
+    return out
+
+
 def vision_act_quant(x: torch.Tensor, salient_token_ratio: float = 0.25, background_clip_ratio: float = 0.75,
                      energy_score_weight: float = 0.5, protect_cls_token: bool = True,
                      out: torch.Tensor | None = None, return_mask: bool = False):

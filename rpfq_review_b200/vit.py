@@ -14,8 +14,9 @@ LN -> qkv -> softmax attention -> proj (+ residual) -> LN -> fc1 -> exact GELU
 On the GPU: every quantized linear is one tcgen05 GEMM launch over the
 decoded coefficients with bias, GELU (fc1) and the residual add (proj, fc2)
 fused into its epilogue; the patch embedding (a dense conv in the reference)
-runs through the same GEMM on unfolded patches. LayerNorm and attention use
-PyTorch (SDPA); the hot path is the linears.
+runs through the same GEMM on unfolded patches. LayerNorm (+ activation
+quantization) is one kernel per row block; attention is PyTorch SDPA (cuDNN)
+or, with ``attention="rpfq"``, the library's tcgen05 short-sequence kernel.
 """
 
 from __future__ import annotations
@@ -85,9 +86,15 @@ class PackedViT(nn.Module):
     """
 
     def __init__(self, cfg: ViTConfig, device, seed: int = 0, act_bits: int = 0, weights: str = "random_init",
-                 code_bits: int = 2, prepack: bool = True, vision_quant: dict | None = None):
+                 code_bits: int = 2, prepack: bool = True, vision_quant: dict | None = None,
+                 attention: str = "sdpa"):
         super().__init__()
         self.cfg = cfg
+        if attention not in ("sdpa", "rpfq"):
+            raise ValueError(f"attention must be 'sdpa' or 'rpfq', got {attention!r}")
+        # "rpfq": the library's tcgen05 short-sequence attention kernel (head
+        # dim 64, <= 256 tokens); "sdpa": PyTorch scaled_dot_product_attention
+        self.attention = attention
         # vision_quant: the reference's VisionAwareComplexVisionTransformer
         # (quant_rpfq_vit_vision.py:210-301): every packed linear quantizes its
         # input with the token-saliency quantizer (int8) instead of act_bits
@@ -185,9 +192,12 @@ class PackedViT(nn.Module):
         L = cfg.tokens
         for blk in self.blocks:
             h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab)
-            qkv = blk.qkv(h, prequantized=pre).view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
-            a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2])
-            a = a.transpose(1, 2).reshape(B, L, d)
+            qkv = blk.qkv(h, prequantized=pre)
+            if self.attention == "rpfq" and hd == 64 and L <= ops.ATTENTION_MAX_TOKENS:
+                a = ops.attention(qkv.view(B, L, 3 * d), H)
+            else:
+                qkv = qkv.view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
+                a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2]).transpose(1, 2).reshape(B, L, d)
             blk.proj(a, residual=x, out=x)
             h = ops.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab)
             blk.fc2(blk.fc1(h, prequantized=pre), residual=x, out=x)

@@ -18,15 +18,16 @@ from tests.helpers import rel_err
 pytestmark = pytest.mark.gpu
 
 
-def _model(name, cuda, act_bits=0):
+def _model(name, cuda, act_bits=0, attention="sdpa"):
     from rpfq_review_b200.vit import CONFIGS, PackedViT
     cfg = CONFIGS[name]
-    return cfg, PackedViT(cfg, cuda, seed=0, act_bits=act_bits)
+    return cfg, PackedViT(cfg, cuda, seed=0, act_bits=act_bits, attention=attention)
 
 
+@pytest.mark.parametrize("attention", ["sdpa", "rpfq"])
 @pytest.mark.parametrize("name", ["vit_base_patch16_224", "deit_small_distilled_patch16_224"])
-def test_logits_vs_cpu_reference(cuda, name):
-    cfg, model = _model(name, cuda)
+def test_logits_vs_cpu_reference(cuda, name, attention):
+    cfg, model = _model(name, cuda, attention=attention)
     g = torch.Generator().manual_seed(7)
     images = torch.randn(3, 3, 224, 224, generator=g).half()
     logits = model(images.to(cuda)).cpu()
@@ -38,8 +39,9 @@ def test_logits_vs_cpu_reference(cuda, name):
     assert torch.equal(logits.argmax(-1), ref.argmax(-1))
 
 
-def test_top1_agreement_1024_images(cuda):
-    cfg, model = _model("vit_base_patch16_224", cuda)
+@pytest.mark.parametrize("attention", ["sdpa", "rpfq"])
+def test_top1_agreement_1024_images(cuda, attention):
+    cfg, model = _model("vit_base_patch16_224", cuda, attention=attention)
     w = {k: (tuple(t.to(cuda) for t in v) if isinstance(v, tuple) else v.to(cuda))
          for k, v in vit_ref.extract_weights(model, torch.float32).items()}
     prev = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
