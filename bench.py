@@ -68,6 +68,11 @@ def parse():
     ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
+    ap.add_argument("--attn", default=None,
+                    help="B,L,H: time the short-sequence attention kernel against PyTorch SDPA on one qkv tensor")
+    ap.add_argument("--pack", default=None,
+                    help="N,K: time the GPU packer (rpfq_pack_linear_sm100) on one float [N, K] weight, "
+                         "and the exporter algorithm on the host cores beside it")
     ap.add_argument("--fused-decode", action="store_true",
                     help="--gemm: the fused decode path (packed planes only, M <= 256), rotating over enough "
                          "layer copies that the packed weights stream from HBM")
@@ -587,6 +592,99 @@ def run_gemm(args):
     return 0
 
 
+def run_pack(args):
+    """--pack N,K: the exporter's packing of one float weight, on the GPU
+    (two kernels per residual stage, CUDA-event timed over --steps launches)
+    and with the same algorithm as torch ops on the host cores (the
+    reference exporter's setting, wall clock, one run)."""
+    import torch
+
+    from rpfq_review_b200 import ops
+    from rpfq_review_b200.packing import pack_linear_torch
+
+    n, k = (int(v) for v in args.pack.split(","))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(0)
+    w_cpu = torch.randn(n, k, generator=g) * 0.02
+    w = w_cpu.to(dev)
+    for _ in range(args.warmup):
+        ops.pack_linear(w, None, 2)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        layer = ops.pack_linear(w, None, 2)
+    e1.record()
+    torch.cuda.synchronize()
+    gpu_us = e0.elapsed_time(e1) * 1000 / args.steps
+    torch.set_num_threads(os.cpu_count() or 1)
+    t0 = time.perf_counter()
+    ref = pack_linear_torch(w_cpu, None, 2)
+    cpu_us = (time.perf_counter() - t0) * 1e6
+    same = all(torch.equal(a.cpu(), b) for key in layer.planes for a, b in zip(layer.planes[key], ref.planes[key]))
+    # algorithmic bytes: the weight read once per stage pass pair, the fp32
+    # residual planes written and read, the codes and gammas written
+    nk = (n // 2) * (k // 2)
+    alg = 4 * n * k * 2 + 16 * nk * 2 + 2 * 4 * (n // 2) * (((k // 2) + 255) // 256 * 256) // 4
+    print(json.dumps({"metric": "pack_linear us per layer", "shape": [n, k], "stages": 2, "gpu_us": gpu_us,
+                      "cpu_us": cpu_us, "cpu_threads": os.cpu_count(), "speedup": cpu_us / gpu_us,
+                      "bit_identical": same, "hbm_gbs_algorithmic": alg / gpu_us / 1e3}))
+    return 0
+
+
+def run_attn(args):
+    """--attn B,L,H: rpfq_attention_sm100 against torch SDPA (cuDNN) on the
+    same fp16 qkv [B, L, 3 * 64 H], each replayed from a CUDA graph."""
+    import torch
+    import torch.nn.functional as F
+
+    from rpfq_review_b200 import ops
+
+    B, L, H = (int(v) for v in args.attn.split(","))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    qkvs = [torch.randn(B, L, 3 * 64 * H, device=dev, generator=g).half() for _ in range(2)]
+    outs = [torch.empty(B, L, 64 * H, device=dev, dtype=torch.float16) for _ in range(2)]
+
+    def ours(i):
+        ops.attention(qkvs[i & 1], H, out=outs[i & 1])
+
+    def sdpa(i):
+        x = qkvs[i & 1].view(B, L, 3, H, 64).permute(2, 0, 3, 1, 4)
+        outs[i & 1].copy_(F.scaled_dot_product_attention(x[0], x[1], x[2]).transpose(1, 2).reshape(B, L, 64 * H))
+
+    res = {}
+    for name, fn in (("rpfq", ours), ("sdpa", sdpa)):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn(0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) * 1000 / args.steps
+    flops = 4 * B * H * L * L * 64
+    print(json.dumps({"metric": "attention us per launch", "shape": [B, L, H], "rpfq_us": res["rpfq"],
+                      "sdpa_us": res["sdpa"], "rpfq_tflops": flops / res["rpfq"] / 1e6,
+                      "sdpa_tflops": flops / res["sdpa"] / 1e6,
+                      "note": "sdpa includes the transpose copy into the [B, L, d] layout the proj GEMM reads"}))
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -599,6 +697,10 @@ def main():
         return 0
     if args.gemm:
         return run_gemm(args)
+    if args.attn:
+        return run_attn(args)
+    if args.pack:
+        return run_pack(args)
     return run_b200(args)
 
 

@@ -128,6 +128,15 @@ int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t l
 int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, const uint16_t* bias, uint16_t* y,
                          int64_t ldy, int64_t m, int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream);
 
+/* rpfq_layernorm_sm100 with a row gather: output row r is the normalized
+ * input row rows[r] (int32 [m], device memory; x has x_rows rows). Lets a
+ * token permutation (a Swin window partition with its cyclic shift) ride on
+ * the LayerNorm pass. An index outside [0, x_rows) leaves its output row
+ * untouched and records code 901 in the device error word. */
+int rpfq_layernorm_rows_sm100(const float* x, int64_t ldx, int64_t x_rows, const int32_t* rows,
+                              const uint16_t* weight, const uint16_t* bias, uint16_t* y, int64_t ldy, int64_t m,
+                              int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream);
+
 /* Whole layer — QATLinearComplexPhase.forward on packed weights
  * (RPFQ-ViT-main/quant_models/quant_i.py:513-554; Android wideLinear,
  * phase_linear.cpp:279-326): optional activation quantization, then the

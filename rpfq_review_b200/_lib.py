@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_gemm_sm100",
     "rpfq_act_quant_sm100",
     "rpfq_layernorm_sm100",
+    "rpfq_layernorm_rows_sm100",
     "rpfq_wide_linear_sm100",
     "rpfq_wide_linear_noalloc_sm100",
     "rpfq_attention_sm100",
@@ -116,6 +117,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_gemm_sm100.argtypes = [ctypes.POINTER(RpfqGemmArgs), P]
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
+        L.rpfq_layernorm_rows_sm100.argtypes = [P, I64, I64, P, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_wide_linear_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_wide_linear_noalloc_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_attention_sm100.argtypes = [P, I64, I32, I32, I32, P, I64, P]
@@ -130,6 +132,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_last_error.restype = ctypes.c_char_p
         L.rpfq_device_error.argtypes = [ctypes.POINTER(I32)]
         for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
+                     "rpfq_layernorm_rows_sm100",
                      "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_pack_linear_sm100",
                      "rpfq_vision_act_quant_sm100", "rpfq_attention_sm100",
                      "rpfq_device_error",

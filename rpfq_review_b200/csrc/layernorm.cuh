@@ -24,6 +24,9 @@ struct LayerNormParams {
     int64_t m;
     float eps;
     int32_t act_bits;
+    const int32_t* rows;  // optional gather: output row r normalizes input row rows[r]
+    int64_t x_rows;       // rows of x (gather indices outside [0, x_rows) are rejected)
+    int* err;
 };
 
 template <int D>
@@ -37,7 +40,15 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     const int64_t row = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= p.m) return;
-    const float* xr = p.x + row * p.ldx;
+    int64_t src = row;
+    if (p.rows != nullptr) {
+        src = p.rows[row];
+        if (src < 0 || src >= p.x_rows) {  // bad gather index: report, touch nothing
+            if ((threadIdx.x & 31) == 0) atomicCAS(p.err, 0, 901);
+            return;
+        }
+    }
+    const float* xr = p.x + src * p.ldx;
     float v[J][VW];
     float sum = 0.0f;
 #pragma unroll

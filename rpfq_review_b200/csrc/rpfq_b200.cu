@@ -567,6 +567,14 @@ int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t l
 
 int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, const uint16_t* bias, uint16_t* y,
                          int64_t ldy, int64_t m, int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream) {
+    return rpfq_layernorm_rows_sm100(x, ldx, m, nullptr, weight, bias, y, ldy, m, d, eps, act_bits, stream);
+}
+
+int rpfq_layernorm_rows_sm100(const float* x, int64_t ldx, int64_t x_rows, const int32_t* rows,
+                              const uint16_t* weight, const uint16_t* bias, uint16_t* y, int64_t ldy, int64_t m,
+                              int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream) {
+    if (rows != nullptr && ((reinterpret_cast<uintptr_t>(rows) & 3) || x_rows < 0))
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_rows_sm100: rows must be 4-byte aligned, x_rows >= 0");
     if (!x || !weight || !bias || !y) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: null pointer");
     if (m < 0 || ldx < d || ldy < d || ldx % 4 || ldy % 4)
         return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: bad shape or stride (strides must be multiples of 4)");
@@ -590,6 +598,9 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
     p.m = m;
     p.eps = eps;
     p.act_bits = act_bits;
+    p.rows = rows;
+    p.x_rows = x_rows;
+    p.err = st->err_word;
     const int warps = 8;
     const int64_t blocks = (m + warps - 1) / warps;
     if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: m too large");

@@ -270,9 +270,11 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
 
 
 def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, act_bits: int = 0,
-              out: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None, rows: torch.Tensor | None = None) -> torch.Tensor:
     """LayerNorm of an fp32 ``x[..., d]`` into fp16, with the activation
-    quantization of the next packed GEMM fused in when ``act_bits > 0``."""
+    quantization of the next packed GEMM fused in when ``act_bits > 0``.
+    ``rows`` (int32 CUDA tensor of the flattened row count) gathers: output
+    row r is the normalized input row ``rows[r]``."""
     if not x.is_cuda or x.dtype != torch.float32:
         raise ValueError("layernorm: x must be a float32 CUDA tensor")
     _require(weight, "weight")
@@ -282,11 +284,15 @@ def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: fl
     if out is None:
         out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
     y2, ldy = _rows(out, d, "out")
+    if rows is not None:
+        _require(rows, "rows", torch.int32)
+        if rows.numel() != y2.shape[0]:
+            raise ValueError("layernorm: rows must hold one index per output row")
     with torch.cuda.device(x.device):
-        _lib.check(_lib.lib().rpfq_layernorm_sm100(x2.data_ptr(), ldx, weight.data_ptr(), bias.data_ptr(),
-                                                   y2.data_ptr(), ldy, x2.shape[0], d, float(eps), int(act_bits),
-                                                   _stream(x.device)), "rpfq_layernorm_sm100")
-    if x2.shape[0]:
+        _lib.check(_lib.lib().rpfq_layernorm_rows_sm100(
+            x2.data_ptr(), ldx, x2.shape[0], _p(rows), weight.data_ptr(), bias.data_ptr(), y2.data_ptr(), ldy,
+            y2.shape[0], d, float(eps), int(act_bits), _stream(x.device)), "rpfq_layernorm_rows_sm100")
+    if y2.shape[0]:
         _count_launch()
     return out
 

@@ -15,9 +15,11 @@ tokens, head.
 
 On the GPU the packed linears run the tcgen05 GEMM with bias, GELU (fc1) and
 the residual add (fc2) fused; LayerNorm (+ activation quantization) is the
-``rpfq_layernorm_sm100`` kernel; window partition / shift are PyTorch views
-and copies, window attention is PyTorch SDPA with the relative-position bias
-(and shift mask) as an additive mask.
+``rpfq_layernorm_rows_sm100`` kernel, whose row gather also performs the
+cyclic shift and the window partition; the attention output returns to the
+residual stream through one ``index_add_`` scatter; window attention is
+PyTorch SDPA with the relative-position bias (and shift mask) as an additive
+mask.
 """
 
 from __future__ import annotations
@@ -112,6 +114,19 @@ def shift_mask(res: int, ws: int, shift: int) -> torch.Tensor:
     return torch.where(diff == 0, 0.0, -100.0)
 
 
+def window_order(res: int, ws: int, shift: int) -> torch.Tensor:
+    """[res*res] source token of each position of the window-partitioned
+    (cyclically shifted by -shift) layout: token t of window w comes from
+    image position ((wy ws + i + shift) mod res, (wx ws + j + shift) mod res).
+    The same permutation scatters the windows back (and undoes the shift)."""
+    nw = res // ws
+    wy, wx, i, j = torch.meshgrid(torch.arange(nw), torch.arange(nw), torch.arange(ws), torch.arange(ws),
+                                  indexing="ij")
+    y = (wy * ws + i + shift) % res
+    x = (wx * ws + j + shift) % res
+    return (y * res + x).reshape(-1)
+
+
 def window_partition(x: torch.Tensor, ws: int) -> torch.Tensor:
     """[B, R, R, C] -> [B * (R/ws)^2, ws*ws, C] (windows in row-major order)."""
     b, r, _, c = x.shape
@@ -181,6 +196,7 @@ class PackedSwin(nn.Module):
         self.register_buffer("norm_b", torch.zeros(dims[-1], dtype=torch.float16, device=dev))
         self.head = make("head.fc", cfg.classes, dims[-1])
         self._masks: dict = {}
+        self._orders: dict = {}
         if prepack:
             for m in self.modules():
                 if isinstance(m, PackedPhaseLinear):
@@ -217,6 +233,22 @@ class PackedSwin(nn.Module):
             self._masks[key] = m
         return m
 
+    def orders(self, s: int, shift: int, batch: int):
+        """(perm [R*R] int64, rows [B*R*R] int32) of stage s: the window order
+        of the tokens and its per-image row gather for the LayerNorm kernel."""
+        key = (s, shift, batch)
+        o = self._orders.get(key)
+        if o is None:
+            cfg = self.cfg
+            r = cfg.resolutions()[s]
+            ws, _ = cfg.stage_window(s)
+            dev = self.patch_w.device
+            perm = window_order(r, ws, shift).to(dev)
+            rows = (torch.arange(batch, device=dev)[:, None] * (r * r) + perm[None]).reshape(-1).to(torch.int32)
+            o = (perm, rows)
+            self._orders[key] = o
+        return o
+
     def patchify(self, images: torch.Tensor) -> torch.Tensor:
         b, c, h, w = images.shape
         p = self.cfg.patch
@@ -239,18 +271,16 @@ class PackedSwin(nn.Module):
             ws, shift = cfg.stage_window(s)
             for i, blk in enumerate(stage.blocks):
                 sh = shift if i % 2 == 1 else 0
-                h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab).view(B, r, r, c)
-                if sh:
-                    h = torch.roll(h, shifts=(-sh, -sh), dims=(1, 2))
-                win = window_partition(h, ws)  # [B nW, L, c]
+                perm, rows = self.orders(s, sh, B)
+                # LayerNorm writes the tokens already shifted and window-partitioned
+                win = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab, rows=rows).view(-1, ws * ws, c)
                 qkv = blk.qkv(win, prequantized=True)
                 qkv = qkv.view(win.shape[0], ws * ws, 3, nh, hd).permute(2, 0, 3, 1, 4)
                 a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=self.attn_mask(s, i, B))
                 a = a.transpose(1, 2).reshape(win.shape[0], ws * ws, c)
-                o = window_reverse(blk.proj(a, out_dtype=torch.float32), ws, r)
-                if sh:
-                    o = torch.roll(o, shifts=(sh, sh), dims=(1, 2))
-                x += o.reshape(B, r * r, c)
+                o = blk.proj(a, out_dtype=torch.float32)
+                # un-partition, un-shift and add to the residual stream in one scatter
+                x.index_add_(1, perm, o.view(B, r * r, c))
                 h = ops.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab)
                 blk.fc2(blk.fc1(h, prequantized=True), residual=x, out=x)
             if hasattr(stage, "reduction"):

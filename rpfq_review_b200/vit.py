@@ -187,8 +187,12 @@ class PackedViT(nn.Module):
         patches = self.patchify(images.to(torch.float16))
         emb = ops.gemm(patches, self.patch_w, self.patch_b, out_dtype=torch.float32)
         ntok = cfg.tokens - patches.shape[1]
-        x = torch.cat((self.cls_tokens.float().expand(B, -1, -1), emb), dim=1)
-        x += self.pos_embed.float()
+        # residual stream [cls (+ dist), patches] + position embedding, written in
+        # one pass over the patch embeddings
+        pos = self.pos_embed.float()
+        x = torch.empty((B, cfg.tokens, d), dtype=torch.float32, device=emb.device)
+        x[:, :ntok] = self.cls_tokens.float() + pos[:, :ntok]
+        torch.add(emb, pos[:, ntok:], out=x[:, ntok:])
         L = cfg.tokens
         for blk in self.blocks:
             h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab)

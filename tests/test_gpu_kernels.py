@@ -306,3 +306,29 @@ def test_gemm_fp32_bias_matches_fp16_bias(cuda, out_dtype):
         y16 = ops.gemm(x, w, b16, activation=act, out_dtype=out_dtype)
         y32 = ops.gemm(x, w, b16.float(), activation=act, out_dtype=out_dtype)
         assert torch.equal(y16, y32)
+
+
+def test_layernorm_row_gather(cuda):
+    """rpfq_layernorm_rows_sm100: output row r is LN(x[rows[r]]), bit-identical
+    to the ungathered kernel's row; an index outside x is reported through the
+    device error word (code 901) and its output row is left untouched."""
+    from rpfq_review_b200 import _lib
+    ops = _ops()
+    g = torch.Generator().manual_seed(5)
+    m, d = 3136, 96
+    x = torch.randn(m, d, generator=g).to(cuda)
+    w = (torch.randn(d, generator=g) * 0.2 + 1).half().to(cuda)
+    b = (torch.randn(d, generator=g) * 0.1).half().to(cuda)
+    perm = torch.randperm(m, generator=g).to(torch.int32).to(cuda)
+    full = ops.layernorm(x, w, b, 1e-5, act_bits=4)
+    gathered = ops.layernorm(x, w, b, 1e-5, act_bits=4, rows=perm)
+    assert torch.equal(gathered, full[perm.long()])
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    bad = perm.clone()
+    bad[10] = m + 5
+    out = torch.zeros(m, d, dtype=torch.float16, device=cuda)
+    ops.layernorm(x, w, b, 1e-5, rows=bad, out=out)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 901
+    assert torch.count_nonzero(out[10]) == 0

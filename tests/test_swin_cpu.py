@@ -54,3 +54,16 @@ def test_swin_reference_forward_runs_on_cpu():
     images = torch.randn(1, 3, 224, 224, generator=torch.Generator().manual_seed(0))
     logits = swin_ref.swin_forward(w, SWIN_T, images)
     assert logits.shape == (1, 1000) and torch.isfinite(logits).all()
+
+
+def test_window_order_equals_roll_then_partition():
+    from rpfq_review_b200.swin import window_order
+    for r, ws, sh in ((56, 7, 3), (14, 7, 0), (28, 7, 3), (7, 7, 0)):
+        x = torch.arange(r * r * 2, dtype=torch.float32).view(1, r, r, 2)
+        rolled = torch.roll(x, shifts=(-sh, -sh), dims=(1, 2)) if sh else x
+        want = window_partition(rolled, ws).reshape(-1, 2)
+        perm = window_order(r, ws, sh)
+        assert torch.equal(x.view(r * r, 2)[perm], want)
+        # scattering back through the same permutation undoes partition and shift
+        back = torch.zeros(r * r, 2).index_add_(0, perm, want)
+        assert torch.equal(back, x.view(r * r, 2))
