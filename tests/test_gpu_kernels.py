@@ -332,3 +332,23 @@ def test_layernorm_row_gather(cuda):
     torch.cuda.synchronize()
     assert _lib.device_error() == 901
     assert torch.count_nonzero(out[10]) == 0
+
+
+def test_gelu_epilogue_accuracy(cuda):
+    """The epilogue's GELU (A&S 7.1.26 erf, |error| <= 1.5e-7, with the SFU
+    reciprocal and exp2) against float64 exact-erf GELU, read through an
+    identity GEMM with fp32 output: |err| <= 5e-7 * max(1, |x|) for |x| <= 12,
+    and the far tails (x for large x, 0 for very negative x)."""
+    ops = _ops()
+    k = 64
+    vals = torch.cat([torch.linspace(-12, 12, 64 * 1000), torch.tensor([-40.0, -20.0, 20.0, 40.0, 0.0, -0.0])])
+    m = (vals.numel() + k - 1) // k
+    x = torch.zeros(m * k)
+    x[: vals.numel()] = vals
+    x = x.half().view(m, k)  # the GEMM operand is fp16: compare on the rounded values
+    eye = torch.eye(k, dtype=torch.float16)
+    y = ops.gemm(x.to(cuda), eye.to(cuda), None, activation="gelu", out_dtype=torch.float32).cpu().double()
+    ref = torch.nn.functional.gelu(x.double())
+    err = (y - ref).abs()
+    bound = 5e-7 * torch.clamp(x.double().abs(), min=1.0)
+    assert bool((err <= bound).all()), float((err / bound).max())
