@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const ActQuantParams p) 
     const int warps_per_block = blockDim.x >> 5;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_launch_dependents();
     if (row >= p.m) return;
     const __half* xr = p.x + row * p.ldx;
     __half* yr = p.y + row * p.ldy;

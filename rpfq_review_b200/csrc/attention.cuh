@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(192, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the predecessor's outputs (x, residual) are complete from here on
+    pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {

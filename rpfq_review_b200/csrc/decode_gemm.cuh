@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(320, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the predecessor's outputs (x, residual) are complete from here on
+    pdl_launch_dependents();
 
     auto stage_ptr = [&](int s) { return smem + s * C::STAGE_BYTES; };
 

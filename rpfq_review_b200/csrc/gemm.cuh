@@ -187,6 +187,8 @@ __global__ void __launch_bounds__(384, 1)
     if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the predecessor's outputs (x, residual) are complete from here on
+    pdl_launch_dependents();
 
     if (warp < 4) {
         setmaxnreg_dec40();

@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     const int warps = blockDim.x >> 5;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_launch_dependents();
     if (row >= p.m) return;
     int64_t src = row;
     if (p.rows != nullptr) {

@@ -89,6 +89,17 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
     }
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with the programmatic-stream-serialization attribute may
+// start while its predecessor in the stream is still running: pdl_wait()
+// blocks until that predecessor has completed and its writes are visible, so
+// every kernel calls it before its first global load or store. Its own
+// dependents may be scheduled once all its CTAs have called
+// pdl_launch_dependents() (they still wait for its completion). Both are
+// no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- clusters (CTA pairs)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

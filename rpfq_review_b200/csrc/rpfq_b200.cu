@@ -172,6 +172,46 @@ int make_tmap_f16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Programmatic dependent launch for the per-layer kernels (on unless the
+// environment sets RPFQ_PDL=0): a kernel's launch and prologue overlap the
+// tail of its predecessor in the stream; every such kernel calls pdl_wait()
+// before touching global memory.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("RPFQ_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          int cluster_x, Args... args) {
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster_x;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // x [m][2][k_c] view of the fp16 activations (Re half, Im half), box {64, 1, 128}, 128-B swizzle.
 int make_tmap_x_halves(CUtensorMap* m, const void* base, int64_t rows, int32_t k_c, int64_t ld) {
     EncodeTiledFn fn;
@@ -252,22 +292,12 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
             max_pairs[dev] = n > 0 ? n : 1;
         }
         const int pairs = static_cast<int>(tiles < max_pairs[dev] ? tiles : max_pairs[dev]);
-        cfg.gridDim = dim3(2 * pairs);
-        cfg.blockDim = dim3(C::THREADS);
-        cfg.dynamicSmemBytes = C::SMEM_BYTES;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        RPFQ_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, tx, tw, ty, tr, p));
+        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, dim3(2 * pairs), dim3(C::THREADS),
+                                C::SMEM_BYTES, stream, 2, tx, tw, ty, tr, p));
     } else {
         const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
-        gemm_f16_sm100_kernel<BN, OUT_F32, RES, false><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, tw, ty, tr, p);
-        RPFQ_CUDA(cudaGetLastError());
+        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(grid), dim3(C::THREADS),
+                                C::SMEM_BYTES, stream, 1, tx, tw, ty, tr, p));
     }
     return RPFQ_OK;
 }
@@ -337,8 +367,8 @@ int launch_decode(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx,
     p.err = st->err_word;
     const int items = (L->n_c + RB - 1) / RB;
     const int grid = items < st->sm_count ? items : st->sm_count;
-    decode_gemm_sm100_kernel<RB><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tx, cm, p);
-    RPFQ_CUDA(cudaGetLastError());
+    RPFQ_CUDA(launch_kernel(decode_gemm_sm100_kernel<RB>, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1, tx,
+                            cm, p));
     return RPFQ_OK;
 }
 
@@ -560,7 +590,8 @@ int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t l
     const int warps = 8;
     const int64_t blocks = (m + warps - 1) / warps;
     if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_act_quant_sm100: m too large");
-    act_quant_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    RPFQ_CUDA(launch_kernel(act_quant_kernel, dim3(static_cast<unsigned>(blocks)), dim3(warps * 32), 0,
+                            static_cast<cudaStream_t>(stream), 1, p));
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }
@@ -607,13 +638,13 @@ int rpfq_layernorm_rows_sm100(const float* x, int64_t ldx, int64_t x_rows, const
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned nb = static_cast<unsigned>(blocks);
     switch (d) {
-        case 96: layernorm_f32_f16_kernel<96><<<nb, warps * 32, 0, s>>>(p); break;
-        case 192: layernorm_f32_f16_kernel<192><<<nb, warps * 32, 0, s>>>(p); break;
-        case 384: layernorm_f32_f16_kernel<384><<<nb, warps * 32, 0, s>>>(p); break;
-        case 768: layernorm_f32_f16_kernel<768><<<nb, warps * 32, 0, s>>>(p); break;
-        case 1024: layernorm_f32_f16_kernel<1024><<<nb, warps * 32, 0, s>>>(p); break;
-        case 1536: layernorm_f32_f16_kernel<1536><<<nb, warps * 32, 0, s>>>(p); break;
-        case 3072: layernorm_f32_f16_kernel<3072><<<nb, warps * 32, 0, s>>>(p); break;
+        case 96: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<96>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+        case 192: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<192>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+        case 384: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<384>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+        case 768: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<768>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+        case 1024: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<1024>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+        case 1536: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<1536>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+        case 3072: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<3072>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
         default:
             return fail(RPFQ_ERR_UNSUPPORTED,
                         "rpfq_layernorm_sm100: row length %d (supported: 96, 192, 384, 768, 1024, 1536, 3072)", d);
@@ -670,8 +701,8 @@ int rpfq_attention_sm100(const uint16_t* qkv, int64_t images, int32_t tokens, in
     p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
     p.err = st->err_word;
     const int64_t qtiles = (tokens + 127) / 128;
-    attn_short_sm100_kernel<<<static_cast<unsigned>(images * heads * qtiles), AttnCfg::THREADS, AttnCfg::SMEM_BYTES,
-                              static_cast<cudaStream_t>(stream)>>>(tm, p);
+    RPFQ_CUDA(launch_kernel(attn_short_sm100_kernel, dim3(static_cast<unsigned>(images * heads * qtiles)),
+                            dim3(AttnCfg::THREADS), AttnCfg::SMEM_BYTES, static_cast<cudaStream_t>(stream), 1, tm, p));
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }
