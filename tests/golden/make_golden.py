@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference checkout is mounted (``--ref``,
-default ``/root/reference``); the fixtures it writes are committed, so the
-tests never need the reference at run time. Fixtures:
+Run where the reference checkout is available (``--ref``, default the
+``RPFQ_REFERENCE_ROOT`` environment variable, as for the build); the
+fixtures it writes are committed, so the tests never need the reference at
+run time. Fixtures:
 
 * ``golden_exporter.npz`` — the reference exporter
   (RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py): ``save_quantized_linear``
@@ -44,7 +45,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("RPFQ_REFERENCE_ROOT", "/root/reference"))
     ap.add_argument("--only", default=None, choices=["exporter", "actquant", "qat", "refcpp", "vision"])
     args = ap.parse_args()
     if args.only == "vision":
