@@ -41,14 +41,14 @@ struct AttnCfg {
     static constexpr int HD = 64;
     static constexpr int LK = 256;             // largest key tile
     static constexpr int TILE = 128 * HD * 2;  // one 128-row x 64 fp16 tile = 16 KB
-    // Q 16 KB | K 32 KB | spare 16 KB | V 32 KB. P (128 queries x 256 keys fp16
-    // = 64 KB) overwrites Q, K and the spare once S = Q K^T is complete.
+    // Q 16 KB | K 32 KB | V 32 KB. P stays in tensor memory: it overwrites the
+    // first lk / 2 columns of S as packed fp16 pairs, the A operand of O = P V.
     static constexpr int Q_OFF = 0;
     static constexpr int K_OFF = TILE;
-    static constexpr int P_OFF = 0;
-    static constexpr int V_OFF = 4 * TILE;
-    static constexpr int BAR_OFF = 6 * TILE;
-    static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 128;  // two CTAs per SM
+    static constexpr int V_OFF = 3 * TILE;
+    static constexpr int BAR_OFF = 5 * TILE;
+    static constexpr int O_COL = 128;  // O = P V lands in TMEM columns [128, 192)
+    static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 128;  // two CTAs per SM (80 KB each)
     static constexpr int THREADS = 192;
     static constexpr int TMEM_COLS = 256;
     static_assert(2 * SMEM_BYTES <= 232448, "two CTAs per SM");
@@ -142,10 +142,9 @@ __global__ void __launch_bounds__(192, 2)
                     tc_fence_after();
                     constexpr uint32_t idesc_o = umma_idesc_f16(128, C::HD) | (1u << 16);  // B (= V) MN-major
                     for (int kk = 0; kk < lk / 16; ++kk) {
-                        const uint64_t pdesc =
-                            umma_desc_sw128_kmajor(base + C::P_OFF + (kk >> 2) * C::TILE) + 2 * (kk & 3);
                         const uint64_t vdesc = umma_desc_sw128_mnmajor(base + C::V_OFF + kk * 2048);
-                        umma_f16(tmem_base, pdesc, vdesc, idesc_o, kk != 0);
+                        // A = P from TMEM: keys 16 kk .. 16 kk + 15 are columns 8 kk .. 8 kk + 7
+                        umma_f16_ts(tmem_base + C::O_COL, tmem_base + 8 * kk, vdesc, idesc_o, kk != 0);
                     }
                     umma_commit(o_full);
                 }
@@ -183,46 +182,39 @@ __global__ void __launch_bounds__(192, 2)
                 }
                 const float nmx = -mx * p.scale_log2;
                 const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), m2 = f2_pack(nmx, nmx);
-                // pass 2: p = 2^(s c - max c) (fp32x2 fma, ex2 on the SFU), fp16 P into the
-                // swizzled A tile; the row sum adds the fp16-rounded weights the MMA sees
+                // pass 2: p = 2^(s c - max c) (fp32x2 fma, ex2 on the SFU), packed as fp16
+                // pairs over the first columns of S (chunk c -> columns 16 c .. 16 c + 15, all
+                // of whose S values this thread has already read); the row sum adds the
+                // fp16-rounded weights the MMA sees
                 float sum = 0.0f;
-                uint8_t* prow = smem + C::P_OFF + row * 128;
                 for (int c = 0; c < nchunk; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + 32 * c, r);
                     tmem_ld_wait();
                     const bool full = 32 * c + 32 <= p.L;
-                    const int ngran = min(4, (lk - 32 * c) >> 3);  // 8-key granules the MMAs read
+                    uint32_t pw[16];
 #pragma unroll
-                    for (int gg = 0; gg < 4; ++gg) {
-                        if (gg >= ngran) break;
-                        uint32_t pw[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int e = 8 * gg + 2 * u;
-                            float a0, a1;
-                            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), c2, m2), a0,
-                                      a1);
-                            a0 = ex2_approx(a0);
-                            a1 = ex2_approx(a1);
-                            if (!full) {
-                                if (32 * c + e >= p.L) a0 = 0.0f;
-                                if (32 * c + e + 1 >= p.L) a1 = 0.0f;
-                            }
-                            const __half2 hh = __floats2half2_rn(a0, a1);
-                            const float2 f = __half22float2(hh);
-                            sum += f.x + f.y;
-                            pw[u] = *reinterpret_cast<const uint32_t*>(&hh);
+                    for (int u = 0; u < 16; ++u) {
+                        const int e = 2 * u;
+                        float a0, a1;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), c2, m2), a0, a1);
+                        a0 = ex2_approx(a0);
+                        a1 = ex2_approx(a1);
+                        if (!full) {
+                            if (32 * c + e >= p.L) a0 = 0.0f;
+                            if (32 * c + e + 1 >= p.L) a1 = 0.0f;
                         }
-                        const int gran = 4 * (c & 1) + gg;
-                        *reinterpret_cast<uint4*>(prow + (c >> 1) * C::TILE + ((gran ^ (row & 7)) << 4)) =
-                            make_uint4(pw[0], pw[1], pw[2], pw[3]);
+                        const __half2 hh = __floats2half2_rn(a0, a1);
+                        const float2 f = __half22float2(hh);
+                        sum += f.x + f.y;
+                        pw[u] = *reinterpret_cast<const uint32_t*>(&hh);
                     }
+                    tmem_st_32x32b_x16(t_row + 16 * c, pw);
                 }
+                tmem_st_wait();
                 inv_sum = 1.0f / sum;
             }
-            tc_fence_before();  // the S columns are about to be overwritten by O
-            fence_proxy_async_smem();
+            tc_fence_before();  // P is in TMEM; O will land next to it
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
             ok = wait_bar(o_full, 0, abort_flag, p.err, 806);
@@ -230,8 +222,8 @@ __global__ void __launch_bounds__(192, 2)
         if (ok && warp_live) {
             tc_fence_after();
             uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(t_row, r0);
-            tmem_ld_32x32b_x32(t_row + 32, r1);
+            tmem_ld_32x32b_x32(t_row + C::O_COL, r0);
+            tmem_ld_32x32b_x32(t_row + C::O_COL + 32, r1);
             tmem_ld_wait();
             if (l < p.L) {
                 __half* orow = p.out + (static_cast<int64_t>(b) * p.L + l) * p.ldo + h * C::HD;
