@@ -1,8 +1,6 @@
 // Short-sequence multi-head attention on tcgen05 for the ViT / DeiT token
-// counts (L <= 256 keys, head dim 64): softmax(Q K^T / sqrt(64)) V for one
-// (image, head, 128-query tile) per CTA, all keys in one tile, so no online
-// rescaling; two CTAs per SM overlap one's loads and MMAs with the other's
-// softmax.
+// counts (L <= 256 keys, head dim 64): softmax(Q K^T / sqrt(64)) V per
+// (image, head), all keys in one tile, so no online rescaling.
 //
 // Input: the qkv GEMM output [B, L, 3 d] (fp16; per token q heads, k heads, v
 // heads, 64 columns each), read through a 3-D tensor map [B][L][3 d] so that
@@ -11,16 +9,18 @@
 // reference models (RPFQ-ViT-main/quant_models/quant_rpfq_vit.py; runtime
 // restatement RPFQ-ViTApple/scripts/audit_rpfq_vit_ios_parity.py:612-614).
 //
-// Per CTA (6 warps), lk = L rounded up to 16:
-//   warp 0    TMA: the Q tile, K and V (one or two 128-row boxes each)
-//   warp 1    TMEM (256 columns) + MMA issue:
-//               S = Q K^T      M=128, N=lk, K=64   -> TMEM cols [0, lk)
-//               O = P V        M=128, N=64, K=lk   -> TMEM cols [0, 64)
-//             (V is the B operand in its natural [key][dim] layout: MN-major)
-//   warps 2-5 one query row per thread: row max over the valid keys,
-//             p = 2^((s - max) c) (SFU ex2), row sum of the fp16-rounded p,
-//             fp16 P into shared memory (128-B swizzled K-major A operand, over
-//             the dead Q / K tiles), then O / sum to global.
+// Persistent CTAs (10 warps, one per SM), lk = L rounded up to 16, query tile g:
+//   warp 0    TMA: Q (one or two 128-row tiles), K and V (one or two boxes
+//             each) into one of two shared-memory stages
+//   warp 1    TMEM (512 columns) + MMA issue:
+//               S_g = Q_g K^T   M=128, N=lk, K=64   -> TMEM cols [256 g, 256 g + lk)
+//               O_g = P_g V     M=128, N=64, K=lk   -> TMEM cols [256 g + 128, 256 g + 192)
+//             (P_g is the TMEM A operand; V the B operand in its natural
+//             [key][dim] layout: MN-major)
+//   warps 2-9 group g = query tile g, one query row per thread: row max over
+//             the valid keys, p = 2^((s - max) c) (SFU ex2), row sum of the
+//             fp16-rounded p, P as packed fp16 over the first lk/2 columns of
+//             S_g, then O_g / sum to global.
 // Every wait is bounded (wait_bar) and reports through the device error word.
 #pragma once
 
@@ -31,6 +31,7 @@ namespace rpfq {
 struct AttnParams {
     __half* out;       // [B * L, ldo]
     int64_t ldo;
+    int32_t images;
     int32_t L;         // tokens per image (<= 256)
     int32_t heads;     // d = 64 * heads
     float scale_log2;  // log2(e) / sqrt(head_dim)
@@ -41,17 +42,18 @@ struct AttnCfg {
     static constexpr int HD = 64;
     static constexpr int LK = 256;             // largest key tile
     static constexpr int TILE = 128 * HD * 2;  // one 128-row x 64 fp16 tile = 16 KB
-    // Q 16 KB | K 32 KB | V 32 KB. P stays in tensor memory: it overwrites the
-    // first lk / 2 columns of S as packed fp16 pairs, the A operand of O = P V.
+    // One stage per (image, head): Q0 | Q1 | K (2 tiles) | V (2 tiles) = 96 KB.
     static constexpr int Q_OFF = 0;
-    static constexpr int K_OFF = TILE;
-    static constexpr int V_OFF = 3 * TILE;
-    static constexpr int BAR_OFF = 5 * TILE;
-    static constexpr int O_COL = 128;  // O = P V lands in TMEM columns [128, 192)
-    static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 128;  // two CTAs per SM (80 KB each)
-    static constexpr int THREADS = 192;
-    static constexpr int TMEM_COLS = 256;
-    static_assert(2 * SMEM_BYTES <= 232448, "two CTAs per SM");
+    static constexpr int K_OFF = 2 * TILE;
+    static constexpr int V_OFF = 4 * TILE;
+    static constexpr int STAGE_BYTES = 6 * TILE;
+    static constexpr int STAGES = 2;
+    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+    static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 256;
+    static constexpr int THREADS = 320;
+    static constexpr int TMEM_COLS = 512;  // query tile g: S / P at 256 g, O at 256 g + 128
+    static constexpr int O_COL = 128;
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ uint64_t umma_desc_sw128_mnmajor(uint32_t smem_addr) {
@@ -67,35 +69,42 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mnmajor(uint32_t smem_addr) 
     return d;
 }
 
-// One (image, head, 128-query tile) per CTA; 6 warps: 0 TMA, 1 TMEM + MMA,
-// 2-5 softmax and output (one query row per thread).
-__global__ void __launch_bounds__(192, 2)
+// Persistent, one CTA per SM: CTA c takes (image, head) items c, c + grid, ...;
+// its k-th item uses shared-memory stage k % 2, so the next item's Q, K, V
+// load while the current one computes. Both 128-query tiles of an item share
+// one K / V load.
+__global__ void __launch_bounds__(320, 1)
     attn_short_sm100_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnParams p) {
     using C = AttnCfg;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-    uint64_t* load_bar = bars;  // Q, K, V landed
-    uint64_t* s_full = bars + 1;
-    uint64_t* p_full = bars + 2;  // 4 softmax warps
-    uint64_t* o_full = bars + 3;
-    uint64_t* drain = bars + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+    uint64_t* load_full = bars;        // [stage] Q, K, V landed
+    uint64_t* stage_free = bars + 2;   // [stage] the item's MMAs are done reading it
+    uint64_t* s_full = bars + 4;       // [tile] S in TMEM
+    uint64_t* p_full = bars + 6;       // [tile] P in TMEM (4 warps)
+    uint64_t* o_full = bars + 8;       // [tile] O in TMEM
+    uint64_t* tmem_free = bars + 10;   // [tile] O read out (4 warps)
+    uint64_t* drain = bars + 12;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qtiles = (p.L + 127) >> 7;
-    const int qt = blockIdx.x % qtiles;
-    const int bh = blockIdx.x / qtiles;
-    const int b = bh / p.heads, h = bh % p.heads;
+    const int items = p.images * p.heads;
     const int d = p.heads * C::HD;
     const int lk = (p.L + 15) & ~15;  // keys the MMAs cover (N of S, K of P V)
+    const int kboxes = (lk + 127) >> 7;
+    const int qtiles = (p.L + 127) >> 7;
 
     if (threadIdx.x == 0) {
-        mbar_init(load_bar, 1);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 4);
-        mbar_init(o_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&load_full[i], 1);
+            mbar_init(&stage_free[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&tmem_free[i], 4);
+        }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -109,84 +118,127 @@ __global__ void __launch_bounds__(192, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    pdl_wait();  // the predecessor's outputs (x, residual) are complete from here on
+    pdl_wait();  // the predecessor's outputs (qkv) are complete from here on
     pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
-            const int kboxes = (lk + 127) >> 7;
-            mbar_arrive_expect_tx(load_bar, (1 + 2 * kboxes) * C::TILE);
-            tma_load_3d(smem + C::Q_OFF, &tm_qkv, load_bar, h * C::HD, 128 * qt, b);
-            for (int t = 0; t < kboxes; ++t) {
-                tma_load_3d(smem + C::K_OFF + t * C::TILE, &tm_qkv, load_bar, d + h * C::HD, 128 * t, b);
-                tma_load_3d(smem + C::V_OFF + t * C::TILE, &tm_qkv, load_bar, 2 * d + h * C::HD, 128 * t, b);
+            // ------------------------------------------------------------ producer
+            int issued = 0;
+            for (int item = blockIdx.x, k = 0; item < items; item += gridDim.x, ++k) {
+                const int st = k & 1;
+                const uint32_t use = static_cast<uint32_t>(k >> 1);
+                if (use > 0 && !wait_bar(&stage_free[st], (use - 1) & 1, abort_flag, p.err, 811)) break;
+                const int b = item / p.heads, h = item % p.heads;
+                uint8_t* sm = smem + st * C::STAGE_BYTES;
+                mbar_arrive_expect_tx(&load_full[st], (qtiles + 2 * kboxes) * C::TILE);
+                for (int t = 0; t < qtiles; ++t)
+                    tma_load_3d(sm + C::Q_OFF + t * C::TILE, &tm_qkv, &load_full[st], h * C::HD, 128 * t, b);
+                for (int t = 0; t < kboxes; ++t) {
+                    tma_load_3d(sm + C::K_OFF + t * C::TILE, &tm_qkv, &load_full[st], d + h * C::HD, 128 * t, b);
+                    tma_load_3d(sm + C::V_OFF + t * C::TILE, &tm_qkv, &load_full[st], 2 * d + h * C::HD, 128 * t, b);
+                }
+                ++issued;
             }
-            volatile int no_abort = 0;
-            wait_bar(load_bar, 0, &no_abort, p.err, 801);
+            for (int k = issued - 1; k >= 0 && k >= issued - 2; --k) {
+                volatile int no_abort = 0;
+                wait_bar(&load_full[k & 1], static_cast<uint32_t>(k >> 1) & 1, &no_abort, p.err, 812);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            bool ok = wait_bar(load_bar, 0, abort_flag, p.err, 802);
-            if (ok) {
-                tc_fence_after();
-                const uint32_t base = smem_u32(smem);
-                const uint32_t idesc_s = umma_idesc_f16(128, lk);
-                const uint64_t kdesc = umma_desc_sw128_kmajor(base + C::K_OFF);
-                const uint64_t qdesc = umma_desc_sw128_kmajor(base + C::Q_OFF);
-#pragma unroll
-                for (int kk = 0; kk < C::HD / 16; ++kk)
-                    umma_f16(tmem_base, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk != 0);
-                umma_commit(s_full);
-                ok = wait_bar(p_full, 0, abort_flag, p.err, 803);
-                if (ok) {
-                    tc_fence_after();
-                    constexpr uint32_t idesc_o = umma_idesc_f16(128, C::HD) | (1u << 16);  // B (= V) MN-major
-                    for (int kk = 0; kk < lk / 16; ++kk) {
-                        const uint64_t vdesc = umma_desc_sw128_mnmajor(base + C::V_OFF + kk * 2048);
-                        // A = P from TMEM: keys 16 kk .. 16 kk + 15 are columns 8 kk .. 8 kk + 7
-                        umma_f16_ts(tmem_base + C::O_COL, tmem_base + 8 * kk, vdesc, idesc_o, kk != 0);
+            // ------------------------------------------------------------ MMA issuer
+            const uint32_t base = smem_u32(smem);
+            const uint32_t idesc_s = umma_idesc_f16(128, lk);
+            constexpr uint32_t idesc_o = umma_idesc_f16(128, C::HD) | (1u << 16);  // B (= V) MN-major
+            bool ok = true;
+            for (int item = blockIdx.x, k = 0; item < items && ok; item += gridDim.x, ++k) {
+                const int st = k & 1;
+                const uint32_t sb = base + st * C::STAGE_BYTES;
+                if (!wait_bar(&load_full[st], static_cast<uint32_t>(k >> 1) & 1, abort_flag, p.err, 813)) break;
+                const uint64_t kdesc = umma_desc_sw128_kmajor(sb + C::K_OFF);
+                for (int g = 0; g < qtiles; ++g) {
+                    if (k > 0 && !wait_bar(&tmem_free[g], (k - 1) & 1, abort_flag, p.err, 814)) {
+                        ok = false;
+                        break;
                     }
-                    umma_commit(o_full);
+                    tc_fence_after();
+                    const uint64_t qdesc = umma_desc_sw128_kmajor(sb + C::Q_OFF + g * C::TILE);
+#pragma unroll
+                    for (int kk = 0; kk < C::HD / 16; ++kk)
+                        umma_f16(tmem_base + 256 * g, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk != 0);
+                    umma_commit(&s_full[g]);
                 }
+                for (int g = 0; g < qtiles && ok; ++g) {
+                    if (!wait_bar(&p_full[g], k & 1, abort_flag, p.err, 815)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int kk = 0; kk < lk / 16; ++kk) {
+                        const uint64_t vdesc = umma_desc_sw128_mnmajor(sb + C::V_OFF + kk * 2048);
+                        // A = P from TMEM: keys 16 kk .. 16 kk + 15 are columns 8 kk .. 8 kk + 7
+                        umma_f16_ts(tmem_base + 256 * g + C::O_COL, tmem_base + 256 * g + 8 * kk, vdesc, idesc_o,
+                                    kk != 0);
+                    }
+                    umma_commit(&o_full[g]);
+                }
+                if (ok) umma_commit(&stage_free[st]);
             }
             umma_commit(drain);
             volatile int no_abort = 0;
-            wait_bar(drain, 0, &no_abort, p.err, 804);
+            wait_bar(drain, 0, &no_abort, p.err, 816);
         }
     } else {
+        // ---------------------------------------------------------------- softmax + output
+        const int g = (warp - 2) >> 2;  // query tile of this warp group
         const int q = warp & 3;         // TMEM lane quarter
         const int row = 32 * q + lane;  // query row within the tile
-        const int l = 128 * qt + row;
-        const bool warp_live = 128 * qt + 32 * q < p.L;  // some row of this warp is a real query
-        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
         const int nchunk = (lk + 31) >> 5;
-        bool ok = wait_bar(s_full, 0, abort_flag, p.err, 805);
-        float inv_sum = 0.0f;
-        if (ok) {
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(256 * g);
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+        const bool group_live = g < qtiles;
+        const bool warp_live = 128 * g + 32 * q < p.L;  // some row of this warp is a real query
+        const int l = 128 * g + row;
+        for (int item = blockIdx.x, k = 0; item < items && group_live; item += gridDim.x, ++k) {
+            const int b = item / p.heads, h = item % p.heads;
+            if (!wait_bar(&s_full[g], k & 1, abort_flag, p.err, 817)) break;
             tc_fence_after();
+            float inv_sum = 0.0f;
             if (warp_live) {
-                // pass 1: row max over the valid keys
-                float mx = -INFINITY;
-                for (int c = 0; c < nchunk; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(t_row + 32 * c, r);
+                // pass 1: row max over the valid keys (two TMEM chunks per wait, eight
+                // independent running maxima)
+                float m8[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
+                for (int c0 = 0; c0 < nchunk; c0 += 2) {
+                    uint32_t r[2][32];
+                    tmem_ld_32x32b_x32(t_row + 32 * c0, r[0]);
+                    if (c0 + 1 < nchunk) tmem_ld_32x32b_x32(t_row + 32 * (c0 + 1), r[1]);
                     tmem_ld_wait();
-                    if (32 * c + 32 <= p.L) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
-                    } else {
+                    for (int j = 0; j < 2; ++j) {
+                        const int c = c0 + j;
+                        if (c >= nchunk) break;
+                        if (32 * c + 32 <= p.L) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (32 * c + e < p.L) mx = fmaxf(mx, __uint_as_float(r[e]));
+                            for (int e = 0; e < 32; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(r[j][e]));
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                if (32 * c + e < p.L) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(r[j][e]));
+                        }
                     }
                 }
+                const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
                 const float nmx = -mx * p.scale_log2;
-                const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), m2 = f2_pack(nmx, nmx);
+                const uint64_t m2 = f2_pack(nmx, nmx);
                 // pass 2: p = 2^(s c - max c) (fp32x2 fma, ex2 on the SFU), packed as fp16
                 // pairs over the first columns of S (chunk c -> columns 16 c .. 16 c + 15, all
                 // of whose S values this thread has already read); the row sum adds the
                 // fp16-rounded weights the MMA sees
-                float sum = 0.0f;
+                float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 for (int c = 0; c < nchunk; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + 32 * c, r);
@@ -206,40 +258,43 @@ __global__ void __launch_bounds__(192, 2)
                         }
                         const __half2 hh = __floats2half2_rn(a0, a1);
                         const float2 f = __half22float2(hh);
-                        sum += f.x + f.y;
+                        s4[u & 3] += f.x + f.y;
                         pw[u] = *reinterpret_cast<const uint32_t*>(&hh);
                     }
                     tmem_st_32x32b_x16(t_row + 16 * c, pw);
                 }
                 tmem_st_wait();
-                inv_sum = 1.0f / sum;
+                inv_sum = 1.0f / ((s4[0] + s4[1]) + (s4[2] + s4[3]));
             }
             tc_fence_before();  // P is in TMEM; O will land next to it
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            ok = wait_bar(o_full, 0, abort_flag, p.err, 806);
-        }
-        if (ok && warp_live) {
+            if (lane == 0) mbar_arrive(&p_full[g]);
+            if (!wait_bar(&o_full[g], k & 1, abort_flag, p.err, 818)) break;
             tc_fence_after();
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(t_row + C::O_COL, r0);
-            tmem_ld_32x32b_x32(t_row + C::O_COL + 32, r1);
-            tmem_ld_wait();
-            if (l < p.L) {
-                __half* orow = p.out + (static_cast<int64_t>(b) * p.L + l) * p.ldo + h * C::HD;
+            if (warp_live) {
+                uint32_t r0[32], r1[32];
+                tmem_ld_32x32b_x32(t_row + C::O_COL, r0);
+                tmem_ld_32x32b_x32(t_row + C::O_COL + 32, r1);
+                tmem_ld_wait();
+                if (l < p.L) {
+                    __half* orow = p.out + (static_cast<int64_t>(b) * p.L + l) * p.ldo + h * C::HD;
 #pragma unroll
-                for (int gg = 0; gg < 8; ++gg) {
-                    const uint32_t* rr = gg < 4 ? &r0[8 * gg] : &r1[8 * (gg - 4)];
-                    uint32_t pw[4];
+                    for (int gg = 0; gg < 8; ++gg) {
+                        const uint32_t* rr = gg < 4 ? &r0[8 * gg] : &r1[8 * (gg - 4)];
+                        uint32_t o4[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const __half2 hh = __floats2half2_rn(__uint_as_float(rr[2 * u]) * inv_sum,
-                                                             __uint_as_float(rr[2 * u + 1]) * inv_sum);
-                        pw[u] = *reinterpret_cast<const uint32_t*>(&hh);
+                        for (int u = 0; u < 4; ++u) {
+                            const __half2 hh = __floats2half2_rn(__uint_as_float(rr[2 * u]) * inv_sum,
+                                                                 __uint_as_float(rr[2 * u + 1]) * inv_sum);
+                            o4[u] = *reinterpret_cast<const uint32_t*>(&hh);
+                        }
+                        *reinterpret_cast<uint4*>(orow + 8 * gg) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
                     }
-                    *reinterpret_cast<uint4*>(orow + 8 * gg) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_free[g]);
         }
     }
     tc_fence_before();

@@ -700,10 +700,11 @@ int rpfq_attention_sm100(const uint16_t* qkv, int64_t images, int32_t tokens, in
     p.heads = heads;
     p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
     p.err = st->err_word;
-    const int64_t qtiles = (tokens + 127) / 128;
-    RPFQ_CUDA(launch_kernel(attn_short_sm100_kernel, dim3(static_cast<unsigned>(images * heads * qtiles)),
-                            dim3(AttnCfg::THREADS), AttnCfg::SMEM_BYTES, static_cast<cudaStream_t>(stream), 1, tm, p));
-    RPFQ_CUDA(cudaGetLastError());
+    p.images = static_cast<int32_t>(images);
+    const int64_t items = images * heads;
+    const int grid = static_cast<int>(std::min<int64_t>(items, st->sm_count));
+    RPFQ_CUDA(launch_kernel(attn_short_sm100_kernel, dim3(grid), dim3(AttnCfg::THREADS), AttnCfg::SMEM_BYTES,
+                            static_cast<cudaStream_t>(stream), 1, tm, p));
     return RPFQ_OK;
 }
 
