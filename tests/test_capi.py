@@ -90,3 +90,48 @@ def test_torch_ops_registered():
     # CUDA-only: a CPU call fails in the dispatcher instead of falling back
     with pytest.raises(Exception):
         torch.ops.rpfq.act_quant(torch.zeros(2, 8, dtype=torch.float16), 4)
+
+
+def test_pack_linear_validation():
+    """rpfq_pack_linear_sm100 / rpfq_pack_workspace_bytes reject bad shapes,
+    stage counts, strides and workspaces before any device work."""
+    L = _lib.lib()
+    assert L.rpfq_pack_workspace_bytes(0, 8) == 0
+    ws = L.rpfq_pack_workspace_bytes(48, 40)
+    assert ws >= 16 * 48 * 40
+    outs = (_lib.RpfqPhasePlaneOut * 2)()
+    for o in outs:
+        o.codes, o.gamma_real, o.gamma_imag = 64, 128, 256
+    args = dict(weight=16, ldw=80, n_c=48, k_c=40, stages=2, ws=4096, ws_bytes=ws)
+
+    def call(**kw):
+        a = {**args, **kw}
+        return L.rpfq_pack_linear_sm100(a["weight"], a["ldw"], a["n_c"], a["k_c"], a["stages"], outs, outs,
+                                        a["ws"], a["ws_bytes"], None)
+
+    assert call(weight=None) == _lib.RPFQ_ERR_INVALID
+    assert call(n_c=0) == _lib.RPFQ_ERR_INVALID
+    assert call(stages=5) == _lib.RPFQ_ERR_INVALID and b"stages" in L.rpfq_last_error()
+    assert call(ldw=60) == _lib.RPFQ_ERR_INVALID and b"ldw" in L.rpfq_last_error()
+    assert call(ws=4100) == _lib.RPFQ_ERR_INVALID  # not 16-byte aligned
+    assert call(ws_bytes=ws - 1) == _lib.RPFQ_ERR_INVALID and b"workspace" in L.rpfq_last_error()
+
+
+def test_vision_attention_layernorm_validation():
+    L = _lib.lib()
+    # vision-aware quantizer: the reference's ValueError messages
+    assert L.rpfq_vision_act_quant_sm100(16, 64, 16, 64, 2, 197, 64, 1.5, 0.75, 0.5, 1, None, None, 0,
+                                         None) == _lib.RPFQ_ERR_INVALID
+    assert b"salient_token_ratio must be in [0, 1]." in L.rpfq_last_error()
+    assert L.rpfq_vision_act_quant_sm100(16, 64, 16, 64, 2, 197, 64, 0.25, 0.0, 0.5, 1, None, None, 0,
+                                         None) == _lib.RPFQ_ERR_INVALID
+    assert L.rpfq_vision_act_quant_sm100(16, 64, 16, 64, 2, 197, 60, 0.25, 0.75, 0.5, 1, None, None, 0,
+                                         None) == _lib.RPFQ_ERR_INVALID  # k % 16
+    assert L.rpfq_vision_workspace_bytes(2, 197) == 24 * 2 * 197
+    # attention: head dim 64 and <= 256 tokens only
+    assert L.rpfq_attention_sm100(16, 2, 197, 12, 80, 32, 768, None) == _lib.RPFQ_ERR_UNSUPPORTED
+    assert L.rpfq_attention_sm100(16, 2, 300, 12, 64, 32, 768, None) == _lib.RPFQ_ERR_UNSUPPORTED
+    assert L.rpfq_attention_sm100(None, 2, 197, 12, 64, 32, 768, None) == _lib.RPFQ_ERR_INVALID
+    # LayerNorm gather: misaligned index array
+    assert L.rpfq_layernorm_rows_sm100(16, 96, 10, 18, 16, 16, 16, 96, 10, 96, ctypes.c_float(1e-5), 0,
+                                       None) == _lib.RPFQ_ERR_INVALID
