@@ -66,6 +66,7 @@ def parse():
     ap.add_argument("--gemm", default=None, help="M,N,K: time one packed layer instead of the model")
     ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
     ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
+    ap.add_argument("--no-bias", action="store_true", help="--gemm: run the epilogue without the bias add")
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
     ap.add_argument("--attn", default=None,
@@ -577,7 +578,7 @@ def run_gemm(args):
     ys = [torch.randn(m, n, device=dev, generator=g).to(out_dtype) for _ in range(2)]
     from rpfq_review_b200 import ops
     packed = mod.packed()
-    bias32 = mod._bias_f32()  # what the layer hands the epilogue
+    bias32 = None if args.no_bias else mod._bias_f32()  # what the layer hands the epilogue
     act = "gelu" if args.epilogue == "gelu" else "none"
 
     def step(i):
@@ -585,7 +586,7 @@ def run_gemm(args):
         if args.fused_decode:
             ops.wide_linear(xs[i & 1], packs[i % copies], None, mod.act_bits, activation=act, residual=res,
                             out=ys[i & 1], bias=bias32)
-        elif args.block_n or args.cta_pair or args.epilogue != "none":
+        elif args.block_n or args.cta_pair or args.epilogue != "none" or args.no_bias:
             ops.gemm(xs[i & 1], mod.dense, bias32, residual=res, activation=act, block_n=args.block_n,
                      out=ys[i & 1], cta_pair=args.cta_pair)
         else:

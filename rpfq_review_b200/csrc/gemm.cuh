@@ -384,6 +384,34 @@ __global__ void __launch_bounds__(384, 1)
                         load_residual(0, col0, row0);
                     }
                 }
+                // this step's bias words are requested before the TMEM wait, so the two
+                // latencies overlap (every lane reads the same 16 B: one broadcast each);
+                // only a step that crosses n needs per-word bounds
+                uint4 bq[CW / 4];
+                if (p.bias != nullptr) {
+                    const bool whole = col0 + CW <= p.n;
+                    if (p.bias_f32) {
+                        const uint4* bp = reinterpret_cast<const uint4*>(static_cast<const float*>(p.bias) + col0);
+                        if (whole) {
+#pragma unroll
+                            for (int g = 0; g < CW / 4; ++g) bq[g] = __ldg(bp + g);
+                        } else {
+#pragma unroll
+                            for (int g = 0; g < CW / 4; ++g)
+                                bq[g] = col0 + 4 * g < p.n ? __ldg(bp + g) : make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    } else {
+                        const uint4* bp = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.bias) + col0);
+                        if (whole) {
+#pragma unroll
+                            for (int g = 0; g < CW / 8; ++g) bq[g] = __ldg(bp + g);
+                        } else {
+#pragma unroll
+                            for (int g = 0; g < CW / 8; ++g)
+                                bq[g] = col0 + 8 * g < p.n ? __ldg(bp + g) : make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
+                }
                 uint32_t r[CW];
 #pragma unroll
                 for (int h = 0; h < CW / 32; ++h)
@@ -393,30 +421,22 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                 for (int jj = 0; jj < CW; ++jj) v[jj] = __uint_as_float(r[jj]);
                 if (p.bias != nullptr && p.bias_f32) {
-                    // every lane reads the same 16 B: one broadcast transaction per load
 #pragma unroll
                     for (int g = 0; g < CW / 4; ++g) {
-                        if (col0 + 4 * g < p.n) {
-                            const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias) + (col0 >> 2) + g);
-                            v[4 * g + 0] += b4.x;
-                            v[4 * g + 1] += b4.y;
-                            v[4 * g + 2] += b4.z;
-                            v[4 * g + 3] += b4.w;
-                        }
+                        v[4 * g + 0] += __uint_as_float(bq[g].x);
+                        v[4 * g + 1] += __uint_as_float(bq[g].y);
+                        v[4 * g + 2] += __uint_as_float(bq[g].z);
+                        v[4 * g + 3] += __uint_as_float(bq[g].w);
                     }
                 } else if (p.bias != nullptr) {
 #pragma unroll
                     for (int g = 0; g < CW / 8; ++g) {
-                        if (col0 + 8 * g < p.n) {
-                            const uint4 bv =
-                                __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(p.bias) + col0 + 8 * g));
-                            const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+                        const __half2* bh = reinterpret_cast<const __half2*>(&bq[g]);
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 f = __half22float2(bh[e]);
-                                v[8 * g + 2 * e] += f.x;
-                                v[8 * g + 2 * e + 1] += f.y;
-                            }
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __half22float2(bh[e]);
+                            v[8 * g + 2 * e] += f.x;
+                            v[8 * g + 2 * e + 1] += f.y;
                         }
                     }
                 }
