@@ -30,6 +30,7 @@ its line with ``"impl": "reference"``.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -101,12 +102,18 @@ class ClockSampler:
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,timestamp")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.window = None  # (t0, t1) wall-clock seconds of the timed region
+
+    def mark(self, t0: float, t1: float):
+        """Wall-clock bounds of the timed region (the sampler starts before the
+        warm-up so that it is producing samples by then)."""
+        self.window = (t0, t1)
 
     def start(self):
         try:
@@ -128,21 +135,31 @@ class ClockSampler:
         self.file.seek(0)
         rows = [ln.strip().split(", ") for ln in self.file.read().splitlines() if ln.strip()]
         os.unlink(self.file.name)
-        sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        parsed = []
         for r in rows:
-            if len(r) < 9:
+            if len(r) < 10:
                 continue
             try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
+                t = datetime.datetime.strptime(r[9].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                parsed.append((t, float(r[1]), float(r[2]), [n for n, v in zip(names, r[5:9])
+                                                             if v.strip().lower() == "active"]))
             except ValueError:
                 continue
-            for name, val in zip(names, r[5:9]):
-                if val.strip().lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        scope = "timed region"
+        sel = parsed
+        if self.window is not None:
+            t0, t1 = self.window
+            sel = [x for x in parsed if t0 - 0.05 <= x[0] <= t1 + 0.05]
+            if not sel:
+                # a timed region shorter than the sampling period: the samples
+                # of the same work during the warm-up just before it
+                sel = [x for x in parsed if x[0] <= t1 + 0.05][-5:]
+                scope = "warm-up just before the timed region (timed region shorter than the sampling period)"
+        sm = [x[1] for x in sel]
+        reasons = sorted({n for x in sel for n in x[3]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": sel[-1][2] if sel else None,
+                "reasons": reasons, "samples": len(sm), "scope": scope}
 
 
 # ----------------------------------------------------------------------------- CPU side
@@ -355,20 +372,23 @@ def run_b200(args):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
+    clocks = ClockSampler(local)
+    clocks.start()  # before the warm-up, so that it samples from the first timed step on
     for _ in range(args.warmup):
         step()
-    clocks = ClockSampler(local)
     barrier()
-    clocks.start()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.cudart().cudaProfilerStart()  # lets `ncu --profile-from-start off` see only the timed steps
+    t_wall0 = time.time()
     ev0.record()
     for _ in range(args.steps):
         step()
     ev1.record()
     barrier()
+    t_wall1 = time.time()
     torch.cuda.cudart().cudaProfilerStop()
+    clocks.mark(t_wall0, t_wall1)
     clk = clocks.stop()
     if args.gemm_breakdown and rank == 0:
         for s_ev, e_ev, fl in timer.gemm_events:
