@@ -68,6 +68,8 @@ def parse():
     ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
     ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
     ap.add_argument("--no-bias", action="store_true", help="--gemm: run the epilogue without the bias add")
+    ap.add_argument("--split-k", type=int, default=None,
+                    help="--gemm: K splits per tile (0 automatic, 1 never, 2..8 forced; default: the library's)")
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
     ap.add_argument("--attn", default=None,
@@ -608,9 +610,10 @@ def run_gemm(args):
                             out=ys[i & 1], bias=bias32)
         elif args.block_n or args.cta_pair or args.epilogue != "none" or args.no_bias:
             ops.gemm(xs[i & 1], mod.dense, bias32, residual=res, activation=act, block_n=args.block_n,
-                     out=ys[i & 1], cta_pair=args.cta_pair)
+                     out=ys[i & 1], cta_pair=args.cta_pair, split_k=args.split_k)
         else:
-            ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1], bias=bias32)
+            ops.wide_linear(xs[i & 1], packed, mod.dense, mod.act_bits, out=ys[i & 1], bias=bias32,
+                            split_k=args.split_k)
 
     for i in range(args.warmup):
         step(i)
@@ -646,7 +649,7 @@ def run_gemm(args):
                       "epilogue": args.epilogue,
                       "path": "fused_decode" if args.fused_decode else "prepacked",
                       "weight_copies": copies, "packed_weight_bytes": packed_bytes,
-                      "us_per_launch": ms * 1000, "act_bits": args.act_bits,
+                      "us_per_launch": ms * 1000, "act_bits": args.act_bits, "split_k": args.split_k,
                       "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                                    "frac": tf / peak, "peak_source": f"{src} bf16_tflops (burst)"},
                       "hbm_gbs_algorithmic": hbm_bytes / (ms / 1000) / 1e9}))

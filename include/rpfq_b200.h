@@ -92,7 +92,15 @@ int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32
  * (kernel.py:573). y may alias residual (in-place residual add); the residual
  * has the output's dtype (RPFQ_GEMM_RESIDUAL_F32 iff RPFQ_GEMM_OUT_F32).
  * Requirements: k % 8 == 0, n % 8 == 0, ldx % 8 == 0, ldy % 8 == 0,
- * ldr % 8 == 0, 16-byte aligned x / w / y / bias / residual. */
+ * ldr % 8 == 0, 16-byte aligned x / w / y / bias / residual.
+ * Split-K: when few output tiles would leave most SMs idle (small m), the
+ * K dimension of each tile is split over a cluster of up to 8 CTAs whose
+ * fp32 partials meet in `workspace` (device memory, 16-byte aligned, at
+ * least rpfq_gemm_workspace_bytes(m, n, k) bytes; it holds no state between
+ * calls, but calls that run concurrently need their own). With workspace ==
+ * NULL the call never splits. split_k: 0 = automatic, 1 = never, 2..8 = that
+ * many splits (needs the workspace). The partials are summed in a fixed
+ * order: results are deterministic. */
 typedef struct RpfqGemmArgs {
     const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements)                */
     int64_t ldx;
@@ -108,8 +116,17 @@ typedef struct RpfqGemmArgs {
     int32_t block_n;          /* 0 = automatic; else 128 or 256                         */
     int32_t flags;            /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32 | RPFQ_GEMM_BIAS_F32 */
     int32_t cta_pair;         /* 0 = automatic; 1 = one CTA per tile; 2 = CTA pairs      */
+    int32_t split_k;          /* 0 = automatic; 1 = off; 2..8 = K splits per tile       */
+    int32_t reserved;
+    void* workspace;          /* split-K partials, or NULL (no split)                   */
+    uint64_t workspace_bytes;
 } RpfqGemmArgs;
 int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
+/* Workspace bytes that rpfq_gemm_sm100 (split_k = 0) uses for an m x n x k
+ * product on the current device (0: it does not split); m == 0 returns the
+ * largest amount any shape uses, so one buffer of that size serves every
+ * call on a stream. */
+uint64_t rpfq_gemm_workspace_bytes(int64_t m, int32_t n, int32_t k);
 
 /* Activation quantization of a complex input (per row, Re and Im halves
  * separately), fp16 in / fp16 out. Replaces ActivationQuantSTE.forward
@@ -161,8 +178,10 @@ typedef struct RpfqWideLinearArgs {
     int32_t act_bits;              /* 0 = no activation quantization, else 2..8 */
     int32_t activation;            /* RPFQ_ACT_NONE or RPFQ_ACT_GELU */
     uint16_t* scratch;             /* fp16 [m, 2 k_c] when act_bits > 0 */
-    int32_t flags;                 /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32 */
-    int32_t reserved;
+    int32_t flags;                 /* RPFQ_GEMM_OUT_F32 | RPFQ_GEMM_RESIDUAL_F32 | RPFQ_GEMM_BIAS_F32 */
+    int32_t split_k;               /* as RpfqGemmArgs.split_k (dense path) */
+    void* workspace;               /* as RpfqGemmArgs.workspace, or NULL */
+    uint64_t workspace_bytes;
 } RpfqWideLinearArgs;
 int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream);
 

@@ -32,6 +32,7 @@ ROUND_TIES_AWAY = 1
 EXPORTED_SYMBOLS = (
     "rpfq_prepack_sm100",
     "rpfq_gemm_sm100",
+    "rpfq_gemm_workspace_bytes",
     "rpfq_act_quant_sm100",
     "rpfq_layernorm_sm100",
     "rpfq_layernorm_rows_sm100",
@@ -75,6 +76,8 @@ class RpfqGemmArgs(ctypes.Structure):
         ("m", ctypes.c_int64), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
         ("activation", ctypes.c_int32), ("block_n", ctypes.c_int32),
         ("flags", ctypes.c_int32), ("cta_pair", ctypes.c_int32),
+        ("split_k", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -89,7 +92,8 @@ class RpfqWideLinearArgs(ctypes.Structure):
         ("m", ctypes.c_int64),
         ("act_bits", ctypes.c_int32), ("activation", ctypes.c_int32),
         ("scratch", ctypes.c_void_p),
-        ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32), ("split_k", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -115,6 +119,8 @@ def lib() -> ctypes.CDLL:
         I64 = ctypes.c_int64
         L.rpfq_prepack_sm100.argtypes = [ctypes.POINTER(RpfqPackedLinear), P, I32, P]
         L.rpfq_gemm_sm100.argtypes = [ctypes.POINTER(RpfqGemmArgs), P]
+        L.rpfq_gemm_workspace_bytes.argtypes = [I64, I32, I32]
+        L.rpfq_gemm_workspace_bytes.restype = ctypes.c_uint64
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_layernorm_rows_sm100.argtypes = [P, I64, I64, P, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]

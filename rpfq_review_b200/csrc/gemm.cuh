@@ -29,6 +29,17 @@
 //        per warp) and the output is written over it; WG0 warp 2 prefetches
 //        each tile's residual into L2 two tiles ahead.
 // Register split: 128 x 40 + 256 x 232 = 64512 = 384 threads x 168 at launch.
+//
+// Split-K (one CTA per tile, p.splits > 1; small M, where the tiles alone
+// would leave most SMs idle and each busy SM would stream a long K at the
+// per-SM load rate): the launch is a grid of tiles x splits CTAs in clusters
+// of `splits` CTAs; cluster rank s accumulates k-blocks
+// [s num_k / S, (s + 1) num_k / S) of its tile into TMEM and writes the raw
+// fp32 partial to the workspace in the epilogue warps' own order (every
+// store instruction of a warp covers 512 contiguous bytes). After a cluster
+// barrier (release / acquire) each CTA reduces 1/S of the tile over the S
+// partials in the fixed order 0..S-1 (deterministic) and applies bias, GELU
+// and residual to it.
 #pragma once
 
 #include "ptx.cuh"
@@ -45,6 +56,10 @@ struct GemmParams {
     int32_t n, k;
     int32_t activation;
     int32_t bias_f32;        // bias holds fp32 values (no per-element conversion in the epilogue)
+    int32_t splits;          // K splits per tile (1: none; > 1 only with PAIR = false, cluster = splits)
+    float* ws;               // split-K partials: [tiles * splits][128 * BN] fp32 (splits > 1)
+    void* y;                 // the output (y's dtype, row stride ldy): split-K stores it directly
+    int64_t ldy;
     int* err;                // device error word
 };
 
@@ -123,6 +138,112 @@ __device__ __forceinline__ void setmaxnreg_inc232() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 232;\n" ::: "memory");
 }
 
+// Split-K reduction of tile `tile` by its split `split`: float4 granules
+// [split E / S, (split + 1) E / S) of the S partials (E = 128 BN / 4, laid out
+// as the epilogue warps write them) are summed in the order 0..S-1, then
+// bias, GELU and residual are applied as in the one-pass epilogue and the
+// four outputs of each granule stored (256 threads, tid 0..255). Each thread
+// takes kRedBatch granules at a time and issues all their partial, bias and
+// residual loads before the first use, so a batch costs one memory latency.
+constexpr int kRedMaxSplits = 8;
+constexpr int kRedBatch = 4;
+
+template <int BN, bool OUT_F32>
+__device__ __forceinline__ void splitk_reduce(const GemmParams& p, int tile, int split, int num_n, int tid) {
+    constexpr int E = 128 * BN / 4;
+    constexpr int NS = BN / 64;  // 32-column steps per epilogue warp (half a tile row)
+    const int S = p.splits;
+    const int64_t m0 = static_cast<int64_t>(tile / num_n) * 128;
+    const int n0 = (tile % num_n) * BN;
+    const float4* __restrict__ part = reinterpret_cast<const float4*>(p.ws) + static_cast<size_t>(tile) * S * E;
+    const int lo = split * E / S, hi = (split + 1) * E / S;
+    for (int e0 = lo + tid; e0 < hi; e0 += 256 * kRedBatch) {
+        int64_t row[kRedBatch];
+        int col[kRedBatch];
+        bool live[kRedBatch];
+        float4 buf[kRedMaxSplits][kRedBatch];
+        float4 bb[kRedBatch];
+        float4 rr[kRedBatch];
+#pragma unroll
+        for (int b = 0; b < kRedBatch; ++b) {
+            const int e = e0 + 256 * b;
+            const int l = e & 31, g = (e >> 5) & 7, rest = e >> 8;
+            const int ew = rest / NS, step = rest - ew * NS;
+            row[b] = m0 + 32 * (ew & 3) + l;
+            col[b] = n0 + (ew >> 2) * (BN / 2) + 32 * step + 4 * g;
+            // n is a multiple of 8: a granule is all in or all out
+            live[b] = e < hi && row[b] < p.m && col[b] < p.n;
+#pragma unroll
+            for (int s = 0; s < kRedMaxSplits; ++s)
+                if (live[b] && s < S) buf[s][b] = __ldcg(part + static_cast<size_t>(s) * E + e);
+            bb[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (live[b] && p.bias != nullptr) {
+                if (p.bias_f32) {
+                    bb[b] = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col[b]));
+                } else {
+                    const uint2 h = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(p.bias) + col[b]));
+                    const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                    const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                    bb[b] = make_float4(b0.x, b0.y, b1.x, b1.y);
+                }
+            }
+            rr[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (live[b] && p.residual != nullptr) {
+                if constexpr (OUT_F32) {
+                    rr[b] = *reinterpret_cast<const float4*>(static_cast<const float*>(p.residual) + row[b] * p.ldr + col[b]);
+                } else {
+                    const uint2 h = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p.residual) + row[b] * p.ldr + col[b]);
+                    const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                    const float2 r1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                    rr[b] = make_float4(r0.x, r0.y, r1.x, r1.y);
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < kRedBatch; ++b) {
+            if (!live[b]) continue;
+            float4 a = buf[0][b];
+#pragma unroll
+            for (int s = 1; s < kRedMaxSplits; ++s) {
+                if (s < S) {
+                    a.x += buf[s][b].x;
+                    a.y += buf[s][b].y;
+                    a.z += buf[s][b].z;
+                    a.w += buf[s][b].w;
+                }
+            }
+            float v[4] = {a.x, a.y, a.z, a.w};
+            if (p.bias != nullptr) {
+                v[0] += bb[b].x;
+                v[1] += bb[b].y;
+                v[2] += bb[b].z;
+                v[3] += bb[b].w;
+            }
+            if (p.activation == kActGelu) {
+                gelu_erf_pair(v[0], v[1]);
+                gelu_erf_pair(v[2], v[3]);
+            }
+            if (p.residual != nullptr) {
+                v[0] += rr[b].x;
+                v[1] += rr[b].y;
+                v[2] += rr[b].z;
+                v[3] += rr[b].w;
+            }
+            if constexpr (OUT_F32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.y) + row[b] * p.ldy + col[b]) =
+                    make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+                __half2 h0 = __floats2half2_rn(v[0], v[1]);
+                __half2 h1 = __floats2half2_rn(v[2], v[3]);
+                uint2 o;
+                o.x = *reinterpret_cast<uint32_t*>(&h0);
+                o.y = *reinterpret_cast<uint32_t*>(&h1);
+                *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + row[b] * p.ldy + col[b]) = o;
+            }
+        }
+    }
+}
+
 template <int BN, bool OUT_F32, int RES, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -147,13 +268,19 @@ __global__ void __launch_bounds__(384, 1)
     const int lane = threadIdx.x & 31;
     // CTA pairs: rank 0 (leader) issues the MMAs; tiles are scheduled per pair.
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-    const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-    const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+    // split-K: CTA blockIdx.x = tile * splits + s takes k-blocks [kb_lo, kb_hi) of one tile
+    const int splits = PAIR ? 1 : p.splits;
+    const int split = PAIR ? 0 : static_cast<int>(blockIdx.x) % splits;
+    const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x) / splits;
+    const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x) / splits;
 
     const int num_m = static_cast<int>((p.m + C::TILE_M - 1) / C::TILE_M);
     const int num_n = (p.n + BN - 1) / BN;
     const int num_k = (p.k + C::BK - 1) / C::BK;
     const int num_tiles = num_m * num_n;
+    const int kb_lo = split * num_k / splits;
+    const int kb_hi = (split + 1) * num_k / splits;
+    const bool use_res = p.residual != nullptr && splits == 1;  // split-K adds the residual in its reduction
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -171,7 +298,7 @@ __global__ void __launch_bounds__(384, 1)
         prefetch_tmap(&tm_x);
         prefetch_tmap(&tm_w);
         prefetch_tmap(&tm_y);
-        if (p.residual != nullptr) prefetch_tmap(&tm_r);
+        if (use_res) prefetch_tmap(&tm_r);
     }
     if (warp == 1) {
         if constexpr (PAIR) {
@@ -201,7 +328,7 @@ __global__ void __launch_bounds__(384, 1)
             for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
                 const int m0 = (tile / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
                 const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * C::B_ROWS;
-                for (int kb = 0; kb < num_k; ++kb) {
+                for (int kb = kb_lo; kb < kb_hi; ++kb) {
                     if (!wait_bar(&empty_bar[stage], phase ^ 1, abort_flag, p.err, 101)) {
                         ok = false;
                         break;
@@ -262,7 +389,7 @@ __global__ void __launch_bounds__(384, 1)
                 if (!wait_bar<PAIR>(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, 201)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < num_k; ++kb) {
+                for (int kb = kb_lo; kb < kb_hi; ++kb) {
                     if (!wait_bar(&full_bar[stage], phase, abort_flag, p.err, 202)) {
                         ok = false;
                         break;
@@ -275,9 +402,9 @@ __global__ void __launch_bounds__(384, 1)
                     for (int kk = 0; kk < C::BK / 16; ++kk) {
                         // +32 B per K step of 16 fp16 inside the 128-B swizzle row
                         if constexpr (PAIR)
-                            umma_f16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                            umma_f16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb - kb_lo) + kk != 0);
                         else
-                            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb - kb_lo) + kk != 0);
                     }
                     commit_both(&empty_bar[stage]);
                     if (++stage == C::STAGES) {
@@ -299,7 +426,7 @@ __global__ void __launch_bounds__(384, 1)
                 umma_commit(drain_bar);
             volatile int no_abort = 0;
             wait_bar(drain_bar, 0, &no_abort, p.err, 203);
-        } else if (warp == 2 && lane == 0 && p.residual != nullptr) {
+        } else if (warp == 2 && lane == 0 && use_res) {
             // -------------------------------------------------------- residual prefetcher
             // The residual of this CTA's tile i+2 is prefetched into L2 (one TMA
             // box per column half) when tile i's accumulator is complete, i.e.
@@ -323,6 +450,12 @@ __global__ void __launch_bounds__(384, 1)
                     acc = 0;
                     acc_phase ^= 1;
                 }
+            }
+        }
+        if constexpr (!PAIR) {
+            if (splits > 1) {
+                __syncwarp();
+                cluster_sync();  // the split-K exchange barrier, which every thread of the cluster joins
             }
         }
     } else {
@@ -356,7 +489,7 @@ __global__ void __launch_bounds__(384, 1)
             const int nsteps = (valid > 0 && row0 < p.m) ? (valid + CW - 1) / CW : 0;
             if constexpr (RES > 0) {
                 // first residual step of the tile lands while the main loop runs
-                if (lane == 0 && nsteps > 0) {
+                if (lane == 0 && nsteps > 0 && splits == 1) {
                     bulk_wait_group_read<0>();
                     load_residual(RES == 2 ? (j & 1) : 0, c_begin, row0);
                 }
@@ -366,8 +499,25 @@ __global__ void __launch_bounds__(384, 1)
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
                                    static_cast<uint32_t>(acc * BN + col_half * HALF);
             bool ok = true;
+            if (splits > 1) {
+                // split-K partial: the raw accumulator, 32 columns per step; granule
+                // (ew, step, g) of lane l at float4 ((ew * NS + step) * 8 + g) * 32 + l
+                constexpr int NS = HALF / 32;
+                float4* dst = reinterpret_cast<float4*>(p.ws) + static_cast<size_t>(blockIdx.x) * (C::BM * BN / 4) +
+                              static_cast<size_t>(ew) * NS * 256 + lane;
 #pragma unroll 1
-            for (int c = 0; c < nsteps; ++c, ++j) {
+                for (int c = 0; c < NS; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + 32 * c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        __stcg(dst + (c * 8 + g) * 32, make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                                                   __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+                }
+            }
+#pragma unroll 1
+            for (int c = 0; c < (splits > 1 ? 0 : nsteps); ++c, ++j) {
                 const int col0 = c_begin + c * CW;
                 if constexpr (RES == 2) {
                     // next residual step into the other slot, once that slot's
@@ -522,6 +672,14 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
+        if constexpr (!PAIR) {
+            if (splits > 1) {
+                // every split's partial is written (release) and visible here (acquire);
+                // the reduction runs in this register-rich region
+                cluster_sync();
+                if (first_tile < num_tiles) splitk_reduce<BN, OUT_F32>(p, first_tile, split, num_n, threadIdx.x - 128);
+            }
+        }
     }
 
     tc_fence_before();

@@ -246,7 +246,7 @@ int make_tmap_codes(CUtensorMap* m, const void* base, int64_t rows, int64_t byte
 
 // ---------------------------------------------------------------- GEMM launch
 template <int BN, bool OUT_F32, int RES, bool PAIR>
-int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
+int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits) {
     using C = GemmCfg<BN, RES, PAIR>;
     constexpr int CW = OUT_F32 ? 32 : 64;   // output / residual columns per 128-B step
     constexpr int ESZ = OUT_F32 ? 4 : 2;
@@ -267,6 +267,10 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     p.n = a->n;
     p.k = a->k;
     p.activation = a->activation;
+    p.splits = PAIR ? 1 : splits;
+    p.ws = static_cast<float*>(a->workspace);
+    p.y = a->y;
+    p.ldy = a->ldy;
     p.err = st->err_word;
     const int64_t tiles = ((a->m + C::TILE_M - 1) / C::TILE_M) * ((a->n + BN - 1) / BN);
     if constexpr (PAIR) {
@@ -294,6 +298,10 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
         const int pairs = static_cast<int>(tiles < max_pairs[dev] ? tiles : max_pairs[dev]);
         RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, dim3(2 * pairs), dim3(C::THREADS),
                                 C::SMEM_BYTES, stream, 2, tx, tw, ty, tr, p));
+    } else if (p.splits > 1) {
+        // split-K: one CTA per (tile, split), the splits of a tile in one cluster
+        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(static_cast<int>(tiles) * p.splits),
+                                dim3(C::THREADS), C::SMEM_BYTES, stream, p.splits, tx, tw, ty, tr, p));
     } else {
         const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
         RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(grid), dim3(C::THREADS),
@@ -302,20 +310,60 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
     return RPFQ_OK;
 }
 
+// ---------------------------------------------------------------- split-K choice
+constexpr int kMaxSplits = 8;        // portable cluster size
+constexpr int kMinSplitKBlocks = 2;  // k-blocks (of 64) per split, automatic choice
+
+// Clusters of `s` one-CTA-per-tile GEMM CTAs that fit on the device at once
+// (queried once per device, tile width and s).
+template <int BN>
+int max_clusters(int s, DeviceState* st) {
+    static int cache[kMaxDevices][kMaxSplits + 1] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cache[dev][s] == 0) {
+        cudaLaunchConfig_t q = {};
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = s;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.gridDim = dim3(s * (st->sm_count / s));
+        q.blockDim = dim3(GemmCfg<BN, 0, false>::THREADS);
+        q.dynamicSmemBytes = GemmCfg<BN, 0, false>::SMEM_BYTES;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_sm100_kernel<BN, false, 0, false>, &q) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        cache[dev][s] = n > 0 ? n : -1;
+    }
+    return cache[dev][s] > 0 ? cache[dev][s] : 0;
+}
+
+int64_t gemm_tiles(int64_t m, int n, int bn) { return ((m + 127) / 128) * ((n + bn - 1) / bn); }
+
+uint64_t splitk_bytes(int64_t m, int n, int bn, int s) {
+    return static_cast<uint64_t>(gemm_tiles(m, n, bn)) * static_cast<uint64_t>(s) * 128u * static_cast<uint64_t>(bn) * 4u;
+}
+
 // Residual slots: two (one main-loop stage less) when the main loop is short
 // and the epilogue must hide the residual latency itself; one otherwise.
+// Split-K reads the residual in its reduction: no staging slots.
 template <int BN, bool PAIR>
-int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream) {
+int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits) {
     const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
-    const int res = a->residual == nullptr ? 0 : (a->k <= 1024 ? 2 : 1);
+    const int res = (a->residual == nullptr || splits > 1) ? 0 : (a->k <= 1024 ? 2 : 1);
     if (f32) {
-        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream);
-        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream);
-        return launch_gemm<BN, true, 0, PAIR>(a, st, stream);
+        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream, splits);
+        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream, splits);
+        return launch_gemm<BN, true, 0, PAIR>(a, st, stream, splits);
     }
-    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream);
-    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream);
-    return launch_gemm<BN, false, 0, PAIR>(a, st, stream);
+    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream, splits);
+    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream, splits);
+    return launch_gemm<BN, false, 0, PAIR>(a, st, stream, splits);
 }
 
 // ---------------------------------------------------------------- K3 fused decode launch
@@ -432,6 +480,66 @@ int pick_block_n(int64_t m, int n, int sm_count) {
     return best;
 }
 
+struct GemmPlan {
+    int bn;      // tile width
+    bool pair;   // CTA pairs (256 x 256 tiles)
+    int splits;  // K splits per tile (one CTA per tile)
+};
+
+// Time (us) of a one-CTA-per-tile plan when few tiles leave SMs idle, fitted
+// to CUDA-event timings on B200 (M = 198..1584, K = 384..4096): a fixed
+// launch-to-store cost (4.8 us for 128-wide tiles, 7.3 us for 256-wide ones:
+// twice the epilogue), 0.28 us per k-block of the busiest CTA (each SM then
+// streams its operands on its own), and for split-K the partial round trip
+// (write, cluster barrier, batched reads) of 0.9 + 6 (bn / 128) / s us.
+// < 0 when the plan does not fit one wave of clusters.
+double small_m_cost(int64_t m, int n, int k, int bn, int s, DeviceState* st) {
+    const int64_t tiles = gemm_tiles(m, n, bn);
+    const int num_k = (k + 63) / 64;
+    if (s > num_k || (s > 1 && num_k / s < kMinSplitKBlocks)) return -1.0;
+    int64_t waves = (tiles + st->sm_count - 1) / st->sm_count;
+    if (s > 1) {
+        const int fit = bn == 256 ? max_clusters<256>(s, st) : max_clusters<128>(s, st);
+        if (tiles > fit) return -1.0;
+        waves = 1;
+    }
+    const double fixed = bn == 256 ? 7.3 : 4.8;
+    const double reduce = s > 1 ? 0.9 + 6.0 * (bn / 128.0) / s : 0.0;
+    return static_cast<double>(waves) * (fixed + 0.28 * ((num_k + s - 1) / s) + reduce);
+}
+
+// Tile width, CTA pairs and K splits of one call. Without a workspace (or
+// split_k = 1) the tile width comes from the wave-quantisation model of
+// pick_block_n; with one, shapes whose 128-wide tiles do not fill the SMs are
+// planned by small_m_cost over tile widths and split counts.
+GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split_k, bool have_ws, DeviceState* st) {
+    GemmPlan g;
+    g.bn = block_n ? block_n : pick_block_n(m, n, st->sm_count);
+    const int64_t pair_tiles = ((m + 255) / 256) * ((n + 255) / 256);
+    g.pair = g.bn == 256 && (cta_pair == 2 || (cta_pair == 0 && split_k <= 1 && pair_tiles >= st->sm_count / 2));
+    g.splits = 1;
+    if (g.pair || !have_ws || split_k == 1) return g;
+    const int num_k = (k + 63) / 64;
+    if (split_k > 1) {
+        g.splits = std::min(split_k, num_k);
+        return g;
+    }
+    if (gemm_tiles(m, n, 128) > st->sm_count) return g;
+    double best = -1.0;
+    for (int bn : {128, 256}) {
+        if (block_n && bn != block_n) continue;
+        for (int s = 1; s <= kMaxSplits; ++s) {
+            const double c = small_m_cost(m, n, k, bn, s, st);
+            if (c >= 0 && (best < 0 || c < best - 1e-9)) {
+                best = c;
+                g.bn = bn;
+                g.splits = s;
+            }
+        }
+    }
+    return g;
+}
+
 int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: null args");
     if (!a->x || !a->w || !a->y) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: x, w and y are required");
@@ -451,23 +559,35 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: all pointers must be 16-byte aligned");
     if (a->activation != RPFQ_ACT_NONE && a->activation != RPFQ_ACT_GELU)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: unknown activation %d", a->activation);
+    if (a->split_k < 0 || a->split_k > kMaxSplits)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: split_k must be 0..%d (got %d)", kMaxSplits, a->split_k);
+    if (a->workspace && !aligned16(a->workspace))
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: the workspace must be 16-byte aligned");
+    if (a->split_k > 1 && a->cta_pair == 2)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: split_k > 1 runs one CTA per tile (cta_pair 2 given)");
+    if (a->split_k > 1 && !a->workspace)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: split_k %d needs a workspace", a->split_k);
     if (a->m > (int64_t(1) << 31) - 256) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_gemm_sm100: m too large");
     if (a->m == 0) return RPFQ_OK;
     DeviceState* st;
     int rc = device_state(&st);
     if (rc) return rc;
-    int bn = a->block_n ? a->block_n : pick_block_n(a->m, a->n, st->sm_count);
-    // CTA pairs (256 x 256 tiles over two SMs) when the 256-wide tile is chosen
-    // and there are enough row pairs to fill the GPU; cta_pair forces either way.
-    const int64_t pair_tiles = ((a->m + 255) / 256) * ((a->n + 255) / 256);
-    const bool pair = bn == 256 && (a->cta_pair == 2 || (a->cta_pair == 0 && pair_tiles >= st->sm_count / 2));
     if (a->cta_pair < 0 || a->cta_pair > 2)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: cta_pair must be 0, 1 or 2 (got %d)", a->cta_pair);
-    switch (bn) {
-        case 256: return pair ? launch_gemm_bn<256, true>(a, st, stream) : launch_gemm_bn<256, false>(a, st, stream);
-        case 128: return launch_gemm_bn<128, false>(a, st, stream);
-        default: return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 128 or 256 (got %d)", bn);
-    }
+    if (a->block_n != 0 && a->block_n != 128 && a->block_n != 256)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 128 or 256 (got %d)", a->block_n);
+    // CTA pairs (256 x 256 tiles over two SMs) when the 256-wide tile is chosen
+    // and there are enough row pairs to fill the GPU; cta_pair forces either way.
+    GemmPlan g = plan_gemm(a->m, a->n, a->k, a->block_n, a->cta_pair, a->split_k, a->workspace != nullptr, st);
+    if (a->split_k == 0 && g.splits > 1 && splitk_bytes(a->m, a->n, g.bn, g.splits) > a->workspace_bytes)
+        g = plan_gemm(a->m, a->n, a->k, a->block_n, a->cta_pair, 1, false, st);  // too small a workspace: no split
+    const int splits = g.splits;
+    if (splits > 1 && splitk_bytes(a->m, a->n, g.bn, splits) > a->workspace_bytes)
+        return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: %d K splits need a workspace of %llu bytes (got %llu)", splits,
+                    (unsigned long long)splitk_bytes(a->m, a->n, g.bn, splits), (unsigned long long)a->workspace_bytes);
+    if (g.bn == 256)
+        return g.pair ? launch_gemm_bn<256, true>(a, st, stream, 1) : launch_gemm_bn<256, false>(a, st, stream, splits);
+    return launch_gemm_bn<128, false>(a, st, stream, splits);
 }
 
 // ---------------------------------------------------------------- packed-layer validation
@@ -566,6 +686,15 @@ int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32
 
 int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream) {
     return gemm(args, static_cast<cudaStream_t>(stream));
+}
+
+uint64_t rpfq_gemm_workspace_bytes(int64_t m, int32_t n, int32_t k) {
+    DeviceState* st;
+    if (device_state(&st)) return 0;
+    if (m == 0) return static_cast<uint64_t>(st->sm_count) * 128u * 256u * 4u;  // tiles x splits <= SMs
+    if (m < 0 || n <= 0 || k <= 0) return 0;
+    const GemmPlan g = plan_gemm(m, n, k, 0, 0, 0, true, st);
+    return g.splits > 1 ? splitk_bytes(m, n, g.bn, g.splits) : 0;
 }
 
 int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t ldq, int64_t m, int32_t k,
@@ -898,6 +1027,9 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
     g.k = K;
     g.activation = a->activation;
     g.flags = a->flags;
+    g.split_k = a->split_k;
+    g.workspace = a->workspace;
+    g.workspace_bytes = a->workspace_bytes;
     return gemm(&g, static_cast<cudaStream_t>(stream));
 }
 

@@ -12,6 +12,7 @@ a missing library raises — there is no fallback path.
 from __future__ import annotations
 
 import ctypes
+import os
 import math
 
 import torch
@@ -63,6 +64,28 @@ FUSED_DECODE_MAX_ROWS = 256
 
 def _p(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
+
+
+# Split-K for small-M GEMMs: 0 = automatic, 1 = never, 2..8 = forced (the
+# RPFQ_SPLIT_K environment variable sets the default of every call).
+SPLIT_K = int(os.environ.get("RPFQ_SPLIT_K", "0"))
+
+# One split-K workspace per (device, stream): calls on one stream run in
+# order, so they can share it; calls on different streams may overlap.
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, split_k: int) -> tuple[int | None, int]:
+    if split_k == 1:
+        return None, 0
+    key = (device.index if device.index is not None else torch.cuda.current_device(), _stream(device))
+    ws = _workspaces.get(key)
+    if ws is None:
+        with torch.cuda.device(device):
+            nbytes = int(_lib.lib().rpfq_gemm_workspace_bytes(0, 0, 0))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws.data_ptr(), ws.numel()
 
 
 def _require(t: torch.Tensor, name: str, dtype=torch.float16):
@@ -225,10 +248,12 @@ def _flags(out: torch.Tensor, residual: torch.Tensor | None, bias: torch.Tensor 
 
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, activation="none", block_n: int = 0,
-         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16, cta_pair: int = 0) -> torch.Tensor:
+         out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16, cta_pair: int = 0,
+         split_k: int | None = None) -> torch.Tensor:
     """K2: ``act(x @ w.T + bias) + residual`` with fp16 operands, fp32
     accumulation; ``residual`` and ``out`` may be fp16 or fp32 (and may be the
-    same tensor for an in-place residual add)."""
+    same tensor for an in-place residual add). ``split_k``: 0 automatic (small
+    M splits K over a cluster of CTAs), 1 never, 2..8 forced; None = ``SPLIT_K``."""
     _require(x, "x")
     _require(w, "w")
     n, k = w.shape
@@ -251,9 +276,12 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     y2, ldy = _rows(out, n, "out")
     if y2.data_ptr() != out.data_ptr() or y2.shape[0] != m:
         raise ValueError("out must be a row-major view with unit column stride")
+    split_k = SPLIT_K if split_k is None else int(split_k)
+    ws, ws_bytes = _workspace(x.device, split_k)
     a = _lib.RpfqGemmArgs(x=x2.data_ptr(), ldx=ldx, w=w.data_ptr(), bias=_p(bias), residual=_p(r2), ldr=ldr,
                           y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n,
-                          flags=_flags(out, r2, bias), cta_pair=cta_pair)
+                          flags=_flags(out, r2, bias), cta_pair=cta_pair, split_k=split_k, workspace=ws,
+                          workspace_bytes=ws_bytes)
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:
@@ -316,7 +344,7 @@ def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -
 def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None, act_bits: int = 0,
                 activation="none", residual: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16,
-                bias: torch.Tensor | None = None) -> torch.Tensor:
+                bias: torch.Tensor | None = None, split_k: int | None = None) -> torch.Tensor:
     """Whole layer through ``rpfq_wide_linear_sm100``: optional activation
     quantization, then the GEMM over the prepacked coefficients with bias and
     epilogue. ``x`` is fp16 ``[..., 2 k_c]``; ``residual`` / ``out`` fp16 or
@@ -327,7 +355,8 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
     are decoded inside the GEMM and no dense matrix exists anywhere.
 
     ``bias`` (optional) replaces ``layer.bias`` for this call, e.g. the same
-    values widened to fp32 once, which the epilogue adds without converting."""
+    values widened to fp32 once, which the epilogue adds without converting.
+    ``split_k`` as in :func:`gemm` (dense path)."""
     _require(x, "x")
     if dense is not None:
         _require(dense, "dense")
@@ -348,10 +377,13 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
         raise ValueError("out must be a row-major view with unit column stride")
     scratch = torch.empty((m, K), dtype=torch.float16, device=x.device) if act_bits else None
     s = layer_struct(layer)
+    split_k = SPLIT_K if split_k is None else int(split_k)
+    ws, ws_bytes = _workspace(x.device, split_k) if dense is not None else (None, 0)
     a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=_p(dense), x=x2.data_ptr(), ldx=ldx,
                                 bias=_p(bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
                                 act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch),
-                                flags=_flags(out, r2, bias))
+                                flags=_flags(out, r2, bias), split_k=split_k, workspace=ws,
+                                workspace_bytes=ws_bytes)
     timer = _timer
     with torch.cuda.device(x.device):
         if timer is not None:

@@ -33,11 +33,12 @@ def test_struct_layouts_match_header():
     """ctypes mirrors of the header structs have the C sizes."""
     assert ctypes.sizeof(_lib.RpfqPhasePlane) == 24
     assert ctypes.sizeof(_lib.RpfqPackedLinear) == 6 * 4 + 8 * 24
-    assert ctypes.sizeof(_lib.RpfqGemmArgs) == 8 * 9 + 4 * 6
-    assert ctypes.sizeof(_lib.RpfqWideLinearArgs) == 8 * 10 + 4 * 2 + 8 + 4 * 2
+    assert ctypes.sizeof(_lib.RpfqGemmArgs) == 8 * 9 + 4 * 6 + 4 * 2 + 8 * 2
+    assert ctypes.sizeof(_lib.RpfqWideLinearArgs) == 8 * 10 + 4 * 2 + 8 + 4 * 2 + 8 * 2
 
 
-@pytest.mark.parametrize("bad", ["null", "k", "n", "ldx", "act", "block_n"])
+@pytest.mark.parametrize("bad", ["null", "k", "n", "ldx", "act", "block_n", "split_k", "split_no_ws",
+                                 "ws_align", "split_pair"])
 def test_gemm_validation_rejects_before_launch(bad):
     L = _lib.lib()
     a = _lib.RpfqGemmArgs(x=16, ldx=64, w=32, y=48, ldy=64, m=4, n=64, k=64)
@@ -53,6 +54,16 @@ def test_gemm_validation_rejects_before_launch(bad):
         a.activation = 7
     elif bad == "block_n":
         a.block_n = 96
+    elif bad == "split_k":
+        a.split_k = 9
+        a.workspace, a.workspace_bytes = 4096, 1 << 20
+    elif bad == "split_no_ws":
+        a.split_k = 4
+    elif bad == "ws_align":
+        a.workspace, a.workspace_bytes = 4100, 1 << 20
+    elif bad == "split_pair":
+        a.split_k, a.cta_pair = 2, 2
+        a.workspace, a.workspace_bytes = 4096, 1 << 20
     rc = L.rpfq_gemm_sm100(ctypes.byref(a), None)
     if bad == "block_n":
         # block_n is checked after the device set-up, which needs a GPU

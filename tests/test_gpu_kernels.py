@@ -157,6 +157,70 @@ def test_gemm_fp32_output_and_residual(cuda, m, n, k, cta_pair):
     assert torch.equal(y2, y)
 
 
+SPLIT_SHAPES = [
+    (198, 768, 3072),     # one image through ViT-B fc2
+    (198, 2304, 768),     # one image through ViT-B qkv
+    (1, 384, 1536),       # a single row
+    (300, 1000, 768),     # partial last tile in m and n
+    (129, 96, 96),        # two k-blocks, K tail
+    (64, 256, 4096),
+]
+
+
+@pytest.mark.parametrize("m,n,k", SPLIT_SHAPES)
+@pytest.mark.parametrize("split_k", [0, 2, 3, 8])
+@pytest.mark.parametrize("block_n", [128, 256])
+def test_gemm_split_k_matches_fp64(cuda, m, n, k, split_k, block_n):
+    """Split-K over a cluster (forced counts and the automatic choice): bias
+    + GELU into fp16, and bias + fp32 residual in place, against float64."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, generator=g).half()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, generator=g) * 0.1).half()
+    xc, wc, bc = x.to(cuda), w.to(cuda), b.to(cuda)
+    lin = x.double() @ w.double().T + b.double()
+    y = ops.gemm(xc, wc, bc, activation="gelu", block_n=block_n, cta_pair=1, split_k=split_k).cpu()
+    ref = torch.nn.functional.gelu(lin)
+    assert rel_err(y.numpy(), ref.numpy()) < TOL
+    err = (y.double() - ref).abs()
+    assert torch.all(err <= ref.abs() * 2.0 ** -10 + 1e-3 * ref.abs().max())
+    r = torch.randn(m, n, generator=g) * 3.0
+    res = r.to(cuda)
+    y2 = ops.gemm(xc, wc, bc, residual=res, out=res, block_n=block_n, cta_pair=1, split_k=split_k)
+    ref2 = lin + r.double()
+    assert float((y2.cpu().double() - ref2).abs().max()) < 1e-5 * float(ref2.abs().max()) * k ** 0.5
+
+
+@pytest.mark.parametrize("m,n,k", [(198, 768, 3072), (300, 1000, 768)])
+def test_gemm_split_k_deterministic_and_close_to_one_pass(cuda, m, n, k):
+    """Partials are summed in a fixed order: repeated calls are bit-identical;
+    against the one-pass GEMM only the fp32 summation order differs."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(m, k, generator=g).half().to(cuda)
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).half().to(cuda)
+    b = (torch.randn(n, generator=g) * 0.1).to(cuda)
+    outs = [ops.gemm(x, w, b, out_dtype=torch.float32, cta_pair=1, split_k=4) for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    one = ops.gemm(x, w, b, out_dtype=torch.float32, cta_pair=1, split_k=1)
+    assert float((outs[0] - one).abs().max()) < 1e-5 * float(one.abs().max()) * k ** 0.5
+    assert not torch.equal(outs[0], one) or k <= 256  # the split path really ran
+
+
+def test_gemm_split_k_automatic_choice(cuda):
+    """The automatic choice splits small-M, long-K products and leaves large
+    ones alone; the workspace query bounds every automatic split."""
+    from rpfq_review_b200 import _lib
+    L = _lib.lib()
+    full = L.rpfq_gemm_workspace_bytes(0, 0, 0)
+    assert full >= 148 * 128 * 256 * 4
+    small = L.rpfq_gemm_workspace_bytes(198, 768, 3072)
+    assert 0 < small <= full
+    assert L.rpfq_gemm_workspace_bytes(50432, 768, 768) == 0
+    assert L.rpfq_gemm_workspace_bytes(198, 768, 128) == 0  # two k-blocks: nothing to split
+
+
 @pytest.mark.parametrize("d", [96, 192, 384, 768, 1024, 1536, 3072])
 @pytest.mark.parametrize("act_bits", [0, 4])
 def test_layernorm_kernel(cuda, d, act_bits):
