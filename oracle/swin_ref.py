@@ -12,6 +12,12 @@ head. Every quantized linear uses the dense weight reconstructed from its
 packed planes (``oracle.packed_ref.dense_weight_from_packed``). The window /
 mask helpers are the product's (pure index bookkeeping, checked separately
 by their own unit test); the arithmetic here is independent.
+
+``fp16`` / ``fp16_act`` as in ``oracle.vit_ref``: the coefficients rounded
+through fp16 (the runtime's fp16 coefficient cache) and the activations the
+benchmarked configuration keeps in fp16 (LayerNorm outputs, qkv, softmax
+probabilities, attention output, GELU output, the pooled features) rounded,
+with a float32 residual stream and float32 accumulation.
 """
 
 from __future__ import annotations
@@ -24,15 +30,18 @@ from . import packed_ref as pr
 from .vit_ref import packed_to_numpy
 
 
-def extract_weights(model, dtype=torch.float32, linears: bool = True) -> dict:
+def extract_weights(model, dtype=torch.float32, linears: bool = True, fp16: bool = False) -> dict:
     """Dense reference weights of a ``rpfq_review_b200.swin.PackedSwin``
-    (``linears=False``: everything but the packed linears)."""
+    (``linears=False``: everything but the packed linears; ``fp16``: the
+    coefficients rounded through fp16)."""
     w = {"patch_w": model.patch_w.to(dtype).cpu(), "patch_b": model.patch_b.to(dtype).cpu(),
          "patch_norm_w": model.patch_norm_w.to(dtype).cpu(), "patch_norm_b": model.patch_norm_b.to(dtype).cpu(),
          "norm_w": model.norm_w.to(dtype).cpu(), "norm_b": model.norm_b.to(dtype).cpu()}
     for name, mod in (model.quantized_linears() if linears else ()):
         np_layer = packed_to_numpy(mod.packed())
         dense = pr.dense_weight_from_packed(np_layer, mod.n_c, mod.k_c)
+        if fp16:
+            dense = dense.astype(np.float16).astype(np.float32)
         w[name] = (torch.from_numpy(dense).to(dtype), torch.from_numpy(np_layer["bias"].astype(np.float32)).to(dtype))
     for s, stage in enumerate(model.stages):
         w[f"layers.{s}.rel_index"] = stage.rel_index.cpu()
@@ -45,10 +54,14 @@ def extract_weights(model, dtype=torch.float32, linears: bool = True) -> dict:
     return w
 
 
-def swin_forward(w: dict, cfg, images: torch.Tensor, lin=None) -> torch.Tensor:
+def swin_forward(w: dict, cfg, images: torch.Tensor, lin=None, fp16_act: bool = False) -> torch.Tensor:
     """Logits ``[B, classes]``; ``lin(name, t)`` overrides the packed linears
     (default: F.linear with the dense weights in ``w``)."""
     from rpfq_review_b200.swin import shift_mask, window_partition, window_reverse
+
+    def r16(t):
+        return t.half().float() if fp16_act else t
+
     x = images.float()
     b = x.shape[0]
     p = cfg.patch
@@ -71,11 +84,11 @@ def swin_forward(w: dict, cfg, images: torch.Tensor, lin=None) -> torch.Tensor:
         for i in range(depth):
             pre = f"layers.{s}.blocks.{i}"
             sh = shift if i % 2 == 1 else 0
-            h = F.layer_norm(x, (c,), w[f"{pre}.norm1_w"], w[f"{pre}.norm1_b"], cfg.eps).view(b, r, r, c)
+            h = r16(F.layer_norm(x, (c,), w[f"{pre}.norm1_w"], w[f"{pre}.norm1_b"], cfg.eps)).view(b, r, r, c)
             if sh:
                 h = torch.roll(h, shifts=(-sh, -sh), dims=(1, 2))
             win = window_partition(h, ws)
-            qkv = lin(f"{pre}.qkv", win).view(win.shape[0], L, 3, nh, hd).permute(2, 0, 3, 1, 4)
+            qkv = r16(lin(f"{pre}.qkv", win)).view(win.shape[0], L, 3, nh, hd).permute(2, 0, 3, 1, 4)
             q, k, v = qkv[0], qkv[1], qkv[2]
             att = torch.matmul(q, k.transpose(-2, -1)) * (hd ** -0.5)
             bias = w[f"{pre}.rel_table"][idx].reshape(L, L, nh).permute(2, 0, 1)
@@ -84,18 +97,18 @@ def swin_forward(w: dict, cfg, images: torch.Tensor, lin=None) -> torch.Tensor:
                 nw = (r // ws) ** 2
                 m = shift_mask(r, ws, sh)
                 att = (att.view(b, nw, nh, L, L) + m[None, :, None]).view(-1, nh, L, L)
-            a = torch.matmul(torch.softmax(att, dim=-1), v).transpose(1, 2).reshape(win.shape[0], L, c)
+            a = r16(torch.matmul(r16(torch.softmax(att, dim=-1)), v).transpose(1, 2).reshape(win.shape[0], L, c))
             o = window_reverse(lin(f"{pre}.proj", a), ws, r)
             if sh:
                 o = torch.roll(o, shifts=(sh, sh), dims=(1, 2))
             x = x + o.reshape(b, r * r, c)
-            h = F.layer_norm(x, (c,), w[f"{pre}.norm2_w"], w[f"{pre}.norm2_b"], cfg.eps)
-            x = x + lin(f"{pre}.fc2", F.gelu(lin(f"{pre}.fc1", h), approximate="none"))
+            h = r16(F.layer_norm(x, (c,), w[f"{pre}.norm2_w"], w[f"{pre}.norm2_b"], cfg.eps))
+            x = x + lin(f"{pre}.fc2", r16(F.gelu(lin(f"{pre}.fc1", h), approximate="none")))
         if s + 1 < len(cfg.depths):
             xs = x.view(b, r, r, c)
             cat = torch.cat([xs[:, 0::2, 0::2], xs[:, 1::2, 0::2], xs[:, 0::2, 1::2], xs[:, 1::2, 1::2]], dim=-1)
-            h = F.layer_norm(cat.reshape(b, -1, 4 * c), (4 * c,), w[f"layers.{s}.merge_norm_w"],
-                             w[f"layers.{s}.merge_norm_b"], cfg.eps)
+            h = r16(F.layer_norm(cat.reshape(b, -1, 4 * c), (4 * c,), w[f"layers.{s}.merge_norm_w"],
+                                 w[f"layers.{s}.merge_norm_b"], cfg.eps))
             x = lin(f"layers.{s + 1}.downsample.reduction", h)
-    h = F.layer_norm(x, (dims[-1],), w["norm_w"], w["norm_b"], cfg.eps)
-    return lin("head", h.mean(dim=1))
+    h = r16(F.layer_norm(x, (dims[-1],), w["norm_w"], w["norm_b"], cfg.eps))
+    return lin("head", r16(h.mean(dim=1)))

@@ -10,6 +10,16 @@ the class token (DeiT: mean of the two heads at eval). Every quantized
 linear uses the dense weight reconstructed from its packed planes by
 ``oracle.packed_ref.dense_weight_from_packed`` (the exporter's
 ``quantized_forward_weight``), i.e. the deployment path in float32/float64.
+
+``fp16=True`` (``extract_weights``) rounds the dense coefficients through
+fp16, i.e. the reference runtime's fused fp16 coefficient cache
+(RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.cpp:117-166,
+round-to-nearest-even here); ``fp16_act=True`` (``vit_forward``) rounds the
+activations that configs[1] keeps in fp16 — every LayerNorm output (GEMM
+input), the qkv output, the softmax probabilities, the attention output and
+the GELU output — while the residual stream and every accumulation stay
+float32. Together they give the reference forward at the precision the
+benchmarked configuration specifies ("fp16 activations").
 """
 
 from __future__ import annotations
@@ -31,14 +41,17 @@ def packed_to_numpy(layer) -> dict:
     return out
 
 
-def extract_weights(model, dtype=torch.float32) -> dict:
-    """Dense reference weights of a ``rpfq_review_b200.vit.PackedViT``."""
+def extract_weights(model, dtype=torch.float32, fp16: bool = False) -> dict:
+    """Dense reference weights of a ``rpfq_review_b200.vit.PackedViT``
+    (``fp16``: the coefficients rounded through fp16)."""
     w = {"patch_w": model.patch_w.to(dtype).cpu(), "patch_b": model.patch_b.to(dtype).cpu(),
          "cls_tokens": model.cls_tokens.to(dtype).cpu(), "pos_embed": model.pos_embed.to(dtype).cpu(),
          "norm_w": model.norm_w.to(dtype).cpu(), "norm_b": model.norm_b.to(dtype).cpu()}
     for name, mod in model.quantized_linears():
         np_layer = packed_to_numpy(mod.packed())
         dense = pr.dense_weight_from_packed(np_layer, mod.n_c, mod.k_c)
+        if fp16:
+            dense = dense.astype(np.float16).astype(np.float32)
         w[name] = (torch.from_numpy(dense).to(dtype), torch.from_numpy(np_layer["bias"].astype(np.float32)).to(dtype))
     for i, blk in enumerate(model.blocks):
         for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b"):
@@ -46,9 +59,14 @@ def extract_weights(model, dtype=torch.float32) -> dict:
     return w
 
 
-def vit_forward(w: dict, cfg, images: torch.Tensor, act_bits: int = 0) -> torch.Tensor:
-    """Logits ``[B, classes]`` of the reference forward on CPU."""
+def vit_forward(w: dict, cfg, images: torch.Tensor, act_bits: int = 0, fp16_act: bool = False) -> torch.Tensor:
+    """Logits ``[B, classes]`` of the reference forward on CPU (``fp16_act``:
+    the fp16 activations of configs[1], see the module docstring)."""
     dtype = w["patch_w"].dtype
+
+    def r16(t):
+        return t.half().to(t.dtype) if fp16_act else t
+
     x = images.to(dtype)
     B = x.shape[0]
     p = cfg.patch
@@ -67,19 +85,19 @@ def vit_forward(w: dict, cfg, images: torch.Tensor, act_bits: int = 0) -> torch.
 
     L = x.shape[1]
     for i in range(cfg.depth):
-        h = F.layer_norm(x, (d,), w[f"blocks.{i}.norm1_w"], w[f"blocks.{i}.norm1_b"], cfg.eps)
-        qkv = lin(f"blocks.{i}.qkv", h)
+        h = r16(F.layer_norm(x, (d,), w[f"blocks.{i}.norm1_w"], w[f"blocks.{i}.norm1_b"], cfg.eps))
+        qkv = r16(lin(f"blocks.{i}.qkv", h))
         q, k, v = qkv.chunk(3, dim=-1)
         q = q.reshape(B, L, H, hd).transpose(1, 2)
         k = k.reshape(B, L, H, hd).transpose(1, 2)
         v = v.reshape(B, L, H, hd).transpose(1, 2)
-        att = torch.softmax(torch.matmul(q, k.transpose(-2, -1)) * (hd ** -0.5), dim=-1)
-        a = torch.matmul(att, v).transpose(1, 2).reshape(B, L, d)
+        att = r16(torch.softmax(torch.matmul(q, k.transpose(-2, -1)) * (hd ** -0.5), dim=-1))
+        a = r16(torch.matmul(att, v).transpose(1, 2).reshape(B, L, d))
         x = x + lin(f"blocks.{i}.proj", a)
-        h = F.layer_norm(x, (d,), w[f"blocks.{i}.norm2_w"], w[f"blocks.{i}.norm2_b"], cfg.eps)
-        x = x + lin(f"blocks.{i}.fc2", F.gelu(lin(f"blocks.{i}.fc1", h), approximate="none"))
+        h = r16(F.layer_norm(x, (d,), w[f"blocks.{i}.norm2_w"], w[f"blocks.{i}.norm2_b"], cfg.eps))
+        x = x + lin(f"blocks.{i}.fc2", r16(F.gelu(lin(f"blocks.{i}.fc1", h), approximate="none")))
     ntok = 2 if cfg.distilled else 1
-    cls = F.layer_norm(x[:, :ntok], (d,), w["norm_w"], w["norm_b"], cfg.eps)
+    cls = r16(F.layer_norm(x[:, :ntok], (d,), w["norm_w"], w["norm_b"], cfg.eps))
     logits = lin("head", cls[:, 0])
     if cfg.distilled:
         logits = (logits + lin("head_dist", cls[:, 1])) / 2
