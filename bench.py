@@ -86,6 +86,9 @@ def parse():
     ap.add_argument("--code-bits", type=int, default=2, help="phase code width b (3, 4 need --weights synthetic)")
     ap.add_argument("--sweep", action="store_true",
                     help="configs[4] standalone complex-GEMM sweep: M in 256..65536 x K = N in 768/1024/3072/4096")
+    ap.add_argument("--split-sweep", action="store_true",
+                    help="small-M layer shapes (one / eight images, configs[4] M = 256 / 512) with split-K off "
+                         "and automatic, one JSON line each")
     return ap.parse_args()
 
 
@@ -757,6 +760,16 @@ def main():
         for k in (768, 1024, 3072, 4096):
             for m in (256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536):
                 args.gemm = f"{m},{k},{k}"
+                run_gemm(args)
+        return 0
+    if args.split_sweep:
+        shapes = [("198,768,3072", "residual_f32"), ("198,2304,768", "none"), ("198,3072,768", "gelu"),
+                  ("198,768,768", "residual_f32"), ("198,384,1536", "residual_f32"), ("198,1152,384", "none"),
+                  ("1576,768,3072", "residual_f32"), ("1576,768,768", "residual_f32"), ("256,4096,4096", "none"),
+                  ("512,4096,4096", "none"), ("256,3072,3072", "none"), ("256,768,768", "none")]
+        for shape, epi in shapes:
+            for split in (1, 0):
+                args.gemm, args.epilogue, args.split_k = shape, epi, split
                 run_gemm(args)
         return 0
     if args.gemm:
