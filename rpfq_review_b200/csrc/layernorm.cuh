@@ -37,11 +37,15 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     constexpr int VW = D % 128 == 0 ? 4 : (D % 64 == 0 ? 2 : 1);
     constexpr int J = D / (32 * VW);
     const int warps = blockDim.x >> 5;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
+    // Rows are taken last to first: the GEMM that wrote x finished with its
+    // highest row blocks, which are the ones still in L2, and the GEMM that
+    // reads y starts with the lowest rows, the ones written last here.
+    const int64_t slot = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
+    const int64_t row = p.m - 1 - slot;
     const int lane = threadIdx.x & 31;
     pdl_wait();
     pdl_launch_dependents();
-    if (row >= p.m) return;
+    if (slot >= p.m) return;
     int64_t src = row;
     if (p.rows != nullptr) {
         src = p.rows[row];
