@@ -154,6 +154,49 @@ int rpfq_layernorm_rows_sm100(const float* x, int64_t ldx, int64_t x_rows, const
                               const uint16_t* weight, const uint16_t* bias, uint16_t* y, int64_t ldy, int64_t m,
                               int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream);
 
+/* The LayerNorm pass with every row source and output it offers; the two
+ * entry points above are special cases. Row sources (one per output row):
+ *   plain      x[r]
+ *   rows       x[rows[r]] (as rpfq_layernorm_rows_sm100)
+ *   merge_side > 0: Swin PatchMerging (the swin stages' downsample in front of
+ *              the packed `reduction` linear): output row r is token (i, j) of
+ *              image r / (side/2)^2 and concatenates the d/4-wide rows
+ *              (2i, 2j), (2i+1, 2j), (2i, 2j+1), (2i+1, 2j+1) of that image's
+ *              [side, side] grid in x (torch.cat of the four strided slices);
+ *              d % 16 == 0, x_rows >= images * side^2
+ *   add        x[r] + add[add_rows[r]] (add_rows NULL: add[r]): a row-permuted
+ *              residual add, e.g. Swin's window reverse + un-shift + residual
+ *              of the attention branch; needs y32 with y32_prenorm, which then
+ *              receives the updated row (y32 == x: in place). An index outside
+ *              [0, add_bound) records code 902.
+ * Outputs: y (fp16, normalized, activation-quantized with act_bits > 0)
+ * and / or y32 (fp32: the normalized row, or with y32_prenorm the row before
+ * normalization). y32 may alias x only with the plain row mapping. */
+typedef struct RpfqLayerNormArgs {
+    const float* x;           /* fp32 [x_rows, ldx] */
+    int64_t ldx;
+    int64_t x_rows;
+    const int32_t* rows;      /* optional gather */
+    const float* add;         /* optional row-permuted addend [add_bound, ld_add] */
+    int64_t ld_add;
+    int64_t add_bound;
+    const int32_t* add_rows;  /* optional indices into add */
+    const uint16_t* weight;   /* fp16 [d] */
+    const uint16_t* bias;     /* fp16 [d] */
+    uint16_t* y;              /* fp16 [m, ldy] or NULL */
+    int64_t ldy;
+    float* y32;               /* fp32 [m, ldy32] or NULL */
+    int64_t ldy32;
+    int64_t m;
+    int32_t d;
+    float eps;
+    int32_t act_bits;
+    int32_t merge_side;
+    int32_t y32_prenorm;
+    int32_t reserved;
+} RpfqLayerNormArgs;
+int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* args, rpfq_stream_t stream);
+
 /* Whole layer — QATLinearComplexPhase.forward on packed weights
  * (RPFQ-ViT-main/quant_models/quant_i.py:513-554; Android wideLinear,
  * phase_linear.cpp:279-326): optional activation quantization, then the

@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_act_quant_sm100",
     "rpfq_layernorm_sm100",
     "rpfq_layernorm_rows_sm100",
+    "rpfq_layernorm_ex_sm100",
     "rpfq_wide_linear_sm100",
     "rpfq_wide_linear_noalloc_sm100",
     "rpfq_attention_sm100",
@@ -78,6 +79,21 @@ class RpfqGemmArgs(ctypes.Structure):
         ("flags", ctypes.c_int32), ("cta_pair", ctypes.c_int32),
         ("split_k", ctypes.c_int32), ("reserved", ctypes.c_int32),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+class RpfqLayerNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("x_rows", ctypes.c_int64),
+        ("rows", ctypes.c_void_p),
+        ("add", ctypes.c_void_p), ("ld_add", ctypes.c_int64), ("add_bound", ctypes.c_int64),
+        ("add_rows", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("y32", ctypes.c_void_p), ("ldy32", ctypes.c_int64),
+        ("m", ctypes.c_int64), ("d", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("act_bits", ctypes.c_int32), ("merge_side", ctypes.c_int32),
+        ("y32_prenorm", ctypes.c_int32), ("reserved", ctypes.c_int32),
     ]
 
 
@@ -124,6 +140,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_layernorm_rows_sm100.argtypes = [P, I64, I64, P, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
+        L.rpfq_layernorm_ex_sm100.argtypes = [ctypes.POINTER(RpfqLayerNormArgs), P]
         L.rpfq_wide_linear_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_wide_linear_noalloc_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_attention_sm100.argtypes = [P, I64, I32, I32, I32, P, I64, P]
@@ -138,7 +155,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_last_error.restype = ctypes.c_char_p
         L.rpfq_device_error.argtypes = [ctypes.POINTER(I32)]
         for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
-                     "rpfq_layernorm_rows_sm100",
+                     "rpfq_layernorm_rows_sm100", "rpfq_layernorm_ex_sm100",
                      "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_pack_linear_sm100",
                      "rpfq_vision_act_quant_sm100", "rpfq_attention_sm100",
                      "rpfq_device_error",

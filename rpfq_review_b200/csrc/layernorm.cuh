@@ -16,19 +16,36 @@
 namespace rpfq {
 
 struct LayerNormParams {
-    const float* x;
+    const float* x;       // [x_rows, ldx] fp32
     const __half* w;
     const __half* b;
-    __half* y;
-    int64_t ldx, ldy;
+    __half* y;            // fp16 output [m, ldy], or nullptr
+    float* y32;           // fp32 output [m, ldy32], or nullptr (may be x: in-place, plain row mapping only)
+    int64_t ldx, ldy, ldy32;
     int64_t m;
     float eps;
     int32_t act_bits;
     const int32_t* rows;  // optional gather: output row r normalizes input row rows[r]
     int64_t x_rows;       // rows of x (gather indices outside [0, x_rows) are rejected)
+    const float* add;     // optional: the row is x[r] + add[add_rows[r]] (a row-permuted residual add)
+    const int32_t* add_rows;
+    int64_t ld_add, add_bound;
+    int32_t y32_prenorm;  // y32 receives the row before normalization (the updated residual) instead of after
+    int32_t merge_side;   // > 0: 2x2 patch merging of a [images, side, side, D / 4] grid (see below)
     int* err;
 };
 
+// One warp per output row. Row sources:
+//   plain        x[row]
+//   rows         x[rows[row]] (Swin's cyclic shift + window partition)
+//   merge_side   the concatenation of the four D/4-wide rows (2i, 2j), (2i+1, 2j),
+//                (2i, 2j+1), (2i+1, 2j+1) of image row / (side/2)^2 of the
+//                [side, side] token grid, (i, j) = that image's merged token
+//                (Swin PatchMerging's strided slices and concatenation)
+//   add          plus add[add_rows[row]] (Swin's window reverse + un-shift +
+//                residual add of the attention branch)
+// Outputs: fp16 y (normalized, optionally activation-quantized) and / or
+// fp32 y32 (normalized, or with y32_prenorm the row before normalization).
 template <int D>
 __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormParams p) {
     static_assert(D % 32 == 0, "row length must be a multiple of 32");
@@ -46,35 +63,86 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     pdl_wait();
     pdl_launch_dependents();
     if (slot >= p.m) return;
-    int64_t src = row;
-    if (p.rows != nullptr) {
-        src = p.rows[row];
-        if (src < 0 || src >= p.x_rows) {  // bad gather index: report, touch nothing
-            if ((threadIdx.x & 31) == 0) atomicCAS(p.err, 0, 901);
+    // source row of each quarter of the output row (all four equal unless merging)
+    int64_t src[4];
+    if (p.merge_side > 0) {
+        const int64_t half = p.merge_side >> 1;
+        const int64_t img = row / (half * half), t = row - img * half * half;
+        const int64_t i = t / half, j = t - i * half;
+        const int64_t base = img * p.merge_side * p.merge_side + 2 * i * p.merge_side + 2 * j;
+        src[0] = base;
+        src[1] = base + p.merge_side;
+        src[2] = base + 1;
+        src[3] = base + p.merge_side + 1;
+    } else {
+        int64_t s0 = row;
+        if (p.rows != nullptr) {
+            s0 = p.rows[row];
+            if (s0 < 0 || s0 >= p.x_rows) {  // bad gather index: report, touch nothing
+                if (lane == 0) atomicCAS(p.err, 0, 901);
+                return;
+            }
+        }
+        src[0] = src[1] = src[2] = src[3] = s0;
+    }
+    const float* ar = nullptr;
+    if (p.add != nullptr) {
+        const int64_t a = p.add_rows != nullptr ? p.add_rows[row] : row;
+        if (a < 0 || a >= p.add_bound) {
+            if (lane == 0) atomicCAS(p.err, 0, 902);
             return;
         }
+        ar = p.add + a * p.ld_add;
     }
-    const float* xr = p.x + src * p.ldx;
     float v[J][VW];
     float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const int col = 32 * VW * j + VW * lane;
+        const int q = col / (D / 4);  // quarter (VW divides D / 4 whenever merging is allowed)
+        const int64_t sq = q == 0 ? src[0] : (q == 1 ? src[1] : (q == 2 ? src[2] : src[3]));
+        const float* xr = p.x + sq * p.ldx + (p.merge_side > 0 ? col - q * (D / 4) : col);
         if constexpr (VW == 4) {
-            const float4 t = *reinterpret_cast<const float4*>(xr + col);
+            float4 t = *reinterpret_cast<const float4*>(xr);
+            if (ar != nullptr) {
+                const float4 u = *reinterpret_cast<const float4*>(ar + col);
+                t.x += u.x;
+                t.y += u.y;
+                t.z += u.z;
+                t.w += u.w;
+            }
             v[j][0] = t.x;
             v[j][1] = t.y;
             v[j][2] = t.z;
             v[j][3] = t.w;
             sum += (t.x + t.y) + (t.z + t.w);
         } else if constexpr (VW == 2) {
-            const float2 t = *reinterpret_cast<const float2*>(xr + col);
+            float2 t = *reinterpret_cast<const float2*>(xr);
+            if (ar != nullptr) {
+                const float2 u = *reinterpret_cast<const float2*>(ar + col);
+                t.x += u.x;
+                t.y += u.y;
+            }
             v[j][0] = t.x;
             v[j][1] = t.y;
             sum += t.x + t.y;
         } else {
-            v[j][0] = xr[col];
+            v[j][0] = xr[0] + (ar != nullptr ? ar[col] : 0.0f);
             sum += v[j][0];
+        }
+    }
+    if (p.y32 != nullptr && p.y32_prenorm) {
+        // the updated residual row (in place when y32 == x: this warp has read its whole row)
+        float* zr = p.y32 + row * p.ldy32;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const int col = 32 * VW * j + VW * lane;
+            if constexpr (VW == 4)
+                *reinterpret_cast<float4*>(zr + col) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+            else if constexpr (VW == 2)
+                *reinterpret_cast<float2*>(zr + col) = make_float2(v[j][0], v[j][1]);
+            else
+                zr[col] = v[j][0];
         }
     }
 #pragma unroll
@@ -122,6 +190,20 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
                 amax_im = fmaxf(amax_im, a);
         }
     }
+    if (p.y32 != nullptr && !p.y32_prenorm) {
+        float* zr = p.y32 + row * p.ldy32;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const int col = 32 * VW * j + VW * lane;
+            if constexpr (VW == 4)
+                *reinterpret_cast<float4*>(zr + col) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+            else if constexpr (VW == 2)
+                *reinterpret_cast<float2*>(zr + col) = make_float2(v[j][0], v[j][1]);
+            else
+                zr[col] = v[j][0];
+        }
+    }
+    if (p.y == nullptr) return;
     float s_re = 0.0f, s_im = 0.0f, qmax = 0.0f, qmin = 0.0f;
     if (p.act_bits > 0) {
 #pragma unroll

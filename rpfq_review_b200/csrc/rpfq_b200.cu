@@ -733,33 +733,86 @@ int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, co
 int rpfq_layernorm_rows_sm100(const float* x, int64_t ldx, int64_t x_rows, const int32_t* rows,
                               const uint16_t* weight, const uint16_t* bias, uint16_t* y, int64_t ldy, int64_t m,
                               int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream) {
-    if (rows != nullptr && ((reinterpret_cast<uintptr_t>(rows) & 3) || x_rows < 0))
+    if (!y) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: null pointer");
+    RpfqLayerNormArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.x = x;
+    a.ldx = ldx;
+    a.x_rows = x_rows;
+    a.rows = rows;
+    a.weight = weight;
+    a.bias = bias;
+    a.y = y;
+    a.ldy = ldy;
+    a.m = m;
+    a.d = d;
+    a.eps = eps;
+    a.act_bits = act_bits;
+    return rpfq_layernorm_ex_sm100(&a, stream);
+}
+
+int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* a, rpfq_stream_t stream) {
+    if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: null args");
+    const int32_t d = a->d;
+    const int64_t m = a->m;
+    if (a->rows != nullptr && ((reinterpret_cast<uintptr_t>(a->rows) & 3) || a->x_rows < 0))
         return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_rows_sm100: rows must be 4-byte aligned, x_rows >= 0");
-    if (!x || !weight || !bias || !y) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: null pointer");
-    if (m < 0 || ldx < d || ldy < d || ldx % 4 || ldy % 4)
+    if (!a->x || !a->weight || !a->bias || (!a->y && !a->y32))
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: null pointer (x, weight, bias and y or y32 are required)");
+    if (m < 0 || a->ldx < (a->merge_side > 0 ? d / 4 : d) || a->ldx % 4 || (a->y && (a->ldy < d || a->ldy % 4)) ||
+        (a->y32 && (a->ldy32 < d || a->ldy32 % 4)))
         return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: bad shape or stride (strides must be multiples of 4)");
-    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(y) & 7) || (reinterpret_cast<uintptr_t>(weight) & 7) ||
-        (reinterpret_cast<uintptr_t>(bias) & 7))
-        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: x must be 16-byte and y, weight, bias 8-byte aligned");
-    if (act_bits != 0 && (act_bits < 2 || act_bits > 8))
-        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: act_bits must be 0 or 2..8 (got %d)", act_bits);
+    if (!aligned16(a->x) || (a->y && (reinterpret_cast<uintptr_t>(a->y) & 7)) || (a->y32 && !aligned16(a->y32)) ||
+        (reinterpret_cast<uintptr_t>(a->weight) & 7) || (reinterpret_cast<uintptr_t>(a->bias) & 7))
+        return fail(RPFQ_ERR_INVALID,
+                    "rpfq_layernorm_sm100: x and y32 must be 16-byte and y, weight, bias 8-byte aligned");
+    if (a->act_bits != 0 && (a->act_bits < 2 || a->act_bits > 8))
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: act_bits must be 0 or 2..8 (got %d)", a->act_bits);
     if (d % 2) return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_sm100: odd row length %d", d);
+    if (a->merge_side < 0 || a->merge_side % 2)
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_ex_sm100: merge_side must be 0 or even (got %d)", a->merge_side);
+    if (a->merge_side > 0) {
+        const int64_t half = a->merge_side / 2;
+        if (a->rows || a->add || d % 16 || m % (half * half) ||
+            a->x_rows < (m / (half * half)) * a->merge_side * a->merge_side)
+            return fail(RPFQ_ERR_INVALID,
+                        "rpfq_layernorm_ex_sm100: patch merging needs no gather / add, d %% 16 == 0, m a multiple of "
+                        "(side/2)^2 and x_rows >= images * side^2");
+    }
+    if (a->add) {
+        if (a->rows || !a->y32 || !a->y32_prenorm || a->ld_add < d || a->ld_add % 4 || !aligned16(a->add) ||
+            (a->add_rows && (reinterpret_cast<uintptr_t>(a->add_rows) & 3)) || a->add_bound < 0)
+            return fail(RPFQ_ERR_INVALID,
+                        "rpfq_layernorm_ex_sm100: add needs no gather, y32 with y32_prenorm, a 16-byte aligned add "
+                        "with ld_add >= d (a multiple of 4) and 4-byte aligned add_rows");
+    }
+    if (a->y32 && static_cast<const void*>(a->y32) == static_cast<const void*>(a->x) &&
+        (a->rows || a->merge_side || a->ldy32 != a->ldx))
+        return fail(RPFQ_ERR_INVALID, "rpfq_layernorm_ex_sm100: y32 may alias x only with the plain row mapping");
     if (m == 0) return RPFQ_OK;
     DeviceState* st;
     int rc = device_state(&st);
     if (rc) return rc;
     LayerNormParams p;
-    p.x = x;
-    p.w = reinterpret_cast<const __half*>(weight);
-    p.b = reinterpret_cast<const __half*>(bias);
-    p.y = reinterpret_cast<__half*>(y);
-    p.ldx = ldx;
-    p.ldy = ldy;
+    p.x = a->x;
+    p.w = reinterpret_cast<const __half*>(a->weight);
+    p.b = reinterpret_cast<const __half*>(a->bias);
+    p.y = reinterpret_cast<__half*>(a->y);
+    p.y32 = a->y32;
+    p.ldx = a->ldx;
+    p.ldy = a->ldy;
+    p.ldy32 = a->ldy32;
     p.m = m;
-    p.eps = eps;
-    p.act_bits = act_bits;
-    p.rows = rows;
-    p.x_rows = x_rows;
+    p.eps = a->eps;
+    p.act_bits = a->act_bits;
+    p.rows = a->rows;
+    p.x_rows = a->rows ? a->x_rows : 0;
+    p.add = a->add;
+    p.add_rows = a->add_rows;
+    p.ld_add = a->ld_add;
+    p.add_bound = a->add_rows ? a->add_bound : m;
+    p.y32_prenorm = a->y32_prenorm ? 1 : 0;
+    p.merge_side = a->merge_side;
     p.err = st->err_word;
     const int warps = 8;
     const int64_t blocks = (m + warps - 1) / warps;

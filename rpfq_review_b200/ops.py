@@ -325,6 +325,60 @@ def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: fl
     return out
 
 
+def layernorm_ex(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, act_bits: int = 0, *,
+                 rows: torch.Tensor | None = None, merge_side: int = 0, add: torch.Tensor | None = None,
+                 add_rows: torch.Tensor | None = None, out: torch.Tensor | None = None, fp16_out: bool = True,
+                 out32: torch.Tensor | None = None, out32_prenorm: bool = False):
+    """The LayerNorm pass with all its row sources and outputs
+    (``rpfq_layernorm_ex_sm100``); returns ``(fp16 output or None, fp32
+    output or None)``.
+
+    Row sources: ``x`` rows as they are; ``rows`` gathers (output row r is
+    input row ``rows[r]``); ``merge_side`` = s > 0 is Swin's 2x2 patch merging
+    of an ``x`` of ``[images * s * s, c]`` tokens into ``[images * (s/2)^2, 4c]``
+    rows; ``add`` adds ``add[add_rows[r]]`` (or ``add[r]``) to row r before the
+    normalization and needs ``out32`` with ``out32_prenorm=True``, which then
+    receives the updated rows (``out32`` may be ``x``: in place). ``out32``
+    without ``out32_prenorm`` receives the normalized rows in fp32."""
+    if not x.is_cuda or x.dtype != torch.float32:
+        raise ValueError("layernorm: x must be a float32 CUDA tensor")
+    _require(weight, "weight")
+    _require(bias, "bias")
+    c = x.shape[-1]
+    x2, ldx = _rows(x, c, "x")
+    if merge_side:
+        d, m = 4 * c, x2.shape[0] // 4
+    else:
+        d, m = c, (rows.numel() if rows is not None else x2.shape[0])
+    if rows is not None:
+        _require(rows, "rows", torch.int32)
+    if fp16_out and out is None:
+        out = torch.empty((m, d), dtype=torch.float16, device=x.device)
+    y2, ldy = _rows(out, d, "out") if out is not None else (None, 0)
+    z2, ldz = _rows(out32, d, "out32") if out32 is not None else (None, 0)
+    for t in (y2, z2):
+        if t is not None and t.shape[0] != m:
+            raise ValueError(f"layernorm: the outputs must have {m} rows")
+    a2, lda = (None, 0)
+    if add is not None:
+        if not add.is_cuda or add.dtype != torch.float32:
+            raise ValueError("layernorm: add must be a float32 CUDA tensor")
+        a2, lda = _rows(add, d, "add")
+    if add_rows is not None:
+        _require(add_rows, "add_rows", torch.int32)
+    args = _lib.RpfqLayerNormArgs(
+        x=x2.data_ptr(), ldx=ldx, x_rows=x2.shape[0], rows=_p(rows), add=_p(a2), ld_add=lda,
+        add_bound=a2.shape[0] if a2 is not None else 0, add_rows=_p(add_rows), weight=weight.data_ptr(),
+        bias=bias.data_ptr(), y=_p(y2), ldy=ldy, y32=_p(z2), ldy32=ldz, m=m, d=d, eps=float(eps),
+        act_bits=int(act_bits), merge_side=int(merge_side), y32_prenorm=int(bool(out32_prenorm)))
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().rpfq_layernorm_ex_sm100(ctypes.byref(args), _stream(x.device)),
+                   "rpfq_layernorm_ex_sm100")
+    if m:
+        _count_launch()
+    return out, out32
+
+
 def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Per-row symmetric quantization of the Re / Im halves (ActivationQuantSTE)."""
     _require(x, "x")

@@ -14,10 +14,13 @@ stages (2x2 neighbourhood concatenated in the order (0,0), (1,0), (0,1),
 tokens, head.
 
 On the GPU the packed linears run the tcgen05 GEMM with bias, GELU (fc1) and
-the residual add (fc2) fused; LayerNorm (+ activation quantization) is the
-``rpfq_layernorm_rows_sm100`` kernel, whose row gather also performs the
-cyclic shift and the window partition; the attention output returns to the
-residual stream through one ``index_add_`` scatter; window attention is
+the residual add (fc2) fused. Every LayerNorm (+ activation quantization) is
+one pass of the ``rpfq_layernorm_ex_sm100`` kernel, whose row sources carry
+the token bookkeeping: the norm1 pass gathers rows into the shifted window
+order; the norm2 pass adds the attention branch (window order) back into the
+residual stream through the inverse gather, in place, and normalizes the
+updated rows; the patch-merging pass gathers the 2x2 neighbourhoods; the
+patch-embedding norm writes the fp32 residual stream. Window attention is
 PyTorch SDPA with the relative-position bias (and shift mask) as an additive
 mask.
 """
@@ -156,8 +159,8 @@ class PackedSwin(nn.Module):
         c0 = cfg.embed
         self.register_buffer("patch_w", _trunc_normal((c0, pdim), 0.02, g).half().to(dev))
         self.register_buffer("patch_b", torch.zeros(c0, dtype=torch.float16, device=dev))
-        self.register_buffer("patch_norm_w", torch.ones(c0, device=dev))
-        self.register_buffer("patch_norm_b", torch.zeros(c0, device=dev))
+        self.register_buffer("patch_norm_w", torch.ones(c0, dtype=torch.float16, device=dev))
+        self.register_buffer("patch_norm_b", torch.zeros(c0, dtype=torch.float16, device=dev))
 
         def make(name, n_out, n_in, activation="none"):
             gl = torch.Generator().manual_seed(layer_seed(name, seed))
@@ -234,8 +237,11 @@ class PackedSwin(nn.Module):
         return m
 
     def orders(self, s: int, shift: int, batch: int):
-        """(perm [R*R] int64, rows [B*R*R] int32) of stage s: the window order
-        of the tokens and its per-image row gather for the LayerNorm kernel."""
+        """(perm [R*R] int64, rows [B*R*R] int32, inverse [B*R*R] int32) of
+        stage s: the window order of the tokens, its per-image row gather for
+        the LayerNorm kernel (window-order row -> natural row) and the inverse
+        gather (natural row -> window-order row) that brings the attention
+        branch back into the residual stream."""
         key = (s, shift, batch)
         o = self._orders.get(key)
         if o is None:
@@ -244,8 +250,10 @@ class PackedSwin(nn.Module):
             ws, _ = cfg.stage_window(s)
             dev = self.patch_w.device
             perm = window_order(r, ws, shift).to(dev)
-            rows = (torch.arange(batch, device=dev)[:, None] * (r * r) + perm[None]).reshape(-1).to(torch.int32)
-            o = (perm, rows)
+            base = torch.arange(batch, device=dev)[:, None] * (r * r)
+            rows = (base + perm[None]).reshape(-1).to(torch.int32)
+            inverse = (base + torch.argsort(perm)[None]).reshape(-1).to(torch.int32)
+            o = (perm, rows, inverse)
             self._orders[key] = o
         return o
 
@@ -264,14 +272,16 @@ class PackedSwin(nn.Module):
         B = images.shape[0]
         dims, res = cfg.dims(), cfg.resolutions()
         emb = ops.gemm(self.patchify(images.to(torch.float16)), self.patch_w, self.patch_b, out_dtype=torch.float32)
-        x = F.layer_norm(emb, (dims[0],), self.patch_norm_w, self.patch_norm_b, cfg.eps)
+        # patch-embedding LayerNorm in place: the residual stream starts as its fp32 output
+        ops.layernorm_ex(emb, self.patch_norm_w, self.patch_norm_b, cfg.eps, fp16_out=False, out32=emb)
+        x = emb
         for s, stage in enumerate(self.stages):
             c, nh, r = dims[s], cfg.heads[s], res[s]
             hd = c // nh
             ws, shift = cfg.stage_window(s)
             for i, blk in enumerate(stage.blocks):
                 sh = shift if i % 2 == 1 else 0
-                perm, rows = self.orders(s, sh, B)
+                _, rows, inverse = self.orders(s, sh, B)
                 # LayerNorm writes the tokens already shifted and window-partitioned
                 win = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab, rows=rows).view(-1, ws * ws, c)
                 qkv = blk.qkv(win, prequantized=True)
@@ -279,16 +289,15 @@ class PackedSwin(nn.Module):
                 a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=self.attn_mask(s, i, B))
                 a = a.transpose(1, 2).reshape(win.shape[0], ws * ws, c)
                 o = blk.proj(a, out_dtype=torch.float32)
-                # un-partition, un-shift and add to the residual stream in one scatter
-                x.index_add_(1, perm, o.view(B, r * r, c))
-                h = ops.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab)
-                blk.fc2(blk.fc1(h, prequantized=True), residual=x, out=x)
+                # un-partition, un-shift and add to the residual stream (in place) in
+                # the LayerNorm pass that also produces the MLP input
+                h, _ = ops.layernorm_ex(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab, add=o.view(-1, c),
+                                        add_rows=inverse, out32=x, out32_prenorm=True)
+                blk.fc2(blk.fc1(h.view(B, r * r, c), prequantized=True), residual=x, out=x)
             if hasattr(stage, "reduction"):
-                xs = x.view(B, r, r, c)
-                cat = torch.cat([xs[:, 0::2, 0::2], xs[:, 1::2, 0::2], xs[:, 0::2, 1::2], xs[:, 1::2, 1::2]], dim=-1)
-                h = ops.layernorm(cat.reshape(B, (r // 2) ** 2, 4 * c), stage.merge_norm_w, stage.merge_norm_b,
-                                  cfg.eps, ab)
-                x = stage.reduction(h, out_dtype=torch.float32, prequantized=True)
+                # patch merging: the 2x2 neighbourhood concatenation rides on the LayerNorm's row gather
+                h, _ = ops.layernorm_ex(x, stage.merge_norm_w, stage.merge_norm_b, cfg.eps, ab, merge_side=r)
+                x = stage.reduction(h.view(B, (r // 2) ** 2, 4 * c), out_dtype=torch.float32, prequantized=True)
         h = ops.layernorm(x, self.norm_w, self.norm_b, cfg.eps)
         pooled = h.float().mean(dim=1).to(torch.float16)
         return self.head(pooled, out_dtype=torch.float32)

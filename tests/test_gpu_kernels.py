@@ -398,6 +398,73 @@ def test_layernorm_row_gather(cuda):
     assert torch.count_nonzero(out[10]) == 0
 
 
+@pytest.mark.parametrize("c,side,act_bits", [(96, 56, 0), (192, 28, 4), (384, 14, 0)])
+def test_layernorm_patch_merge_gather(cuda, c, side, act_bits):
+    """rpfq_layernorm_ex_sm100 with merge_side: bit-identical to the plain
+    kernel on torch's concatenation of the four strided slices (Swin
+    PatchMerging), for the three Swin-T merges."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(c)
+    B = 3
+    x = torch.randn(B, side * side, c, generator=g).to(cuda)
+    w = (torch.randn(4 * c, generator=g) * 0.2 + 1).half().to(cuda)
+    b = (torch.randn(4 * c, generator=g) * 0.1).half().to(cuda)
+    xs = x.view(B, side, side, c)
+    cat = torch.cat([xs[:, 0::2, 0::2], xs[:, 1::2, 0::2], xs[:, 0::2, 1::2], xs[:, 1::2, 1::2]], dim=-1)
+    want = ops.layernorm(cat.reshape(-1, 4 * c).contiguous(), w, b, 1e-5, act_bits=act_bits)
+    got, _ = ops.layernorm_ex(x, w, b, 1e-5, act_bits, merge_side=side)
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("d", [96, 384, 768])
+def test_layernorm_permuted_residual_add(cuda, d):
+    """rpfq_layernorm_ex_sm100 with add / add_rows and an in-place y32: the
+    residual stream becomes x + add[add_rows] (exactly: one fp32 add per
+    element) and the fp16 output is the plain kernel's LayerNorm of it; an
+    add index outside [0, add_bound) is reported as code 902."""
+    from rpfq_review_b200 import _lib
+    ops = _ops()
+    g = torch.Generator().manual_seed(d)
+    m = 2 * 3136
+    x = torch.randn(m, d, generator=g).to(cuda)
+    o = torch.randn(m, d, generator=g).to(cuda)
+    w = (torch.randn(d, generator=g) * 0.2 + 1).half().to(cuda)
+    b = (torch.randn(d, generator=g) * 0.1).half().to(cuda)
+    inv = torch.randperm(m, generator=g).to(torch.int32).to(cuda)
+    want_x = x + o[inv.long()]
+    want_h = ops.layernorm(want_x, w, b, 1e-5, act_bits=4)
+    xs = x.clone()
+    h, z = ops.layernorm_ex(xs, w, b, 1e-5, 4, add=o, add_rows=inv, out32=xs, out32_prenorm=True)
+    assert z.data_ptr() == xs.data_ptr()
+    assert torch.equal(xs, want_x)
+    assert torch.equal(h, want_h)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    bad = inv.clone()
+    bad[7] = m
+    ops.layernorm_ex(x.clone(), w, b, 1e-5, add=o, add_rows=bad, out32=torch.zeros_like(x), out32_prenorm=True)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 902
+
+
+@pytest.mark.parametrize("d", [96, 768])
+def test_layernorm_fp32_output(cuda, d):
+    """fp32 output of the normalized rows (Swin's patch-embedding norm, in
+    place): within fp32 rounding of torch's LayerNorm, and its fp16 rounding
+    equals the kernel's own fp16 output."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(d + 1)
+    x = torch.randn(4096, d, generator=g).to(cuda) * 3 + 1
+    w = (torch.randn(d, generator=g) * 0.2 + 1).half().to(cuda)
+    b = (torch.randn(d, generator=g) * 0.1).half().to(cuda)
+    ref = torch.nn.functional.layer_norm(x.double(), (d,), w.double(), b.double(), 1e-5)
+    h16 = ops.layernorm(x, w, b, 1e-5)
+    y = x.clone()
+    ops.layernorm_ex(y, w, b, 1e-5, fp16_out=False, out32=y)
+    assert float((y.double() - ref).abs().max()) < 1e-5
+    assert torch.equal(y.half(), h16)
+
+
 def test_gelu_epilogue_accuracy(cuda):
     """The epilogue's GELU (A&S 7.1.26 erf, |error| <= 1.5e-7, with the SFU
     reciprocal and exp2) against float64 exact-erf GELU, read through an
