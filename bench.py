@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--act-bits", type=int, default=0)
     ap.add_argument("--attention", default="sdpa", choices=["sdpa", "rpfq"],
                     help="ViT / DeiT attention: PyTorch SDPA (cuDNN) or the library's tcgen05 kernel")
+    ap.add_argument("--swin-attention", default="rpfq", choices=["sdpa", "rpfq"],
+                    help="Swin window attention: the library's tcgen05 kernel or PyTorch SDPA with the bias mask")
     ap.add_argument("--vision-quant", action="store_true",
                     help="every packed linear uses the vision-aware (token-saliency, int8) activation quantizer")
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -270,7 +272,8 @@ def build_model(cfg, device, args, prepack: bool = True):
     if isinstance(cfg, SwinConfig):
         if args.weights != "random_init" or args.code_bits != 2 or args.vision_quant:
             raise SystemExit("Swin runs random-init 2-bit weights with the standard activation path only")
-        return PackedSwin(cfg, device, seed=0, act_bits=args.act_bits, prepack=prepack)
+        return PackedSwin(cfg, device, seed=0, act_bits=args.act_bits, prepack=prepack,
+                          attention=args.swin_attention)
     vq = dict(salient_token_ratio=0.25, background_clip_ratio=0.75, energy_score_weight=0.5,
               protect_cls_token=True) if args.vision_quant else None
     return PackedViT(cfg, device, seed=0, act_bits=args.act_bits, weights=args.weights, code_bits=args.code_bits,

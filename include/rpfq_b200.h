@@ -239,6 +239,21 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* args, rpfq_stream_t stream)
 int rpfq_attention_sm100(const uint16_t* qkv, int64_t images, int32_t tokens, int32_t heads, int32_t head_dim,
                          uint16_t* out, int64_t ldo, rpfq_stream_t stream);
 
+/* Swin window attention (7x7 windows, head dim 32): for every window w and
+ * head h, softmax(q k^T / sqrt(32) + bias) v over the window's 49 tokens, the
+ * attention of the timm Swin blocks the reference wraps
+ * (RPFQ-ViT-main/quant_models/quant_rpfq_swin.py:64-91). qkv is the qkv
+ * GEMM output in window order, [windows * 49, 3 * 32 * heads] fp16 (row =
+ * token: q heads, k heads, v heads); out[windows * 49, ldo] receives the heads
+ * concatenated (the proj GEMM's input). bias_mask is fp32
+ * [bm_windows, heads, 16, 49, 4]: log2(e) * (relative position bias + shift
+ * mask) of query row i and key column j at [.., j / 4, i, j % 4], -inf for
+ * the padding keys 49..63; window w uses entry w % bm_windows (1 for unshifted
+ * blocks, the windows per image for shifted ones). */
+int rpfq_window_attention_sm100(const uint16_t* qkv, int64_t windows, int32_t heads, int32_t head_dim,
+                                int32_t window_tokens, const float* bias_mask, int32_t bm_windows, uint16_t* out,
+                                int64_t ldo, rpfq_stream_t stream);
+
 /* Vision-aware activation quantization of `images` x `tokens` rows of fp16
  * x[row] = [Re | Im] (k = 2 k_c columns, k_c a multiple of 8) into xq (may
  * alias x): the reference's VisionAwareActivationQuantizer.forward

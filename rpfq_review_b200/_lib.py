@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_wide_linear_sm100",
     "rpfq_wide_linear_noalloc_sm100",
     "rpfq_attention_sm100",
+    "rpfq_window_attention_sm100",
     "rpfq_vision_workspace_bytes",
     "rpfq_vision_act_quant_sm100",
     "rpfq_pack_workspace_bytes",
@@ -144,6 +145,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_wide_linear_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_wide_linear_noalloc_sm100.argtypes = [ctypes.POINTER(RpfqWideLinearArgs), P]
         L.rpfq_attention_sm100.argtypes = [P, I64, I32, I32, I32, P, I64, P]
+        L.rpfq_window_attention_sm100.argtypes = [P, I64, I32, I32, I32, P, I32, P, I64, P]
         L.rpfq_vision_workspace_bytes.argtypes = [I64, I32]
         L.rpfq_vision_workspace_bytes.restype = ctypes.c_uint64
         L.rpfq_vision_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, ctypes.c_double, ctypes.c_double,
@@ -157,7 +159,7 @@ def lib() -> ctypes.CDLL:
         for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
                      "rpfq_layernorm_rows_sm100", "rpfq_layernorm_ex_sm100",
                      "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_pack_linear_sm100",
-                     "rpfq_vision_act_quant_sm100", "rpfq_attention_sm100",
+                     "rpfq_vision_act_quant_sm100", "rpfq_attention_sm100", "rpfq_window_attention_sm100",
                      "rpfq_device_error",
                      "rpfq_version"):
             getattr(L, name).restype = ctypes.c_int

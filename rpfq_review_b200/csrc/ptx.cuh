@@ -171,6 +171,15 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* s
                  : "memory");
 }
 
+// 1-D bulk copy global -> this CTA's shared memory, completing on an mbarrier
+// (16-byte aligned addresses, size a multiple of 16). No multicast.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Fire-and-forget prefetch of a contiguous global range into L2 (16-B aligned,

@@ -20,6 +20,7 @@
 #include "../../include/rpfq_b200.h"
 #include "actquant.cuh"
 #include "attention.cuh"
+#include "window_attention.cuh"
 #include "decode_gemm.cuh"
 #include "gemm.cuh"
 #include "layernorm.cuh"
@@ -886,6 +887,56 @@ int rpfq_attention_sm100(const uint16_t* qkv, int64_t images, int32_t tokens, in
     const int64_t items = images * heads;
     const int grid = static_cast<int>(std::min<int64_t>(items, st->sm_count));
     RPFQ_CUDA(launch_kernel(attn_short_sm100_kernel, dim3(grid), dim3(AttnCfg::THREADS), AttnCfg::SMEM_BYTES,
+                            static_cast<cudaStream_t>(stream), 1, tm, p));
+    return RPFQ_OK;
+}
+
+int rpfq_window_attention_sm100(const uint16_t* qkv, int64_t windows, int32_t heads, int32_t head_dim,
+                                int32_t window_tokens, const float* bias_mask, int32_t bm_windows, uint16_t* out,
+                                int64_t ldo, rpfq_stream_t stream) {
+    using C = WinAttnCfg;
+    if (!qkv || !out || !bias_mask) return fail(RPFQ_ERR_INVALID, "rpfq_window_attention_sm100: null pointer");
+    if (head_dim != C::HD || window_tokens != C::L)
+        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_window_attention_sm100: head_dim %d / %d tokens per window "
+                    "(supported: 32 / 49, the 7x7 windows of Swin)", head_dim, window_tokens);
+    if (windows < 0 || heads <= 0 || bm_windows <= 0 || heads > 4096)
+        return fail(RPFQ_ERR_INVALID, "rpfq_window_attention_sm100: bad shape (windows %lld, heads %d, bm_windows %d)",
+                    (long long)windows, heads, bm_windows);
+    const int64_t d = static_cast<int64_t>(heads) * head_dim;
+    if (ldo < d || ldo % 8 || !aligned16(qkv) || !aligned16(out) || !aligned16(bias_mask))
+        return fail(RPFQ_ERR_INVALID,
+                    "rpfq_window_attention_sm100: 16-byte aligned qkv, out and bias_mask, ldo >= heads * 32, ldo %% 8 == 0");
+    if (windows * C::L > 0x7fffffff - 128)
+        return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_window_attention_sm100: too many windows");
+    if (windows == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr[kMaxDevices];
+    int dev = 0;
+    RPFQ_CUDA(cudaGetDevice(&dev));
+    std::call_once(once[dev], [dev]() {
+        attr[dev] = cudaFuncSetAttribute(attn_window_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         WinAttnCfg::SMEM_BYTES);
+    });
+    RPFQ_CUDA(attr[dev]);
+    // qkv [windows * 49, 3 d], [64 rows x 64 columns] boxes (128-B swizzle)
+    CUtensorMap tm;
+    rc = make_tmap_f16(&tm, qkv, windows * C::L, 3 * d, 3 * d, C::LP, 64);
+    if (rc) return rc;
+    WinAttnParams p;
+    p.bias_mask = bias_mask;
+    p.out = reinterpret_cast<__half*>(out);
+    p.ldo = ldo;
+    p.windows = static_cast<int32_t>(windows);
+    p.heads = heads;
+    p.bm_windows = bm_windows;
+    p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
+    p.err = st->err_word;
+    const int64_t items = ((windows + 1) / 2) * ((heads + 1) / 2);
+    const int grid = static_cast<int>(std::min<int64_t>(items, st->sm_count));
+    RPFQ_CUDA(launch_kernel(attn_window_sm100_kernel, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES,
                             static_cast<cudaStream_t>(stream), 1, tm, p));
     return RPFQ_OK;
 }

@@ -156,6 +156,58 @@ def attention(qkv: torch.Tensor, heads: int, out: torch.Tensor | None = None) ->
     return out
 
 
+WINDOW_TOKENS = 49  # 7 x 7 Swin windows
+WINDOW_HEAD_DIM = 32
+
+
+def window_bias_layout(bias: torch.Tensor) -> torch.Tensor:
+    """``[bm_windows, heads, 49, 49]`` additive attention bias (relative
+    position bias + shift mask, natural units) -> the float32
+    ``[bm_windows, heads, 16, 49, 4]`` operand of :func:`window_attention`
+    (scaled by log2(e), -inf in the padding keys)."""
+    n, h, L, L2 = bias.shape
+    if L != WINDOW_TOKENS or L2 != WINDOW_TOKENS:
+        raise ValueError("window_bias_layout: expects [bm_windows, heads, 49, 49]")
+    full = torch.full((n, h, L, 64), float("-inf"), dtype=torch.float32, device=bias.device)
+    full[..., :L] = bias.float() * 1.4426950408889634
+    return full.view(n, h, L, 16, 4).permute(0, 1, 3, 2, 4).contiguous()
+
+
+def window_attention(qkv: torch.Tensor, heads: int, bias_mask: torch.Tensor,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Swin window attention (``rpfq_window_attention_sm100``): ``qkv`` is the
+    qkv GEMM output in window order, fp16 ``[windows * 49, 3 * 32 * heads]``;
+    ``bias_mask`` fp32 ``[bm_windows, heads, 16, 49, 4]`` holds log2(e) times
+    the relative position bias (+ shift mask) of query row i and key column j
+    at ``[..., j // 4, i, j % 4]``, -inf in key columns 49..63 (window w uses
+    entry ``w % bm_windows``; :func:`window_bias_layout` builds it from
+    ``[bm_windows, heads, 49, 49]``). Returns fp16 ``[windows * 49, 32 * heads]``
+    (or writes ``out``)."""
+    _require(qkv, "qkv")
+    if not bias_mask.is_cuda or bias_mask.dtype != torch.float32 or not bias_mask.is_contiguous():
+        raise ValueError("window_attention: bias_mask must be a contiguous float32 CUDA tensor")
+    d = WINDOW_HEAD_DIM * heads
+    q2, ldq = _rows(qkv, 3 * d, "qkv")
+    if ldq != 3 * d:
+        raise ValueError("window_attention: qkv rows must be contiguous")
+    rows = q2.shape[0]
+    if rows % WINDOW_TOKENS:
+        raise ValueError(f"window_attention: {rows} rows are not whole {WINDOW_TOKENS}-token windows")
+    bm = bias_mask.shape
+    if len(bm) != 5 or bm[1] != heads or bm[2] != 16 or bm[3] != WINDOW_TOKENS or bm[4] != 4:
+        raise ValueError(f"window_attention: bias_mask must be [bm_windows, {heads}, 16, 49, 4], got {tuple(bm)}")
+    if out is None:
+        out = torch.empty((rows, d), dtype=torch.float16, device=qkv.device)
+    o2, ldo = _rows(out, d, "out")
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.lib().rpfq_window_attention_sm100(
+            q2.data_ptr(), rows // WINDOW_TOKENS, heads, WINDOW_HEAD_DIM, WINDOW_TOKENS, bias_mask.data_ptr(),
+            bm[0], o2.data_ptr(), ldo, _stream(qkv.device)), "rpfq_window_attention_sm100")
+    if rows:
+        _count_launch()
+    return out
+
+
 def vision_act_quant(x: torch.Tensor, salient_token_ratio: float = 0.25, background_clip_ratio: float = 0.75,
                      energy_score_weight: float = 0.5, protect_cls_token: bool = True,
                      out: torch.Tensor | None = None, return_mask: bool = False):

@@ -21,8 +21,8 @@ order; the norm2 pass adds the attention branch (window order) back into the
 residual stream through the inverse gather, in place, and normalizes the
 updated rows; the patch-merging pass gathers the 2x2 neighbourhoods; the
 patch-embedding norm writes the fp32 residual stream. Window attention is
-PyTorch SDPA with the relative-position bias (and shift mask) as an additive
-mask.
+the tcgen05 kernel ``rpfq_window_attention_sm100`` (or PyTorch SDPA with the
+relative-position bias and shift mask as an additive mask).
 """
 
 from __future__ import annotations
@@ -147,10 +147,17 @@ def window_reverse(w: torch.Tensor, ws: int, r: int) -> torch.Tensor:
 
 class PackedSwin(nn.Module):
     """Inference Swin with packed complex-phase linears (random-init weights
-    packed by the exporter's algorithm, as for :class:`PackedViT`)."""
+    packed by the exporter's algorithm, as for :class:`PackedViT`).
+    ``attention="rpfq"`` runs the library's tcgen05 window-attention kernel
+    (7x7 windows, head dim 32), ``"sdpa"`` PyTorch SDPA with the bias as an
+    additive mask."""
 
-    def __init__(self, cfg: SwinConfig, device, seed: int = 0, act_bits: int = 0, prepack: bool = True):
+    def __init__(self, cfg: SwinConfig, device, seed: int = 0, act_bits: int = 0, prepack: bool = True,
+                 attention: str = "rpfq"):
         super().__init__()
+        if attention not in ("sdpa", "rpfq"):
+            raise ValueError(f"attention must be 'sdpa' or 'rpfq', got {attention!r}")
+        self.attention = attention
         self.cfg = cfg
         self.act_bits = act_bits
         dev = torch.device(device)
@@ -236,6 +243,28 @@ class PackedSwin(nn.Module):
             self._masks[key] = m
         return m
 
+    def window_bias(self, s: int, i: int) -> torch.Tensor:
+        """bias_mask of block i of stage s for the window attention kernel
+        (``ops.window_bias_layout`` of the relative position bias + shift
+        mask); bm_windows = 1 on unshifted blocks, the windows per image on
+        shifted ones. Cached."""
+        key = ("wb", s, i)
+        m = self._masks.get(key)
+        if m is None:
+            cfg = self.cfg
+            stage = self.stages[s]
+            blk = stage.blocks[i]
+            ws, shift = cfg.stage_window(s)
+            r = cfg.resolutions()[s]
+            L = ws * ws
+            bias = blk.rel_table.float()[stage.rel_index.reshape(-1)].reshape(L, L, -1).permute(2, 0, 1)  # [nh, L, L]
+            m = bias[None]
+            if shift and i % 2 == 1:
+                m = m + shift_mask(r, ws, shift).to(m.device)[:, None]
+            m = ops.window_bias_layout(m)
+            self._masks[key] = m
+        return m
+
     def orders(self, s: int, shift: int, batch: int):
         """(perm [R*R] int64, rows [B*R*R] int32, inverse [B*R*R] int32) of
         stage s: the window order of the tokens, its per-image row gather for
@@ -285,9 +314,12 @@ class PackedSwin(nn.Module):
                 # LayerNorm writes the tokens already shifted and window-partitioned
                 win = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab, rows=rows).view(-1, ws * ws, c)
                 qkv = blk.qkv(win, prequantized=True)
-                qkv = qkv.view(win.shape[0], ws * ws, 3, nh, hd).permute(2, 0, 3, 1, 4)
-                a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=self.attn_mask(s, i, B))
-                a = a.transpose(1, 2).reshape(win.shape[0], ws * ws, c)
+                if self.attention == "rpfq" and ws * ws == ops.WINDOW_TOKENS and hd == ops.WINDOW_HEAD_DIM:
+                    a = ops.window_attention(qkv.view(-1, 3 * c), nh, self.window_bias(s, i)).view(-1, ws * ws, c)
+                else:
+                    qkv = qkv.view(win.shape[0], ws * ws, 3, nh, hd).permute(2, 0, 3, 1, 4)
+                    a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=self.attn_mask(s, i, B))
+                    a = a.transpose(1, 2).reshape(win.shape[0], ws * ws, c)
                 o = blk.proj(a, out_dtype=torch.float32)
                 # un-partition, un-shift and add to the residual stream (in place) in
                 # the LayerNorm pass that also produces the MLP input
