@@ -76,6 +76,9 @@ def parse():
                     help="--gemm epilogue: plain, exact GELU (fc1), or in-place fp32 residual (proj / fc2)")
     ap.add_argument("--attn", default=None,
                     help="B,L,H: time the short-sequence attention kernel against PyTorch SDPA on one qkv tensor")
+    ap.add_argument("--wattn", default=None,
+                    help="W,H[,NW]: time the Swin window-attention kernel against PyTorch SDPA (NW: shifted-block "
+                         "mask over NW windows per image)")
     ap.add_argument("--pack", default=None,
                     help="N,K: time the GPU packer (rpfq_pack_linear_sm100) on one float [N, K] weight, "
                          "and the exporter algorithm on the host cores beside it")
@@ -755,6 +758,74 @@ def run_attn(args):
     return 0
 
 
+def run_wattn(args):
+    """--wattn W,H[,NW]: rpfq_window_attention_sm100 on W windows of 49 tokens
+    and H heads of dim 32 (NW > 0: a shifted block's per-window mask over NW
+    windows per image) against torch SDPA with the same bias as an additive
+    mask (the expanded fp16 mask the Swin harness feeds it), each replayed
+    from a CUDA graph."""
+    import torch
+    import torch.nn.functional as F
+
+    from rpfq_review_b200 import ops
+    from rpfq_review_b200.swin import shift_mask
+
+    vals = [int(v) for v in args.wattn.split(",")]
+    W, H = vals[0], vals[1]
+    nw = vals[2] if len(vals) > 2 else 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    L, d = 49, 32 * H
+    qkvs = [torch.randn(W * L, 3 * d, device=dev, generator=g).half() for _ in range(2)]
+    outs = [torch.empty(W * L, d, device=dev, dtype=torch.float16) for _ in range(2)]
+    bias = torch.randn(H, L, L, device=dev, generator=g) * 0.5
+    if nw:
+        side_ = int(round((nw ** 0.5) * 7))
+        m = bias[None] + shift_mask(side_, 7, 3).to(dev)[:, None]
+    else:
+        m = bias[None]
+    bm = ops.window_bias_layout(m)
+    mask = m[torch.arange(W, device=dev) % m.shape[0]].half().contiguous()  # [W, H, L, L]
+
+    def ours(i):
+        ops.window_attention(qkvs[i & 1], H, bm, out=outs[i & 1])
+
+    def sdpa(i):
+        x = qkvs[i & 1].view(W, L, 3, H, 32).permute(2, 0, 3, 1, 4)
+        a = F.scaled_dot_product_attention(x[0], x[1], x[2], attn_mask=mask)
+        outs[i & 1].copy_(a.transpose(1, 2).reshape(W * L, d))
+
+    res = {}
+    for name, fn in (("rpfq", ours), ("sdpa", sdpa)):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn(0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) * 1000 / args.steps
+    # algorithmic bytes: qkv read, output written, bias rows once per window entry
+    alg = W * L * 3 * d * 2 + W * L * d * 2 + bm.numel() * 4
+    print(json.dumps({"metric": "window attention us per launch", "shape": [W, H, nw], "rpfq_us": res["rpfq"],
+                      "sdpa_us": res["sdpa"], "rpfq_hbm_gbs_algorithmic": alg / res["rpfq"] / 1e3,
+                      "note": "sdpa includes the transpose copy into the layout the proj GEMM reads"}))
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -779,6 +850,8 @@ def main():
         return run_gemm(args)
     if args.attn:
         return run_attn(args)
+    if args.wattn:
+        return run_wattn(args)
     if args.pack:
         return run_pack(args)
     return run_b200(args)
