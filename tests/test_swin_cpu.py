@@ -67,3 +67,37 @@ def test_window_order_equals_roll_then_partition():
         # scattering back through the same permutation undoes partition and shift
         back = torch.zeros(r * r, 2).index_add_(0, perm, want)
         assert torch.equal(back, x.view(r * r, 2))
+
+
+def test_inverse_gather_equals_scatter_add():
+    """The norm2 pass adds the attention branch (window order) back through
+    the inverse gather: x[n] + o[inverse[n]] equals the scatter
+    x.index_add_(perm, o) it replaced, per image of a batch."""
+    from rpfq_review_b200.swin import window_order
+    B = 2
+    for r, ws, sh in ((56, 7, 3), (28, 7, 0), (14, 7, 3), (7, 7, 0)):
+        perm = window_order(r, ws, sh)
+        base = torch.arange(B)[:, None] * (r * r)
+        inverse = (base + torch.argsort(perm)[None]).reshape(-1)
+        g = torch.Generator().manual_seed(r + sh)
+        x = torch.randn(B, r * r, 5, generator=g)
+        o = torch.randn(B * r * r, 5, generator=g)  # window order
+        want = x.clone().index_add_(1, perm, o.view(B, r * r, 5))
+        got = x.reshape(-1, 5) + o[inverse]
+        assert torch.equal(got.view(B, r * r, 5), want)
+
+
+def test_window_bias_layout():
+    """window_bias_layout: key column j of query row i at [.., j // 4, i, j % 4],
+    scaled by log2(e), -inf in the padding keys 49..63."""
+    import math
+
+    from rpfq_review_b200.ops import window_bias_layout
+    g = torch.Generator().manual_seed(0)
+    bias = torch.randn(3, 2, 49, 49, generator=g)
+    t = window_bias_layout(bias)
+    assert t.shape == (3, 2, 16, 49, 4) and t.dtype == torch.float32
+    full = t.permute(0, 1, 3, 2, 4).reshape(3, 2, 49, 64)
+    assert torch.allclose(full[..., :49], bias * math.log2(math.e))
+    assert torch.isneginf(full[..., 49:]).all()
+    assert float(t[1, 1, 12 // 4, 5, 12 % 4]) == float(bias[1, 1, 5, 12] * math.log2(math.e))
