@@ -303,8 +303,9 @@ int rpfq_pack_linear_sm100(const float* weight, int64_t ldw, int32_t n_c, int32_
 
 /* Allocation-free variant of rpfq_wide_linear_sm100 — no counterpart in the
  * reference. For callers that cannot allocate device memory when they run a
- * layer (code recorded into a CUDA graph, request paths that must not call the
- * synchronising cudaMalloc / cudaFree, hosts that give a library no allocator):
+ * layer (server request paths that must not call cudaMalloc / cudaFree, which
+ * can synchronise the whole device, and plugin or embedded hosts that give a
+ * library no allocator):
  * with act_bits > 0 the quantized activations go to an 8 MiB scratch array
  * built into the library (m * 2 k_c fp16 values at most; larger m is rejected
  * with RPFQ_ERR_INVALID), args->scratch is ignored, and nothing is allocated.

@@ -1143,7 +1143,6 @@ int rpfq_wide_linear_sm100(const RpfqWideLinearArgs* a, rpfq_stream_t stream) {
 // Allocation-free variant of the whole-layer entry point.
 //
 // Some callers cannot allocate device memory at the moment they run a layer:
-// code recorded into a CUDA graph (allocation calls are not capturable),
 // inference servers whose request path must not call cudaMalloc / cudaFree
 // because those calls can synchronise the device and stall every other
 // stream, and embedded or plugin hosts that own a fixed device budget and give

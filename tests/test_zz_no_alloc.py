@@ -1,7 +1,7 @@
 """GPU test of rpfq_wide_linear_noalloc_sm100, the allocation-free variant of
 the whole-layer entry point (for callers that cannot allocate device memory
-while they run a layer, e.g. inside CUDA-graph capture or on a request path
-that must not call the synchronising cudaMalloc / cudaFree).
+while they run a layer, e.g. a server request path that must not call the
+synchronising cudaMalloc / cudaFree, or a plugin host with no allocator).
 
 Called through the C ABI with ctypes, it must give the same output as the
 allocating entry point rpfq_wide_linear_sm100 (given a caller scratch
