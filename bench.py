@@ -70,6 +70,10 @@ def parse():
     ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
     ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
     ap.add_argument("--no-bias", action="store_true", help="--gemm: run the epilogue without the bias add")
+    ap.add_argument("--cpu-layer", action="store_true",
+                    help="--gemm: also time the same layer on the host cores (the reference's C++ fp16-cache runtime "
+                         "and torch F.linear on the dense fp32 weight) and through the C ABI with host buffers "
+                         "(configs[0]: 1576,768,768)")
     ap.add_argument("--split-k", type=int, default=None,
                     help="--gemm: K splits per tile (0 automatic, 1 never, 2..8 forced; default: the library's)")
     ap.add_argument("--epilogue", default="none", choices=["none", "gelu", "residual_f32"],
@@ -654,8 +658,9 @@ def run_gemm(args):
     hbm_bytes = 2 * m * k + 2 * m * n + n * k // 4 + 2 * n
     if args.epilogue == "residual_f32":
         hbm_bytes += 6 * m * n
+    cpu = layer_cpu_legs(args, layer, mod, xs[0], ys[0], step) if args.cpu_layer else None
     print(json.dumps({"metric": "complex-GEMM TFLOP/s", "value": tf, "unit": "TFLOP/s", "shape": [m, n, k],
-                      "epilogue": args.epilogue,
+                      "epilogue": args.epilogue, "cpu_layer": cpu,
                       "path": "fused_decode" if args.fused_decode else "prepacked",
                       "weight_copies": copies, "packed_weight_bytes": packed_bytes,
                       "us_per_launch": ms * 1000, "act_bits": args.act_bits, "split_k": args.split_k,
@@ -663,6 +668,70 @@ def run_gemm(args):
                                    "frac": tf / peak, "peak_source": f"{src} bf16_tflops (burst)"},
                       "hbm_gbs_algorithmic": hbm_bytes / (ms / 1000) / 1e9}))
     return 0
+
+
+def layer_cpu_legs(args, layer, mod, x_dev, y_dev, step):
+    """configs[0] legs of --gemm --cpu-layer, each on the same layer and input:
+    the reference's own C++ fp16-cache runtime (oracle/_ref, all host threads,
+    when built), torch F.linear on the export-dequantized fp32 weight (all
+    host threads: the dense contraction of the reference's PyTorch path,
+    without its per-call weight quantization), and the GPU layer end to end
+    through the public call with host buffers (pinned upload of x, the layer,
+    download of y, timed with CUDA events). Each leg runs for about a second."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import packed_ref as pr
+    from oracle import ref_lib
+    from oracle.vit_ref import packed_to_numpy
+
+    threads = os.cpu_count() or 1
+    np_layer = packed_to_numpy(layer)
+    n_c, k_c = layer.n_c, layer.k_c
+    x_cpu = x_dev.float().cpu()
+
+    def timed(fn, budget=1.0):
+        fn()
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            reps += 1
+            if time.perf_counter() - t0 > budget:
+                return (time.perf_counter() - t0) / reps * 1e6
+
+    out = {"cores": threads, "m": int(x_cpu.shape[0])}
+    if ref_lib.load() is not None:
+        prep = ref_lib.PreparedLayer(np_layer, n_c, k_c)
+        xn = x_cpu.numpy()
+        out["reference_cpp_fp16_cache_us"] = timed(lambda: prep.run(xn, threads))
+    torch.set_num_threads(threads)
+    w = torch.from_numpy(pr.dense_weight_from_packed(np_layer, n_c, k_c))
+    b = torch.from_numpy(np_layer["bias"].astype(np.float32))
+    out["torch_cpu_dense_fp32_us"] = timed(lambda: F.linear(x_cpu, w, b))
+    # the GPU layer with host buffers: pinned x up, layer, y down
+    x_host = x_dev.cpu().pin_memory()
+    y_host = torch.empty(y_dev.shape, dtype=y_dev.dtype).pin_memory()
+
+    def e2e():
+        x_dev.copy_(x_host, non_blocking=True)
+        step(0)
+        y_host.copy_(y_dev, non_blocking=True)
+
+    for _ in range(3):
+        e2e()
+    torch.cuda.synchronize()
+    reps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        e2e()
+    e1.record()
+    torch.cuda.synchronize()
+    out["gpu_e2e_host_buffers_us"] = e0.elapsed_time(e1) * 1000 / reps
+    out["h2d_bytes"] = x_host.numel() * x_host.element_size()
+    out["d2h_bytes"] = y_host.numel() * y_host.element_size()
+    return out
 
 
 def run_pack(args):
