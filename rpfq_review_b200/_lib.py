@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_gemm_sm100",
     "rpfq_gemm_workspace_bytes",
     "rpfq_act_quant_sm100",
+    "rpfq_patch_unfold_sm100",
     "rpfq_layernorm_sm100",
     "rpfq_layernorm_rows_sm100",
     "rpfq_layernorm_ex_sm100",
@@ -139,6 +140,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_gemm_workspace_bytes.argtypes = [I64, I32, I32]
         L.rpfq_gemm_workspace_bytes.restype = ctypes.c_uint64
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
+        L.rpfq_patch_unfold_sm100.argtypes = [P, I32, I64, I32, I32, I32, I32, P, I64, P]
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_layernorm_rows_sm100.argtypes = [P, I64, I64, P, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
         L.rpfq_layernorm_ex_sm100.argtypes = [ctypes.POINTER(RpfqLayerNormArgs), P]

@@ -22,6 +22,7 @@
 #include "attention.cuh"
 #include "window_attention.cuh"
 #include "decode_gemm.cuh"
+#include "embed.cuh"
 #include "gemm.cuh"
 #include "layernorm.cuh"
 #include "pack.cuh"
@@ -726,6 +727,43 @@ int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t l
     return RPFQ_OK;
 }
 
+int rpfq_patch_unfold_sm100(const void* images, int32_t images_f32, int64_t batch, int32_t channels,
+                            int32_t height, int32_t width, int32_t patch, uint16_t* patches, int64_t ldp,
+                            rpfq_stream_t stream) {
+    if (!images || !patches) return fail(RPFQ_ERR_INVALID, "rpfq_patch_unfold_sm100: null pointer");
+    if (batch < 0 || channels <= 0 || patch <= 0 || patch % 8 || height <= 0 || width <= 0 || height % patch ||
+        width % patch)
+        return fail(RPFQ_ERR_INVALID,
+                    "rpfq_patch_unfold_sm100: patch must be a positive multiple of 8 that divides height and width "
+                    "(got %d for %dx%d)", patch, height, width);
+    const int64_t k = static_cast<int64_t>(channels) * patch * patch;
+    if (ldp < k || ldp % 8)
+        return fail(RPFQ_ERR_INVALID, "rpfq_patch_unfold_sm100: ldp must be >= channels * patch^2 and a multiple of 8");
+    if (!aligned16(images) || !aligned16(patches))
+        return fail(RPFQ_ERR_INVALID, "rpfq_patch_unfold_sm100: images and patches must be 16-byte aligned");
+    const int64_t chunks = batch * channels * static_cast<int64_t>(height) * width / 8;
+    if (chunks == 0) return RPFQ_OK;
+    DeviceState* st;
+    int rc = device_state(&st);
+    if (rc) return rc;
+    PatchUnfoldParams p;
+    p.images = images;
+    p.out = reinterpret_cast<__half*>(patches);
+    p.ldo = ldp;
+    p.chunks = chunks;
+    p.c = channels;
+    p.h = height;
+    p.w = width;
+    p.patch = patch;
+    p.f32 = images_f32 ? 1 : 0;
+    const int64_t blocks = (chunks + 255) / 256;
+    if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_patch_unfold_sm100: too many images");
+    RPFQ_CUDA(launch_kernel(patch_unfold_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                            static_cast<cudaStream_t>(stream), 1, p));
+    RPFQ_CUDA(cudaGetLastError());
+    return RPFQ_OK;
+}
+
 int rpfq_layernorm_sm100(const float* x, int64_t ldx, const uint16_t* weight, const uint16_t* bias, uint16_t* y,
                          int64_t ldy, int64_t m, int32_t d, float eps, int32_t act_bits, rpfq_stream_t stream) {
     return rpfq_layernorm_rows_sm100(x, ldx, m, nullptr, weight, bias, y, ldy, m, d, eps, act_bits, stream);
@@ -781,10 +819,10 @@ int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* a, rpfq_stream_t stream) {
                         "(side/2)^2 and x_rows >= images * side^2");
     }
     if (a->add) {
-        if (a->rows || !a->y32 || !a->y32_prenorm || a->ld_add < d || a->ld_add % 4 || !aligned16(a->add) ||
+        if (!a->y32 || !a->y32_prenorm || a->ld_add < d || a->ld_add % 4 || !aligned16(a->add) ||
             (a->add_rows && (reinterpret_cast<uintptr_t>(a->add_rows) & 3)) || a->add_bound < 0)
             return fail(RPFQ_ERR_INVALID,
-                        "rpfq_layernorm_ex_sm100: add needs no gather, y32 with y32_prenorm, a 16-byte aligned add "
+                        "rpfq_layernorm_ex_sm100: add needs y32 with y32_prenorm, a 16-byte aligned add "
                         "with ld_add >= d (a multiple of 4) and 4-byte aligned add_rows");
     }
     if (a->y32 && static_cast<const void*>(a->y32) == static_cast<const void*>(a->x) &&

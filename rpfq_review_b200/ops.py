@@ -431,6 +431,32 @@ def layernorm_ex(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps:
     return out, out32
 
 
+def patch_unfold(images: torch.Tensor, patch: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """images ``[B, C, H, W]`` (fp16 or fp32) -> fp16 patch rows ``[B, (H/P)(W/P), C P P]``
+    in the CHW patch order of the reference's ``patchify_tensor``
+    (``audit_rpfq_vit_ios_parity.py:125-134``), ``rpfq_patch_unfold_sm100``."""
+    if not images.is_cuda or images.dtype not in (torch.float16, torch.float32) or images.dim() != 4:
+        raise ValueError("patch_unfold: images must be a [B, C, H, W] float16 or float32 CUDA tensor")
+    images = images.contiguous()
+    B, C, H, W = images.shape
+    if patch <= 0 or H % patch or W % patch:
+        raise ValueError(f"patch_unfold: patch {patch} must divide the image size {H}x{W}")
+    n, k = (H // patch) * (W // patch), C * patch * patch
+    if out is None:
+        out = torch.empty((B, n, k), dtype=torch.float16, device=images.device)
+    o2, ldo = _rows(out, k, "out")
+    if o2.data_ptr() != out.data_ptr() or o2.shape[0] != B * n:
+        raise ValueError(f"patch_unfold: out must be a row-major view of {B * n} rows with unit column stride")
+    if B == 0:
+        return out
+    with torch.cuda.device(images.device):
+        _lib.check(_lib.lib().rpfq_patch_unfold_sm100(images.data_ptr(), int(images.dtype == torch.float32), B, C, H,
+                                                      W, int(patch), o2.data_ptr(), ldo, _stream(images.device)),
+                   "rpfq_patch_unfold_sm100")
+    _count_launch()
+    return out
+
+
 def act_quant(x: torch.Tensor, num_bits: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Per-row symmetric quantization of the Re / Im halves (ActivationQuantSTE)."""
     _require(x, "x")

@@ -161,11 +161,25 @@ class PackedViT(nn.Module):
             yield "head_dist", self.head_dist
 
     # ------------------------------------------------------------------ forward
-    def patchify(self, images: torch.Tensor) -> torch.Tensor:
-        B, C, H, W = images.shape
-        p = self.cfg.patch
-        x = images.reshape(B, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5)
-        return x.reshape(B, (H // p) * (W // p), C * p * p)
+    def _token_index(self, B: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """int32 tables over the B x tokens rows of the residual stream: the
+        source row of each token (class tokens first, then image b's patch
+        embeddings at ntok + b * patches) and its position index. Kept per
+        batch size; built without caching while a CUDA graph is captured (the
+        graph's memory pool must not back a cached tensor)."""
+        key = (B, str(device))
+        cache = self.__dict__.setdefault("_token_index_cache", {})
+        if key in cache:
+            return cache[key]
+        L, n_p = self.cfg.tokens, (self.cfg.img // self.cfg.patch) ** 2
+        ntok = L - n_p
+        t = torch.arange(L, dtype=torch.int32, device=device).repeat(B)
+        b = torch.arange(B, dtype=torch.int32, device=device).repeat_interleave(L)
+        rows = torch.where(t < ntok, t, ntok + b * n_p + (t - ntok)).to(torch.int32)
+        if not torch.cuda.is_current_stream_capturing():
+            cache.clear()
+            cache[key] = (rows, t)
+        return rows, t
 
     @torch.no_grad()
     def forward(self, images: torch.Tensor) -> torch.Tensor:
@@ -184,18 +198,28 @@ class PackedViT(nn.Module):
         hd = d // H
         ab = self.act_bits
         pre = self.vision_quant is None  # LayerNorm applied the quantizer
-        patches = self.patchify(images.to(torch.float16))
-        emb = ops.gemm(patches, self.patch_w, self.patch_b, out_dtype=torch.float32)
-        ntok = cfg.tokens - patches.shape[1]
-        # residual stream [cls (+ dist), patches] + position embedding, written in
-        # one pass over the patch embeddings
-        pos = self.pos_embed.float()
-        x = torch.empty((B, cfg.tokens, d), dtype=torch.float32, device=emb.device)
-        x[:, :ntok] = self.cls_tokens.float() + pos[:, :ntok]
-        torch.add(emb, pos[:, ntok:], out=x[:, ntok:])
+        patches = ops.patch_unfold(images, cfg.patch)
+        n_p = patches.shape[1]
+        ntok = cfg.tokens - n_p
         L = cfg.tokens
-        for blk in self.blocks:
-            h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab)
+        # token sources: the class (+ distillation) token rows, then the patch
+        # embeddings, which the patch GEMM writes straight below them
+        src = torch.empty((ntok + B * n_p, d), dtype=torch.float32, device=patches.device)
+        src[:ntok].copy_(self.cls_tokens[0])
+        ops.gemm(patches, self.patch_w, self.patch_b, out=src[ntok:].view(B, n_p, d))
+        # residual stream x = [cls (+ dist), patches] + position embedding
+        # (reference forward_runtime_path, audit_rpfq_vit_ios_parity.py:638-645),
+        # assembled by the first LayerNorm pass: it gathers each token's source
+        # row, adds its position row, writes x and normalizes it
+        rows, tok = self._token_index(B, patches.device)
+        pos = self.pos_embed[0].float()
+        x = torch.empty((B, L, d), dtype=torch.float32, device=patches.device)
+        for i, blk in enumerate(self.blocks):
+            if i == 0:
+                h, _ = ops.layernorm_ex(src, blk.norm1_w, blk.norm1_b, cfg.eps, ab, rows=rows, add=pos,
+                                        add_rows=tok, out32=x, out32_prenorm=True)
+            else:
+                h = ops.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, ab)
             qkv = blk.qkv(h, prequantized=pre)
             if self.attention == "rpfq" and hd == 64 and L <= ops.ATTENTION_MAX_TOKENS:
                 a = ops.attention(qkv.view(B, L, 3 * d), H)

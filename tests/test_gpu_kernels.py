@@ -483,3 +483,71 @@ def test_gelu_epilogue_accuracy(cuda):
     err = (y - ref).abs()
     bound = 5e-7 * torch.clamp(x.double().abs(), min=1.0)
     assert bool((err <= bound).all()), float((err / bound).max())
+
+
+def _patchify_ref(images: torch.Tensor, p: int) -> torch.Tensor:
+    """The reference's patchify_tensor (audit_rpfq_vit_ios_parity.py:125-134),
+    batched: CHW patch order."""
+    B, C, H, W = images.shape
+    x = images.reshape(B, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5)
+    return x.reshape(B, (H // p) * (W // p), C * p * p)
+
+
+@pytest.mark.parametrize("B,C,H,W,p,dtype", [(3, 3, 224, 224, 16, torch.float16), (2, 3, 224, 224, 16, torch.float32),
+                                             (2, 3, 32, 48, 8, torch.float16), (1, 1, 48, 16, 16, torch.float32),
+                                             (0, 3, 224, 224, 16, torch.float16)])
+def test_patch_unfold_bit_exact(cuda, B, C, H, W, p, dtype):
+    """rpfq_patch_unfold_sm100 against the reference's patch order: bit-exact
+    fp16 rows (fp32 images rounded to nearest even, as .to(float16)), into a
+    fresh tensor and into a strided row view of a wider buffer."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(B * 1000 + H + p)
+    images = (torch.randn(B, C, H, W, generator=g) * 3).to(dtype).to(cuda)
+    want = _patchify_ref(images.to(torch.float16), p)
+    got = ops.patch_unfold(images, p)
+    assert got.shape == want.shape
+    assert torch.equal(got.view(torch.int16), want.contiguous().view(torch.int16))
+    k = C * p * p
+    wide = torch.full((B * (H // p) * (W // p), k + 24), 7.0, dtype=torch.float16, device=cuda)
+    ops.patch_unfold(images, p, out=wide[:, :k])
+    assert torch.equal(wide[:, :k].view(torch.int16), want.reshape(-1, k).view(torch.int16))
+    assert bool((wide[:, k:] == 7.0).all())
+
+
+def test_patch_unfold_rejects_bad_shapes(cuda):
+    from rpfq_review_b200 import _lib
+    ops = _ops()
+    with pytest.raises(ValueError):
+        ops.patch_unfold(torch.zeros(1, 3, 30, 32, dtype=torch.float16, device=cuda), 16)  # 16 does not divide 30
+    out = torch.empty(4, 48, dtype=torch.float16, device=cuda)
+    rc = _lib.lib().rpfq_patch_unfold_sm100(out.data_ptr(), 0, 1, 3, 8, 8, 4, out.data_ptr(), 48, None)
+    assert rc != 0 and b"multiple of 8" in _lib.lib().rpfq_last_error()
+
+
+@pytest.mark.parametrize("d,ntok", [(768, 1), (384, 2), (1024, 1)])
+def test_layernorm_token_assembly(cuda, d, ntok):
+    """The first LayerNorm pass of PackedViT assembles the residual stream: row
+    (b, t) gathers source row t (class tokens) or ntok + b * patches + t - ntok
+    (patch embeddings), adds position row t, writes the fp32 stream and its
+    LayerNorm; both equal the torch assembly (one fp32 add) and the plain
+    kernel's LayerNorm of it, bit for bit."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(d + ntok)
+    B, n_p = 5, 196
+    L = n_p + ntok
+    src = torch.randn(ntok + B * n_p, d, generator=g).to(cuda)
+    pos = torch.randn(L, d, generator=g).to(cuda)
+    w = (torch.randn(d, generator=g) * 0.2 + 1).half().to(cuda)
+    b = (torch.randn(d, generator=g) * 0.1).half().to(cuda)
+    t = torch.arange(L, dtype=torch.int32).repeat(B)
+    bi = torch.arange(B, dtype=torch.int32).repeat_interleave(L)
+    rows = torch.where(t < ntok, t, ntok + bi * n_p + (t - ntok)).to(torch.int32)
+    want_x = torch.empty(B, L, d, device=cuda)
+    want_x[:, :ntok] = src[:ntok] + pos[:ntok]
+    want_x[:, ntok:] = src[ntok:].view(B, n_p, d) + pos[ntok:]
+    want_h = ops.layernorm(want_x, w, b, 1e-6, act_bits=4)
+    x = torch.empty(B, L, d, device=cuda)
+    h, _ = ops.layernorm_ex(src, w, b, 1e-6, 4, rows=rows.to(cuda), add=pos, add_rows=t.to(cuda), out32=x,
+                            out32_prenorm=True)
+    assert torch.equal(x, want_x)
+    assert torch.equal(h.view(B, L, d), want_h)
