@@ -46,7 +46,9 @@ struct LayerNormParams {
 //                residual add of the attention branch)
 // Outputs: fp16 y (normalized, optionally activation-quantized) and / or
 // fp32 y32 (normalized, or with y32_prenorm the row before normalization).
-template <int D>
+// PLAIN instances (row source x[row], fp16 output only: every LayerNorm of
+// the ViT / DeiT blocks) compile without the source selection.
+template <int D, bool PLAIN>
 __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormParams p) {
     static_assert(D % 32 == 0, "row length must be a multiple of 32");
     // VW consecutive floats per lane and step: element e of step j of lane l
@@ -64,35 +66,37 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     pdl_launch_dependents();
     if (slot >= p.m) return;
     // source row of each quarter of the output row (all four equal unless merging)
-    int64_t src[4];
-    if (p.merge_side > 0) {
-        const int64_t half = p.merge_side >> 1;
-        const int64_t img = row / (half * half), t = row - img * half * half;
-        const int64_t i = t / half, j = t - i * half;
-        const int64_t base = img * p.merge_side * p.merge_side + 2 * i * p.merge_side + 2 * j;
-        src[0] = base;
-        src[1] = base + p.merge_side;
-        src[2] = base + 1;
-        src[3] = base + p.merge_side + 1;
-    } else {
-        int64_t s0 = row;
-        if (p.rows != nullptr) {
-            s0 = p.rows[row];
-            if (s0 < 0 || s0 >= p.x_rows) {  // bad gather index: report, touch nothing
-                if (lane == 0) atomicCAS(p.err, 0, 901);
+    int64_t src[4] = {row, row, row, row};
+    const float* ar = nullptr;
+    if constexpr (!PLAIN) {
+        if (p.merge_side > 0) {
+            const int64_t half = p.merge_side >> 1;
+            const int64_t img = row / (half * half), t = row - img * half * half;
+            const int64_t i = t / half, j = t - i * half;
+            const int64_t base = img * p.merge_side * p.merge_side + 2 * i * p.merge_side + 2 * j;
+            src[0] = base;
+            src[1] = base + p.merge_side;
+            src[2] = base + 1;
+            src[3] = base + p.merge_side + 1;
+        } else {
+            int64_t s0 = row;
+            if (p.rows != nullptr) {
+                s0 = p.rows[row];
+                if (s0 < 0 || s0 >= p.x_rows) {  // bad gather index: report, touch nothing
+                    if (lane == 0) atomicCAS(p.err, 0, 901);
+                    return;
+                }
+            }
+            src[0] = src[1] = src[2] = src[3] = s0;
+        }
+        if (p.add != nullptr) {
+            const int64_t a = p.add_rows != nullptr ? p.add_rows[row] : row;
+            if (a < 0 || a >= p.add_bound) {
+                if (lane == 0) atomicCAS(p.err, 0, 902);
                 return;
             }
+            ar = p.add + a * p.ld_add;
         }
-        src[0] = src[1] = src[2] = src[3] = s0;
-    }
-    const float* ar = nullptr;
-    if (p.add != nullptr) {
-        const int64_t a = p.add_rows != nullptr ? p.add_rows[row] : row;
-        if (a < 0 || a >= p.add_bound) {
-            if (lane == 0) atomicCAS(p.err, 0, 902);
-            return;
-        }
-        ar = p.add + a * p.ld_add;
     }
     float v[J][VW];
     float sum = 0.0f;
@@ -100,8 +104,8 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     for (int j = 0; j < J; ++j) {
         const int col = 32 * VW * j + VW * lane;
         const int q = col / (D / 4);  // quarter (VW divides D / 4 whenever merging is allowed)
-        const int64_t sq = q == 0 ? src[0] : (q == 1 ? src[1] : (q == 2 ? src[2] : src[3]));
-        const float* xr = p.x + sq * p.ldx + (p.merge_side > 0 ? col - q * (D / 4) : col);
+        const int64_t sq = PLAIN ? row : (q == 0 ? src[0] : (q == 1 ? src[1] : (q == 2 ? src[2] : src[3])));
+        const float* xr = p.x + sq * p.ldx + (!PLAIN && p.merge_side > 0 ? col - q * (D / 4) : col);
         if constexpr (VW == 4) {
             float4 t = *reinterpret_cast<const float4*>(xr);
             if (ar != nullptr) {
@@ -131,7 +135,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
             sum += v[j][0];
         }
     }
-    if (p.y32 != nullptr && p.y32_prenorm) {
+    if (!PLAIN && p.y32 != nullptr && p.y32_prenorm) {
         // the updated residual row (in place when y32 == x: this warp has read its whole row)
         float* zr = p.y32 + row * p.ldy32;
 #pragma unroll
@@ -190,7 +194,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
                 amax_im = fmaxf(amax_im, a);
         }
     }
-    if (p.y32 != nullptr && !p.y32_prenorm) {
+    if (!PLAIN && p.y32 != nullptr && !p.y32_prenorm) {
         float* zr = p.y32 + row * p.ldy32;
 #pragma unroll
         for (int j = 0; j < J; ++j) {

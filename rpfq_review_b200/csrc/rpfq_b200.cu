@@ -858,14 +858,21 @@ int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* a, rpfq_stream_t stream) {
     if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: m too large");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned nb = static_cast<unsigned>(blocks);
+    const bool plain = !a->rows && !a->add && !a->merge_side && !a->y32;
     switch (d) {
-        case 96: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<96>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
-        case 192: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<192>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
-        case 384: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<384>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
-        case 768: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<768>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
-        case 1024: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<1024>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
-        case 1536: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<1536>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
-        case 3072: RPFQ_CUDA(launch_kernel(layernorm_f32_f16_kernel<3072>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); break;
+#define RPFQ_LN_CASE(D)                                                                                            \
+    case D:                                                                                                        \
+        RPFQ_CUDA(plain ? launch_kernel(layernorm_f32_f16_kernel<D, true>, dim3(nb), dim3(warps * 32), 0, s, 1, p) \
+                        : launch_kernel(layernorm_f32_f16_kernel<D, false>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); \
+        break;
+        RPFQ_LN_CASE(96)
+        RPFQ_LN_CASE(192)
+        RPFQ_LN_CASE(384)
+        RPFQ_LN_CASE(768)
+        RPFQ_LN_CASE(1024)
+        RPFQ_LN_CASE(1536)
+        RPFQ_LN_CASE(3072)
+#undef RPFQ_LN_CASE
         default:
             return fail(RPFQ_ERR_UNSUPPORTED,
                         "rpfq_layernorm_sm100: row length %d (supported: 96, 192, 384, 768, 1024, 1536, 3072)", d);
