@@ -35,6 +35,24 @@ struct LayerNormParams {
     int* err;
 };
 
+// VW consecutive floats at p (16-, 8- or 4-byte aligned by the caller).
+template <int VW>
+__device__ __forceinline__ void load_row_part(const float* p, float (&v)[VW]) {
+    if constexpr (VW == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(p);
+        v[0] = t.x;
+        v[1] = t.y;
+        v[2] = t.z;
+        v[3] = t.w;
+    } else if constexpr (VW == 2) {
+        const float2 t = *reinterpret_cast<const float2*>(p);
+        v[0] = t.x;
+        v[1] = t.y;
+    } else {
+        v[0] = p[0];
+    }
+}
+
 // One warp per output row. Row sources:
 //   plain        x[row]
 //   rows         x[rows[row]] (Swin's cyclic shift + window partition)
@@ -98,42 +116,35 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
             ar = p.add + a * p.ld_add;
         }
     }
+    // every load of the row is issued before the first use (x, then the add
+    // rows), with no branch between them
     float v[J][VW];
-    float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const int col = 32 * VW * j + VW * lane;
         const int q = col / (D / 4);  // quarter (VW divides D / 4 whenever merging is allowed)
         const int64_t sq = PLAIN ? row : (q == 0 ? src[0] : (q == 1 ? src[1] : (q == 2 ? src[2] : src[3])));
         const float* xr = p.x + sq * p.ldx + (!PLAIN && p.merge_side > 0 ? col - q * (D / 4) : col);
-        if constexpr (VW == 4) {
-            float4 t = *reinterpret_cast<const float4*>(xr);
-            if (ar != nullptr) {
-                const float4 u = *reinterpret_cast<const float4*>(ar + col);
-                t.x += u.x;
-                t.y += u.y;
-                t.z += u.z;
-                t.w += u.w;
-            }
-            v[j][0] = t.x;
-            v[j][1] = t.y;
-            v[j][2] = t.z;
-            v[j][3] = t.w;
-            sum += (t.x + t.y) + (t.z + t.w);
-        } else if constexpr (VW == 2) {
-            float2 t = *reinterpret_cast<const float2*>(xr);
-            if (ar != nullptr) {
-                const float2 u = *reinterpret_cast<const float2*>(ar + col);
-                t.x += u.x;
-                t.y += u.y;
-            }
-            v[j][0] = t.x;
-            v[j][1] = t.y;
-            sum += t.x + t.y;
-        } else {
-            v[j][0] = xr[0] + (ar != nullptr ? ar[col] : 0.0f);
+        load_row_part<VW>(xr, v[j]);
+    }
+    if (!PLAIN && ar != nullptr) {
+        float u[J][VW];
+#pragma unroll
+        for (int j = 0; j < J; ++j) load_row_part<VW>(ar + 32 * VW * j + VW * lane, u[j]);
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int e = 0; e < VW; ++e) v[j][e] += u[j][e];
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        if constexpr (VW == 4)
+            sum += (v[j][0] + v[j][1]) + (v[j][2] + v[j][3]);
+        else if constexpr (VW == 2)
+            sum += v[j][0] + v[j][1];
+        else
             sum += v[j][0];
-        }
     }
     if (!PLAIN && p.y32 != nullptr && p.y32_prenorm) {
         // the updated residual row (in place when y32 == x: this warp has read its whole row)
