@@ -139,11 +139,12 @@ int rpfq_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, int64_t l
  * width] (fp16, or fp32 with images_f32 != 0, contiguous) -> fp16 rows
  * patches[b * gh * gw + i * gw + j][c * patch^2 + y * patch + x] =
  * image[b][c][i * patch + y][j * patch + x], the input of the patch-embedding
- * GEMM (row stride ldp >= channels * patch^2, a multiple of 8). Replaces the
+ * GEMM (row stride ldp >= channels * patch^2, a multiple of 8, or of 4 when
+ * patch is not a multiple of 8). Replaces the
  * reference's patchify_tensor (RPFQ-ViTApple/scripts/audit_rpfq_vit_ios_parity.py:
  * 125-134), the CHW patch order of Conv2d(C, d, patch, stride patch) weights
- * flattened to [d, C patch^2]. patch must be a multiple of 8 dividing height
- * and width; both pointers 16-byte aligned. */
+ * flattened to [d, C patch^2]. patch must be a multiple of 4 (ViT / DeiT 16,
+ * Swin 4) dividing height and width; both pointers 16-byte aligned. */
 int rpfq_patch_unfold_sm100(const void* images, int32_t images_f32, int64_t batch, int32_t channels,
                             int32_t height, int32_t width, int32_t patch, uint16_t* patches, int64_t ldp,
                             rpfq_stream_t stream);

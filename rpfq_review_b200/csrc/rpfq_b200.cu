@@ -731,17 +731,19 @@ int rpfq_patch_unfold_sm100(const void* images, int32_t images_f32, int64_t batc
                             int32_t height, int32_t width, int32_t patch, uint16_t* patches, int64_t ldp,
                             rpfq_stream_t stream) {
     if (!images || !patches) return fail(RPFQ_ERR_INVALID, "rpfq_patch_unfold_sm100: null pointer");
-    if (batch < 0 || channels <= 0 || patch <= 0 || patch % 8 || height <= 0 || width <= 0 || height % patch ||
+    if (batch < 0 || channels <= 0 || patch <= 0 || patch % 4 || height <= 0 || width <= 0 || height % patch ||
         width % patch)
         return fail(RPFQ_ERR_INVALID,
-                    "rpfq_patch_unfold_sm100: patch must be a positive multiple of 8 that divides height and width "
+                    "rpfq_patch_unfold_sm100: patch must be a positive multiple of 4 that divides height and width "
                     "(got %d for %dx%d)", patch, height, width);
+    const int chunk = patch % 8 == 0 ? 8 : 4;  // pixels per thread (one 16- or 8-byte store)
     const int64_t k = static_cast<int64_t>(channels) * patch * patch;
-    if (ldp < k || ldp % 8)
-        return fail(RPFQ_ERR_INVALID, "rpfq_patch_unfold_sm100: ldp must be >= channels * patch^2 and a multiple of 8");
+    if (ldp < k || ldp % chunk)
+        return fail(RPFQ_ERR_INVALID,
+                    "rpfq_patch_unfold_sm100: ldp must be >= channels * patch^2 and a multiple of %d", chunk);
     if (!aligned16(images) || !aligned16(patches))
         return fail(RPFQ_ERR_INVALID, "rpfq_patch_unfold_sm100: images and patches must be 16-byte aligned");
-    const int64_t chunks = batch * channels * static_cast<int64_t>(height) * width / 8;
+    const int64_t chunks = batch * channels * static_cast<int64_t>(height) * width / chunk;
     if (chunks == 0) return RPFQ_OK;
     DeviceState* st;
     int rc = device_state(&st);
@@ -758,8 +760,10 @@ int rpfq_patch_unfold_sm100(const void* images, int32_t images_f32, int64_t batc
     p.f32 = images_f32 ? 1 : 0;
     const int64_t blocks = (chunks + 255) / 256;
     if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_patch_unfold_sm100: too many images");
-    RPFQ_CUDA(launch_kernel(patch_unfold_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
-                            static_cast<cudaStream_t>(stream), 1, p));
+    RPFQ_CUDA(chunk == 8 ? launch_kernel(patch_unfold_kernel<8>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                                         static_cast<cudaStream_t>(stream), 1, p)
+                         : launch_kernel(patch_unfold_kernel<4>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                                         static_cast<cudaStream_t>(stream), 1, p));
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }

@@ -286,12 +286,6 @@ class PackedSwin(nn.Module):
             self._orders[key] = o
         return o
 
-    def patchify(self, images: torch.Tensor) -> torch.Tensor:
-        b, c, h, w = images.shape
-        p = self.cfg.patch
-        x = images.reshape(b, c, h // p, p, w // p, p).permute(0, 2, 4, 1, 3, 5)
-        return x.reshape(b, (h // p) * (w // p), c * p * p)
-
     @torch.no_grad()
     def forward(self, images: torch.Tensor) -> torch.Tensor:
         """images ``[B, 3, 224, 224]`` -> logits fp32 ``[B, classes]``; the
@@ -300,7 +294,7 @@ class PackedSwin(nn.Module):
         ab = self.act_bits
         B = images.shape[0]
         dims, res = cfg.dims(), cfg.resolutions()
-        emb = ops.gemm(self.patchify(images.to(torch.float16)), self.patch_w, self.patch_b, out_dtype=torch.float32)
+        emb = ops.gemm(ops.patch_unfold(images, cfg.patch), self.patch_w, self.patch_b, out_dtype=torch.float32)
         # patch-embedding LayerNorm in place: the residual stream starts as its fp32 output
         ops.layernorm_ex(emb, self.patch_norm_w, self.patch_norm_b, cfg.eps, fp16_out=False, out32=emb)
         x = emb

@@ -495,7 +495,8 @@ def _patchify_ref(images: torch.Tensor, p: int) -> torch.Tensor:
 
 @pytest.mark.parametrize("B,C,H,W,p,dtype", [(3, 3, 224, 224, 16, torch.float16), (2, 3, 224, 224, 16, torch.float32),
                                              (2, 3, 32, 48, 8, torch.float16), (1, 1, 48, 16, 16, torch.float32),
-                                             (0, 3, 224, 224, 16, torch.float16)])
+                                             (0, 3, 224, 224, 16, torch.float16), (2, 3, 224, 224, 4, torch.float16),
+                                             (1, 3, 32, 24, 4, torch.float32)])
 def test_patch_unfold_bit_exact(cuda, B, C, H, W, p, dtype):
     """rpfq_patch_unfold_sm100 against the reference's patch order: bit-exact
     fp16 rows (fp32 images rounded to nearest even, as .to(float16)), into a
@@ -519,9 +520,9 @@ def test_patch_unfold_rejects_bad_shapes(cuda):
     ops = _ops()
     with pytest.raises(ValueError):
         ops.patch_unfold(torch.zeros(1, 3, 30, 32, dtype=torch.float16, device=cuda), 16)  # 16 does not divide 30
-    out = torch.empty(4, 48, dtype=torch.float16, device=cuda)
-    rc = _lib.lib().rpfq_patch_unfold_sm100(out.data_ptr(), 0, 1, 3, 8, 8, 4, out.data_ptr(), 48, None)
-    assert rc != 0 and b"multiple of 8" in _lib.lib().rpfq_last_error()
+    out = torch.empty(4, 108, dtype=torch.float16, device=cuda)
+    rc = _lib.lib().rpfq_patch_unfold_sm100(out.data_ptr(), 0, 1, 3, 12, 12, 6, out.data_ptr(), 108, None)
+    assert rc != 0 and b"multiple of 4" in _lib.lib().rpfq_last_error()
 
 
 @pytest.mark.parametrize("d,ntok", [(768, 1), (384, 2), (1024, 1)])
