@@ -1074,7 +1074,9 @@ int rpfq_vision_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, in
     const int smem = 2 * patches * 4 + tokens;
     vision_select_kernel<<<static_cast<unsigned>(images), kVisionThreads, smem, s>>>(p, stats, scales);
     RPFQ_CUDA(cudaGetLastError());
-    vision_apply_kernel<<<static_cast<unsigned>(stat_ctas), kVisionThreads, 0, s>>>(p, rows, scales);
+    const int64_t apply_ctas =
+        std::min<int64_t>((rows + 16 * kVisionApplyRun - 1) / (16 * kVisionApplyRun), 2 * st->sm_count);  // resident CTAs
+    vision_apply_kernel<<<static_cast<unsigned>(apply_ctas), kVisionThreads, 0, s>>>(p, rows, scales);
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }

@@ -78,20 +78,32 @@ __device__ __forceinline__ void vq_row_stats(const VisionQuantParams& p, const _
                                              float& amax_re, float& amax_im, float& esum) {
     const int lane = threadIdx.x & 31;
     float ar = 0.0f, ai = 0.0f, es = 0.0f;
-    for (int j0 = lane * 8; j0 < p.k_c; j0 += 256) {
-        const uint4 vr = *reinterpret_cast<const uint4*>(row + j0);
-        const uint4 vi = *reinterpret_cast<const uint4*>(row + p.k_c + j0);
-        const __half2* hr = reinterpret_cast<const __half2*>(&vr);
-        const __half2* hi = reinterpret_cast<const __half2*>(&vi);
+    // four 8-column chunks of each half per lane in flight, consumed in column order
+    for (int j00 = lane * 8; j00 < p.k_c; j00 += 4 * 256) {
+        uint4 vr[4], vi[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 r = __half22float2(hr[e]);
-            const float2 i = __half22float2(hi[e]);
-            ar = fmaxf(ar, fmaxf(fabsf(r.x), fabsf(r.y)));
-            ai = fmaxf(ai, fmaxf(fabsf(i.x), fabsf(i.y)));
-            if (energy) {
-                es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.x, r.x), __fmul_rn(i.x, i.x)), kVisionEps)));
-                es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.y, r.y), __fmul_rn(i.y, i.y)), kVisionEps)));
+        for (int u = 0; u < 4; ++u) {
+            const int j0 = j00 + u * 256;
+            if (j0 < p.k_c) {
+                vr[u] = *reinterpret_cast<const uint4*>(row + j0);
+                vi[u] = *reinterpret_cast<const uint4*>(row + p.k_c + j0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (j00 + u * 256 >= p.k_c) break;
+            const __half2* hr = reinterpret_cast<const __half2*>(&vr[u]);
+            const __half2* hi = reinterpret_cast<const __half2*>(&vi[u]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 r = __half22float2(hr[e]);
+                const float2 i = __half22float2(hi[e]);
+                ar = fmaxf(ar, fmaxf(fabsf(r.x), fabsf(r.y)));
+                ai = fmaxf(ai, fmaxf(fabsf(i.x), fabsf(i.y)));
+                if (energy) {
+                    es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.x, r.x), __fmul_rn(i.x, i.x)), kVisionEps)));
+                    es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.y, r.y), __fmul_rn(i.y, i.y)), kVisionEps)));
+                }
             }
         }
     }
@@ -131,6 +143,51 @@ __device__ __forceinline__ void vq_quantize_row(const VisionQuantParams& p, cons
         *reinterpret_cast<uint4*>(out + c0) = o;
     }
 }
+
+// vq_quantize_row with the quotients q / s taken from a table: tab[h][q + 128]
+// = fl(q / s_h) for the integers q in [-128, 127] (the only values q takes), so
+// the IEEE division runs once per table entry instead of once per element.
+// q = -0 reads the +0 entry; x + (q / s - x) is +0 for either sign of zero, so
+// the output bits equal vq_quantize_row's. Eight 16-byte chunks of the row per
+// lane are loaded before the first is used.
+__device__ __forceinline__ void vq_quantize_row_tab(const VisionQuantParams& p, const __half* row, __half* out,
+                                                    float sr, float si, const float (*tab)[256]) {
+    const int lane = threadIdx.x & 31;
+    const int n = 2 * p.k_c;
+    for (int c00 = lane * 8; c00 < n; c00 += 8 * 256) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (c00 + u * 256 < n) v[u] = *reinterpret_cast<const uint4*>(row + c00 + u * 256);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int c0 = c00 + u * 256;
+            if (c0 >= n) break;
+            const bool re = c0 < p.k_c;  // k_c % 8 == 0: a chunk lies in one half
+            const float s = re ? sr : si;
+            const float* th = tab[re ? 0 : 1];
+            const __half2* h = reinterpret_cast<const __half2*>(&v[u]);
+            uint4 o;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(h[e]);
+                float r[2] = {f.x, f.y};
+#pragma unroll
+                for (int w = 0; w < 2; ++w) {
+                    const float q = fminf(fmaxf(rintf(__fmul_rn(r[w], s)), -128.0f), 127.0f);
+                    const float qx = th[static_cast<int>(q) + 128];
+                    r[w] = __fadd_rn(r[w], __fsub_rn(qx, r[w]));
+                }
+                const __half2 hh = __floats2half2_rn(r[0], r[1]);
+                ow[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(out + c0) = o;
+        }
+    }
+}
+
+constexpr int kVisionApplyRun = 4;  // consecutive rows per warp (one image's background rows share scales)
 
 // grid = 0: one warp per token, no shared state (any token count).
 __global__ void __launch_bounds__(kVisionThreads) vision_quant_tokenwise_kernel(const VisionQuantParams p,
@@ -238,11 +295,27 @@ __global__ void __launch_bounds__(kVisionThreads) vision_select_kernel(const Vis
 // One warp per row (no index division), 16 bytes per lane and step.
 __global__ void __launch_bounds__(kVisionThreads) vision_apply_kernel(const VisionQuantParams p, int64_t rows,
                                                                      const float2* scales) {
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * (kVisionThreads / 32);
-    for (int64_t r = static_cast<int64_t>(blockIdx.x) * (kVisionThreads / 32) + (threadIdx.x >> 5); r < rows;
-         r += warps) {
-        const float2 sc = scales[r];
-        vq_quantize_row(p, p.x + r * p.ldx, p.y + r * p.ldy, sc.x, sc.y);
+    __shared__ float qtab[kVisionThreads / 32][2][256];  // per warp: fl(q / s) of the scales it holds
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float(*tab)[256] = qtab[warp];
+    float tab_sr = 0.0f, tab_si = 0.0f;  // scales are > 0: 0 marks an empty table
+    const int64_t step = static_cast<int64_t>(gridDim.x) * (kVisionThreads / 32) * kVisionApplyRun;
+    for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * (kVisionThreads / 32) + warp) * kVisionApplyRun; r0 < rows;
+         r0 += step) {
+        for (int64_t r = r0; r < r0 + kVisionApplyRun && r < rows; ++r) {
+            const float2 sc = scales[r];
+            if (sc.x != tab_sr || sc.y != tab_si) {
+                __syncwarp();  // every lane is done with the previous table
+                for (int t = lane; t < 256; t += 32) {
+                    tab[0][t] = __fdiv_rn(static_cast<float>(t - 128), sc.x);
+                    tab[1][t] = __fdiv_rn(static_cast<float>(t - 128), sc.y);
+                }
+                __syncwarp();
+                tab_sr = sc.x;
+                tab_si = sc.y;
+            }
+            vq_quantize_row_tab(p, p.x + r * p.ldx, p.y + r * p.ldy, sc.x, sc.y, tab);
+        }
     }
 }
 
