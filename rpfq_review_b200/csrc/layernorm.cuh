@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     // Rows are taken last to first: the GEMM that wrote x finished with its
     // highest row blocks, which are the ones still in L2, and the GEMM that
     // reads y starts with the lowest rows, the ones written last here.
+    __shared__ float qtab_all[8][2][264];  // per warp: the activation quantizer's fl(q / s), see below
+    float(*qtab)[264] = qtab_all[threadIdx.x >> 5];
     const int64_t slot = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
     const int64_t row = p.m - 1 - slot;
     const int lane = threadIdx.x & 31;
@@ -231,6 +233,19 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
         // The quantizer sees the fp16 GEMM input, as in the unfused path.
         s_re = __fmul_rn(__frcp_rn(fmaxf(__half2float(__float2half_rn(amax_re)), 1e-5f)), qmax);
         s_im = __fmul_rn(__frcp_rn(fmaxf(__half2float(__float2half_rn(amax_im)), 1e-5f)), qmax);
+        // q takes the 2^act_bits integers in [qmin, qmax] and -0 (rint of a small
+        // negative h): the warp divides each once (IEEE, as per element) into its
+        // table, slot 2^act_bits holding fl(-0 / s)
+        const int nq = 1 << p.act_bits;
+        for (int t = lane; t < nq; t += 32) {
+            qtab[0][t] = __fdiv_rn(qmin + static_cast<float>(t), s_re);
+            qtab[1][t] = __fdiv_rn(qmin + static_cast<float>(t), s_im);
+        }
+        if (lane == 0) {
+            qtab[0][nq] = __fdiv_rn(-0.0f, s_re);
+            qtab[1][nq] = __fdiv_rn(-0.0f, s_im);
+        }
+        __syncwarp();
     }
     __half* yr = p.y + row * p.ldy;
 #pragma unroll
@@ -244,7 +259,8 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
                 const float s = (col + e < D / 2) ? s_re : s_im;
                 const float h = __half2float(__float2half_rn(o[e]));
                 const float q = fminf(fmaxf(rintf(__fmul_rn(h, s)), qmin), qmax);
-                o[e] = __fdiv_rn(q, s);
+                o[e] = qtab[(col + e < D / 2) ? 0 : 1][__float_as_uint(q) == 0x80000000u ? (1 << p.act_bits)
+                                                                                     : static_cast<int>(q - qmin)];
             }
         }
         if constexpr (VW == 4) {
