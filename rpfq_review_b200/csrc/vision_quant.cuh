@@ -78,32 +78,20 @@ __device__ __forceinline__ void vq_row_stats(const VisionQuantParams& p, const _
                                              float& amax_re, float& amax_im, float& esum) {
     const int lane = threadIdx.x & 31;
     float ar = 0.0f, ai = 0.0f, es = 0.0f;
-    // four 8-column chunks of each half per lane in flight, consumed in column order
-    for (int j00 = lane * 8; j00 < p.k_c; j00 += 4 * 256) {
-        uint4 vr[4], vi[4];
+    for (int j0 = lane * 8; j0 < p.k_c; j0 += 256) {
+        const uint4 vr = *reinterpret_cast<const uint4*>(row + j0);
+        const uint4 vi = *reinterpret_cast<const uint4*>(row + p.k_c + j0);
+        const __half2* hr = reinterpret_cast<const __half2*>(&vr);
+        const __half2* hi = reinterpret_cast<const __half2*>(&vi);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j0 = j00 + u * 256;
-            if (j0 < p.k_c) {
-                vr[u] = *reinterpret_cast<const uint4*>(row + j0);
-                vi[u] = *reinterpret_cast<const uint4*>(row + p.k_c + j0);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            if (j00 + u * 256 >= p.k_c) break;
-            const __half2* hr = reinterpret_cast<const __half2*>(&vr[u]);
-            const __half2* hi = reinterpret_cast<const __half2*>(&vi[u]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 r = __half22float2(hr[e]);
-                const float2 i = __half22float2(hi[e]);
-                ar = fmaxf(ar, fmaxf(fabsf(r.x), fabsf(r.y)));
-                ai = fmaxf(ai, fmaxf(fabsf(i.x), fabsf(i.y)));
-                if (energy) {
-                    es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.x, r.x), __fmul_rn(i.x, i.x)), kVisionEps)));
-                    es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.y, r.y), __fmul_rn(i.y, i.y)), kVisionEps)));
-                }
+        for (int e = 0; e < 4; ++e) {
+            const float2 r = __half22float2(hr[e]);
+            const float2 i = __half22float2(hi[e]);
+            ar = fmaxf(ar, fmaxf(fabsf(r.x), fabsf(r.y)));
+            ai = fmaxf(ai, fmaxf(fabsf(i.x), fabsf(i.y)));
+            if (energy) {
+                es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.x, r.x), __fmul_rn(i.x, i.x)), kVisionEps)));
+                es = __fadd_rn(es, __fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(r.y, r.y), __fmul_rn(i.y, i.y)), kVisionEps)));
             }
         }
     }
