@@ -176,7 +176,7 @@ class PackedViT(nn.Module):
         t = torch.arange(L, dtype=torch.int32, device=device).repeat(B)
         b = torch.arange(B, dtype=torch.int32, device=device).repeat_interleave(L)
         rows = torch.where(t < ntok, t, ntok + b * n_p + (t - ntok)).to(torch.int32)
-        if not torch.cuda.is_current_stream_capturing():
+        if torch.device(device).type != "cuda" or not torch.cuda.is_current_stream_capturing():
             cache.clear()
             cache[key] = (rows, t)
         return rows, t
