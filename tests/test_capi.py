@@ -146,3 +146,27 @@ def test_vision_attention_layernorm_validation():
     # LayerNorm gather: misaligned index array
     assert L.rpfq_layernorm_rows_sm100(16, 96, 10, 18, 16, 16, 16, 96, 10, 96, ctypes.c_float(1e-5), 0,
                                        None) == _lib.RPFQ_ERR_INVALID
+
+
+def test_patch_unfold_validation():
+    """rpfq_patch_unfold_sm100 rejects bad shapes, strides and alignment on the
+    host, before any device work (no GPU needed)."""
+    L = _lib.lib()
+    # images pointer, f32, batch, channels, height, width, patch, out pointer, ldp, stream
+    assert L.rpfq_patch_unfold_sm100(None, 0, 1, 3, 224, 224, 16, 16, 768, None) == _lib.RPFQ_ERR_INVALID
+    assert L.rpfq_patch_unfold_sm100(16, 0, 1, 3, 224, 224, 6, 16, 768, None) == _lib.RPFQ_ERR_INVALID  # patch % 4
+    assert b"multiple of 4" in L.rpfq_last_error()
+    assert L.rpfq_patch_unfold_sm100(16, 0, 1, 3, 224, 200, 16, 16, 768, None) == _lib.RPFQ_ERR_INVALID  # 16 ∤ 200
+    assert L.rpfq_patch_unfold_sm100(16, 0, 1, 3, 224, 224, 16, 16, 700, None) == _lib.RPFQ_ERR_INVALID  # ldp < 768
+    assert L.rpfq_patch_unfold_sm100(16, 0, 1, 3, 224, 224, 16, 16, 772, None) == _lib.RPFQ_ERR_INVALID  # ldp % 8
+    assert L.rpfq_patch_unfold_sm100(16, 0, 1, 3, 224, 224, 4, 16, 50, None) == _lib.RPFQ_ERR_INVALID  # ldp % 4
+    assert L.rpfq_patch_unfold_sm100(8, 0, 1, 3, 224, 224, 16, 16, 768, None) == _lib.RPFQ_ERR_INVALID  # alignment
+    assert b"16-byte aligned" in L.rpfq_last_error()
+    assert L.rpfq_patch_unfold_sm100(16, 0, 0, 3, 224, 224, 16, 16, 768, None) == _lib.RPFQ_OK  # no images
+
+
+def test_patch_unfold_wrapper_rejects_cpu_tensors():
+    import torch
+    from rpfq_review_b200 import ops
+    with pytest.raises(ValueError):
+        ops.patch_unfold(torch.zeros(1, 3, 32, 32), 16)
