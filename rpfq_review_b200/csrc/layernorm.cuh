@@ -15,6 +15,8 @@
 
 namespace rpfq {
 
+constexpr int kLnQtab = 264;  // quotient table slots per half: 2^8 values of q, -0, padding
+
 struct LayerNormParams {
     const float* x;       // [x_rows, ldx] fp32
     const __half* w;
@@ -66,7 +68,8 @@ __device__ __forceinline__ void load_row_part(const float* p, float (&v)[VW]) {
 // fp32 y32 (normalized, or with y32_prenorm the row before normalization).
 // PLAIN instances (row source x[row], fp16 output only: every LayerNorm of
 // the ViT / DeiT blocks) compile without the source selection.
-template <int D, bool PLAIN>
+// QUANT instances (act_bits > 0) carry the fused activation quantizer.
+template <int D, bool PLAIN, bool QUANT>
 __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormParams p) {
     static_assert(D % 32 == 0, "row length must be a multiple of 32");
     // VW consecutive floats per lane and step: element e of step j of lane l
@@ -77,8 +80,10 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     // Rows are taken last to first: the GEMM that wrote x finished with its
     // highest row blocks, which are the ones still in L2, and the GEMM that
     // reads y starts with the lowest rows, the ones written last here.
-    __shared__ float qtab_all[8][2][264];  // per warp: the activation quantizer's fl(q / s), see below
-    float(*qtab)[264] = qtab_all[threadIdx.x >> 5];
+    // per warp: the activation quantizer's fl(q / s), see below (dynamic shared
+    // memory, present only when act_bits > 0)
+    extern __shared__ float ln_qtab[];
+    float(*qtab)[kLnQtab] = reinterpret_cast<float(*)[kLnQtab]>(ln_qtab + (threadIdx.x >> 5) * 2 * kLnQtab);
     const int64_t slot = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
     const int64_t row = p.m - 1 - slot;
     const int lane = threadIdx.x & 31;
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     }
     if (p.y == nullptr) return;
     float s_re = 0.0f, s_im = 0.0f, qmax = 0.0f, qmin = 0.0f;
-    if (p.act_bits > 0) {
+    if (QUANT) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             amax_re = fmaxf(amax_re, __shfl_xor_sync(0xffffffffu, amax_re, o));
@@ -255,7 +260,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
 #pragma unroll
         for (int e = 0; e < VW; ++e) {
             o[e] = v[j][e];
-            if (p.act_bits > 0) {
+            if (QUANT) {
                 const float s = (col + e < D / 2) ? s_re : s_im;
                 const float h = __half2float(__float2half_rn(o[e]));
                 const float q = fminf(fmaxf(rintf(__fmul_rn(h, s)), qmin), qmax);

@@ -863,11 +863,15 @@ int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* a, rpfq_stream_t stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned nb = static_cast<unsigned>(blocks);
     const bool plain = !a->rows && !a->add && !a->merge_side && !a->y32;
+    // the fused quantizer's per-warp quotient tables (dynamic shared memory)
+    const bool quant = a->act_bits > 0;
+    const size_t qtab = quant ? static_cast<size_t>(warps) * 2 * kLnQtab * sizeof(float) : 0;
     switch (d) {
+#define RPFQ_LN_LAUNCH(D, PL, Q) launch_kernel(layernorm_f32_f16_kernel<D, PL, Q>, dim3(nb), dim3(warps * 32), qtab, s, 1, p)
 #define RPFQ_LN_CASE(D)                                                                                            \
     case D:                                                                                                        \
-        RPFQ_CUDA(plain ? launch_kernel(layernorm_f32_f16_kernel<D, true>, dim3(nb), dim3(warps * 32), 0, s, 1, p) \
-                        : launch_kernel(layernorm_f32_f16_kernel<D, false>, dim3(nb), dim3(warps * 32), 0, s, 1, p)); \
+        RPFQ_CUDA(plain ? (quant ? RPFQ_LN_LAUNCH(D, true, true) : RPFQ_LN_LAUNCH(D, true, false))                  \
+                        : (quant ? RPFQ_LN_LAUNCH(D, false, true) : RPFQ_LN_LAUNCH(D, false, false)));              \
         break;
         RPFQ_LN_CASE(96)
         RPFQ_LN_CASE(192)
@@ -877,6 +881,7 @@ int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* a, rpfq_stream_t stream) {
         RPFQ_LN_CASE(1536)
         RPFQ_LN_CASE(3072)
 #undef RPFQ_LN_CASE
+#undef RPFQ_LN_LAUNCH
         default:
             return fail(RPFQ_ERR_UNSUPPORTED,
                         "rpfq_layernorm_sm100: row length %d (supported: 96, 192, 384, 768, 1024, 1536, 3072)", d);
