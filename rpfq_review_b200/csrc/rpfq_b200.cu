@@ -1044,7 +1044,8 @@ int rpfq_vision_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, in
         p.grid = 0;
         const int64_t rows = images * tokens;
         const int64_t ctas = std::min<int64_t>((rows + 15) / 16, 8 * st->sm_count);
-        vision_quant_tokenwise_kernel<<<static_cast<unsigned>(ctas), kVisionThreads, 0, s>>>(p, rows);
+        RPFQ_CUDA(launch_kernel(vision_quant_tokenwise_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kVisionThreads), 0, s,
+                                1, p, rows));
         RPFQ_CUDA(cudaGetLastError());
         return RPFQ_OK;
     }
@@ -1074,14 +1075,17 @@ int rpfq_vision_act_quant_sm100(const uint16_t* x, int64_t ldx, uint16_t* xq, in
     VisionTokenStats* stats = static_cast<VisionTokenStats*>(workspace);
     float2* scales = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + 16 * rows);
     const int64_t stat_ctas = std::min<int64_t>((rows + 15) / 16, 16 * st->sm_count);
-    vision_stats_kernel<<<static_cast<unsigned>(stat_ctas), kVisionThreads, 0, s>>>(p, rows, stats);
+    RPFQ_CUDA(launch_kernel(vision_stats_kernel, dim3(static_cast<unsigned>(stat_ctas)), dim3(kVisionThreads), 0, s, 1, p,
+                            rows, stats));
     RPFQ_CUDA(cudaGetLastError());
     const int smem = 2 * patches * 4 + tokens;
-    vision_select_kernel<<<static_cast<unsigned>(images), kVisionThreads, smem, s>>>(p, stats, scales);
+    RPFQ_CUDA(launch_kernel(vision_select_kernel, dim3(static_cast<unsigned>(images)), dim3(kVisionThreads),
+                            static_cast<size_t>(smem), s, 1, p, stats, scales));
     RPFQ_CUDA(cudaGetLastError());
     const int64_t apply_ctas =
         std::min<int64_t>((rows + 16 * kVisionApplyRun - 1) / (16 * kVisionApplyRun), 2 * st->sm_count);  // resident CTAs
-    vision_apply_kernel<<<static_cast<unsigned>(apply_ctas), kVisionThreads, 0, s>>>(p, rows, scales);
+    RPFQ_CUDA(launch_kernel(vision_apply_kernel, dim3(static_cast<unsigned>(apply_ctas)), dim3(kVisionThreads), 0, s, 1, p,
+                            rows, scales));
     RPFQ_CUDA(cudaGetLastError());
     return RPFQ_OK;
 }

@@ -23,6 +23,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "ptx.cuh"
+
 namespace rpfq {
 
 constexpr int kVisionThreads = 512;
@@ -180,6 +182,8 @@ constexpr int kVisionApplyRun = 4;  // consecutive rows per warp (one image's ba
 // grid = 0: one warp per token, no shared state (any token count).
 __global__ void __launch_bounds__(kVisionThreads) vision_quant_tokenwise_kernel(const VisionQuantParams p,
                                                                                int64_t rows) {
+    pdl_wait();  // the producer of x (or of the statistics) has completed
+    pdl_launch_dependents();
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kVisionThreads / 32);
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * (kVisionThreads / 32) + (threadIdx.x >> 5); r < rows;
          r += warps) {
@@ -203,6 +207,8 @@ struct VisionTokenStats {
 
 __global__ void __launch_bounds__(kVisionThreads) vision_stats_kernel(const VisionQuantParams p, int64_t rows,
                                                                      VisionTokenStats* stats) {
+    pdl_wait();  // the producer of x (or of the statistics) has completed
+    pdl_launch_dependents();
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kVisionThreads / 32);
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * (kVisionThreads / 32) + (threadIdx.x >> 5); r < rows;
          r += warps) {
@@ -217,6 +223,8 @@ __global__ void __launch_bounds__(kVisionThreads) vision_stats_kernel(const Visi
 // Dynamic shared memory: 2 floats per patch (energy then score, contrast) + 1 byte per token.
 __global__ void __launch_bounds__(kVisionThreads) vision_select_kernel(const VisionQuantParams p,
                                                                       const VisionTokenStats* stats, float2* scales) {
+    pdl_wait();  // the producer of x (or of the statistics) has completed
+    pdl_launch_dependents();
     extern __shared__ float vsm[];
     const int T = p.tokens;
     const int P = T - 1;
@@ -283,6 +291,8 @@ __global__ void __launch_bounds__(kVisionThreads) vision_select_kernel(const Vis
 // One warp per row (no index division), 16 bytes per lane and step.
 __global__ void __launch_bounds__(kVisionThreads) vision_apply_kernel(const VisionQuantParams p, int64_t rows,
                                                                      const float2* scales) {
+    pdl_wait();  // the producer of x (or of the statistics) has completed
+    pdl_launch_dependents();
     __shared__ float qtab[kVisionThreads / 32][2][256];  // per warp: fl(q / s) of the scales it holds
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float(*tab)[256] = qtab[warp];
