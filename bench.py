@@ -4,12 +4,14 @@
 Workload: ViT-B/16 at 224x224, 12 layers, d = 768,
 12 heads, MLP 3072, 1000 classes; every linear a 2-bit phase-quantized
 complex layer packed from seeded random init; fp16 activations; a batch of
-256 synthetic N(0, 1) images per GPU. One step = one forward of that batch
-(49 packed GEMMs + patch-embedding GEMM through the tcgen05 kernel, attention
-/ LayerNorm through PyTorch), replayed from a CUDA graph. Multi-GPU: one
-process per GPU (torchrun), a full weight replica per rank, images sharded by
-rank (weak scaling: 256 images per GPU), and one NCCL all-gather of the
-logits per step.
+256 synthetic N(0, 1) images. One step = one forward of that batch (49
+packed GEMMs + the patch-embedding GEMM through the tcgen05 kernel, LayerNorm
+through the library, attention through cuDNN SDPA), replayed from a CUDA
+graph. Multi-GPU: one process per GPU (torchrun), a full weight replica per
+rank, the global batch of 256 split contiguously by rank (strong scaling:
+256 / N images per GPU; ``--batch B`` is the weak mode, B per GPU), and one
+NCCL all-gather of the logits per step; rank 0 recomputes the last rank's
+shard and checks the gathered logits bit for bit.
 
 Reported (one JSON line on rank 0):
 * value — images/s over all ranks, device-timed (CUDA events, max over ranks);
@@ -17,11 +19,16 @@ Reported (one JSON line on rank 0):
   host->device copy of the images and the device->host copy of the logits
   inside the timed region;
 * roofline — the GEMM kernel: algorithmic flops (2 M K N per launch) over its
-  CUDA-event durations inside the timed region, against the measured
-  sustained bf16/fp16 tensor peak;
+  CUDA-event durations in a forward replayed right after the timed region,
+  against the measured burst bf16/fp16 tensor peak (fraction of the
+  sustained figure beside it);
 * cpu_baseline — the reference's own C++ CPU runtime for the packed layer
   (oracle/_ref, fp16 coefficient cache, all host threads) plus PyTorch CPU
-  for the rest of the forward, on a bounded sample of images.
+  for the rest of the forward, on a bounded sample of images; beside it
+  (cpu_baseline_legs) the reference's PyTorch runtime forward with F.linear
+  on the dequantized fp32 weights;
+* torch_cublas_arm (1 GPU) — the reference's PyTorch path on the same GPU:
+  cuBLAS F.linear on the dequantized fp16 weights, one CUDA graph.
 
 ``--impl reference`` runs only that CPU implementation (rank 0) and prints
 its line with ``"impl": "reference"``.
@@ -53,7 +60,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--model", default="vit_base_patch16_224")
-    ap.add_argument("--batch", type=int, default=256, help="images per GPU")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="images per step over all ranks, split by rank (strong scaling; default: the model's "
+                         "BASELINE configuration, ViT-B/16 256, ViT-L/16 2048)")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU (weak scaling; overrides --global-batch)")
     ap.add_argument("--act-bits", type=int, default=0)
     ap.add_argument("--attention", default="sdpa", choices=["sdpa", "rpfq"],
                     help="ViT / DeiT attention: PyTorch SDPA (cuDNN) or the library's tcgen05 kernel")
@@ -65,6 +75,9 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=1, help="images per CPU-baseline step")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline in the GPU arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--torch-arm", action=argparse.BooleanOptionalAction, default=True,
+                    help="(1 GPU) also time the reference's PyTorch path on this GPU: cuBLAS F.linear on the "
+                         "dequantized fp16 weights, torch LayerNorm / SDPA / GELU, one CUDA graph")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--gemm", default=None, help="M,N,K: time one packed layer instead of the model")
     ap.add_argument("--block-n", type=int, default=0, help="GEMM tile width for --gemm (0 = automatic)")
@@ -130,12 +143,20 @@ class ClockSampler:
         self.window = (t0, t1)
 
     def start(self):
+        """Start sampling and wait (up to 3 s) for the first sample, so that a
+        short warm-up and timed region are covered."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and self.proc.poll() is None:
+            if os.path.getsize(self.file.name) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -177,11 +198,14 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU side
-def cpu_forward_factory(cfg, model, threads: int):
+def cpu_forward_factory(cfg, model, threads: int, linear_path: str = "auto"):
     """CPU forward of the same model on host cores: every packed linear through
     the reference's C++ runtime (fp16 coefficient cache, wide_linear_cache_neon.cpp
     path, prepared once like the reference loader) when oracle/_ref is built
-    ("reference"), else through the oracle's dense restatement ("port");
+    ("reference"), else — or with ``linear_path="torch"`` — ``F.linear`` on the
+    export-dequantized fp32 weight (``quantized_forward_weight``,
+    export_rpfq_vit_to_mlx.py:336-375), which is the reference's own PyTorch
+    runtime forward (audit_rpfq_vit_ios_parity.py:630-688) restated ("port");
     attention / LayerNorm / GELU through PyTorch CPU in float32."""
     import numpy as np
     import torch
@@ -191,7 +215,7 @@ def cpu_forward_factory(cfg, model, threads: int):
     from oracle import packed_ref as pr
 
     torch.set_num_threads(threads)
-    kind = "reference" if ref_lib.load() is not None else "port"
+    kind = "reference" if linear_path == "auto" and ref_lib.load() is not None else "port"
     linears = {}
     for name, mod in model.quantized_linears():
         np_layer = vit_ref.packed_to_numpy(mod.packed())
@@ -296,6 +320,7 @@ def run_reference(args):
 
     cfg = model_config(args.model)
     threads = os.cpu_count() or 1
+    gb, _, scaling = batch_plan(args, cfg, args.gpus, 0)
     # Same seeded weights as the GPU arm, packed on the CPU (no CUDA involved).
     model = build_model(cfg, "cpu", args, prepack=False)
     forward, kind = cpu_forward_factory(cfg, model, threads)
@@ -305,50 +330,195 @@ def run_reference(args):
         times = time_cpu(forward, images, args.steps, args.warmup)
     total = sum(times)
     value = args.cpu_sample * len(times) / total
+    what = ("the reference C++ fp16-cache runtime (oracle/_ref)" if kind == "reference" else
+            "F.linear on the export-dequantized fp32 weights (restated reference PyTorch runtime forward)")
     line = {
         "metric": METRIC, "value": value, "unit": "images/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": len(times), "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic N(0,1) images, seeded random-init packed weights",
-        "config": {"workload": f"{cfg.name} packed 2-bit phase inference (CPU sample)",
-                   "images_per_step": args.cpu_sample, "tokens": cfg.tokens, "act_bits": args.act_bits},
+        "config": {"workload": f"{cfg.name} inference, packed {args.code_bits}-bit complex-phase linears (2 "
+                               f"residual stages, {args.weights} weights), global batch {gb}: bounded CPU sample",
+                   "images_per_step": args.cpu_sample, "global_batch": gb, "tokens": cfg.tokens,
+                   "act_bits": args.act_bits},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind,
                          "sample": f"{args.cpu_sample} image(s) per step of the {cfg.name} forward; packed "
-                                   f"linears through the reference C++ fp16-cache runtime "
-                                   f"(oracle/_ref), rest through PyTorch CPU fp32"},
+                                   f"linears through {what}, rest through PyTorch CPU fp32"},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
     return 0
 
 
+def cpu_baselines(cfg, model, args):
+    """The GPU arm's CPU baselines on the host cores (all threads), each a
+    bounded sample of the same model: the reference's C++ fp16-cache runtime
+    for the packed linears (the headline ``cpu_baseline``, the same
+    implementation as ``--impl reference``) and, beside it, the reference's
+    PyTorch runtime forward with F.linear on the dequantized fp32 weights
+    (BASELINE B4; B2 is its per-layer contraction)."""
+    import torch
+    threads = os.cpu_count() or 1
+    gc = torch.Generator().manual_seed(99)
+    sample = torch.randn(args.cpu_sample, 3, cfg.img, cfg.img, generator=gc).half()
+    out = {}
+    for leg in ("auto", "torch"):
+        try:
+            forward, kind = cpu_forward_factory(cfg, model, threads, linear_path=leg)
+            with torch.no_grad():
+                times = time_cpu(forward, sample, steps=50, warmup=1, budget_s=args.cpu_seconds)
+            what = ("the reference C++ fp16-cache runtime (oracle/_ref)" if kind == "reference" else
+                    "F.linear on the export-dequantized fp32 weights (the reference's PyTorch runtime "
+                    "forward, restated)")
+            out[leg] = {"value": args.cpu_sample * len(times) / sum(times), "unit": "images/s", "cores": threads,
+                        "kind": kind,
+                        "sample": f"{len(times)} forward(s) of {args.cpu_sample} image(s) of {cfg.name}; packed "
+                                  f"linears through {what}, rest PyTorch CPU fp32"}
+        except Exception as e:  # a baseline is reported, never required
+            out[leg] = {"value": None, "unit": "images/s", "cores": threads, "kind": "port",
+                        "sample": f"failed: {type(e).__name__}: {e}"}
+    legs = {"torch_dense_fp32": out["torch"]}
+    if out["auto"]["kind"] == "port":  # oracle/_ref absent: the torch leg is the only one
+        return out["torch"], legs
+    return out["auto"], legs
+
+
+def torch_cublas_arm(cfg, model, images, args):
+    """The reference's PyTorch path on this GPU, as the fastest plain-PyTorch
+    form of it: every quantized linear as cuBLAS ``F.linear`` on its
+    dequantized fp16 weight (the dense coefficient matrix, which is
+    ``quantized_forward_weight``'s block layout), torch LayerNorm, SDPA and
+    exact GELU, an fp16 residual stream, the whole forward in one CUDA graph,
+    on the same images. Times it like the main leg and reports its logits'
+    distance from the packed path's."""
+    import torch
+    import torch.nn.functional as F
+
+    from rpfq_review_b200.vit import ViTConfig
+    if not isinstance(cfg, ViTConfig):
+        return None
+    dev = images.device
+    lin = {name: (mod.prepack().contiguous(), mod.packed().bias.to(torch.float16)) for name, mod in
+           model.quantized_linears()}
+    d, H, L, eps = cfg.dim, cfg.heads, cfg.tokens, cfg.eps
+    ntok = 2 if cfg.distilled else 1
+    pw, pb = model.patch_w, model.patch_b
+    cls_t, pos = model.cls_tokens, model.pos_embed
+    norms = [(b.norm1_w, b.norm1_b, b.norm2_w, b.norm2_b) for b in model.blocks]
+
+    def forward(img):
+        B = img.shape[0]
+        p = cfg.patch
+        pt = img.reshape(B, 3, cfg.img // p, p, cfg.img // p, p).permute(0, 2, 4, 1, 3, 5).reshape(B, -1, 3 * p * p)
+        x = torch.cat((cls_t.expand(B, -1, -1), F.linear(pt, pw, pb)), 1) + pos
+        for i in range(cfg.depth):
+            n1w, n1b, n2w, n2b = norms[i]
+            h = F.layer_norm(x, (d,), n1w, n1b, eps)
+            qkv = F.linear(h, *lin[f"blocks.{i}.qkv"]).view(B, L, 3, H, d // H).permute(2, 0, 3, 1, 4)
+            a = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2]).transpose(1, 2).reshape(B, L, d)
+            x = x + F.linear(a, *lin[f"blocks.{i}.proj"])
+            h = F.layer_norm(x, (d,), n2w, n2b, eps)
+            x = x + F.linear(F.gelu(F.linear(h, *lin[f"blocks.{i}.fc1"])), *lin[f"blocks.{i}.fc2"])
+        c = F.layer_norm(x[:, :ntok], (d,), model.norm_w, model.norm_b, eps)
+        logits = F.linear(c[:, 0], *lin["head"]).float()
+        if cfg.distilled:
+            logits = (logits + F.linear(c[:, 1], *lin["head_dist"]).float()) / 2
+        return logits
+
+    with torch.no_grad():
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                forward(images)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = forward(images)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        ours = model(images)
+        torch.cuda.synchronize(dev)
+        diff = float((out - ours).abs().max() / ours.abs().max().clamp_min(1e-30))
+    del graph
+    B = images.shape[0]
+    return {"value": B / (ms / 1000.0), "unit": "images/s", "ms_per_step": ms, "steps": args.steps,
+            "what": "cuBLAS F.linear on the dequantized fp16 weights + torch LayerNorm / SDPA / GELU, fp16 "
+                    "residual stream, one CUDA graph, same GPU and images",
+            "logits_max_abs_diff_over_max": diff}
+
+
+# Global batch of each model's BASELINE configuration (configs[1] ViT-B/16
+# 256, configs[2] DeiT-S largest sweep point 512, configs[3] Swin-T 128,
+# configs[4] ViT-L/16 2048 over 8 GPUs), split across the ranks.
+DEFAULT_GLOBAL_BATCH = {"vit_base_patch16_224": 256, "deit_small_distilled_patch16_224": 512,
+                        "swin_tiny_patch4_window7_224": 128, "vit_large_patch16_224": 2048}
+
+
+def batch_plan(args, cfg, world: int, rank: int):
+    """(global batch, this rank's [start, end) slice, scaling mode). Strong
+    scaling by default: one global batch split contiguously by rank
+    (``dist.shard_range``); ``--batch B`` is the weak mode, B images per GPU."""
+    from rpfq_review_b200 import dist as rdist
+    if args.batch is not None:
+        gb = args.batch * world
+        mode = "weak"
+    else:
+        gb = args.global_batch if args.global_batch is not None else DEFAULT_GLOBAL_BATCH.get(cfg.name, 256)
+        mode = "strong"
+    if gb < world:
+        raise SystemExit(f"global batch {gb} is smaller than the {world} ranks")
+    return gb, rdist.shard_range(gb, world, rank), mode
+
+
+def global_images(cfg, gb: int, start: int, end: int, device):
+    """Images [start, end) of the seeded synthetic global batch (N(0, 1),
+    fp16): every rank draws the same global batch and keeps its slice, so a
+    shard's images do not depend on the world size."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(1000)
+    return torch.randn(gb, 3, cfg.img, cfg.img, device=device, generator=g)[start:end].half().contiguous()
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
 
+    from rpfq_review_b200 import dist as rdist
     from rpfq_review_b200 import ops
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = rdist.env_rank_world()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        rdist.init("nccl", timeout_s=120, device=dev)
 
     cfg = model_config(args.model)
-    B = args.batch
+    gb, (s0, s1), scaling = batch_plan(args, cfg, world, rank)
+    B = s1 - s0
     model = build_model(cfg, dev, args)
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    images = torch.randn(B, 3, cfg.img, cfg.img, device=dev, generator=g).half()
-    gathered = torch.empty((world * B, cfg.classes), dtype=torch.float32, device=dev) if world > 1 else None
+    images = global_images(cfg, gb, s0, s1, dev)
+    gather = rdist.LogitsGather(gb, cfg.classes, world, rank, device=dev) if world > 1 else None
 
-    timer = ops.LaunchTimer()
+    # Two graphs of the same forward: the timed one without instrumentation
+    # (its kernels chain through programmatic launch edges), and one with a
+    # CUDA event pair around every GEMM, replayed after the timed region for
+    # the per-GEMM times of the roofline.
+    timer = ops.LaunchTimer(events=False)
+    gemm_timer = ops.LaunchTimer(events=True)
     use_graph = not args.no_graph
     graph = None
+    graph_t = None
     static_out = None
     if use_graph:
         side = torch.cuda.Stream(dev)
@@ -361,22 +531,25 @@ def run_b200(args):
         ops.set_launch_timer(timer)
         with torch.cuda.graph(graph):
             static_out = model(images)
+        graph_t = torch.cuda.CUDAGraph()
+        ops.set_launch_timer(gemm_timer)
+        with torch.cuda.graph(graph_t, pool=graph.pool()):
+            model(images)
         ops.set_launch_timer(None)
         launches_per_step = timer.launches
 
         def step():
             graph.replay()
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, static_out)
+            if gather is not None:
+                gather(static_out)
             return static_out
     else:
         def step():
-            timer.gemm_events.clear()
             ops.set_launch_timer(timer)
             out = model(images)
             ops.set_launch_timer(None)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, out)
+            if gather is not None:
+                gather(out)
             return out
         timer.launches = 0
         step()
@@ -405,24 +578,49 @@ def run_b200(args):
     torch.cuda.cudart().cudaProfilerStop()
     clocks.mark(t_wall0, t_wall1)
     clk = clocks.stop()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    # per-GEMM event times from the instrumented forward (after the timed region)
+    for _ in range(3):
+        if graph_t is not None:
+            graph_t.replay()
+        else:
+            gemm_timer.gemm_events.clear()
+            ops.set_launch_timer(gemm_timer)
+            model(images)
+            ops.set_launch_timer(None)
+    torch.cuda.synchronize(dev)
+    gemm_ms, gemm_flops = gemm_timer.gemm_ms_and_flops()  # last replay's launches
     if args.gemm_breakdown and rank == 0:
-        for s_ev, e_ev, fl in timer.gemm_events:
+        for s_ev, e_ev, fl in gemm_timer.gemm_events:
             ms_ = s_ev.elapsed_time(e_ev)
             print(f"gemm {fl / 1e9:8.2f} GFLOP {ms_ * 1000:8.1f} us {fl / ms_ / 1e9:7.1f} TFLOP/s", file=sys.stderr)
-    elapsed_ms = ev0.elapsed_time(ev1)
-    gemm_ms, gemm_flops = timer.gemm_ms_and_flops()  # last step's launches
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    value = world * B * args.steps / (max_ms / 1000.0)
+    max_ms = rdist.max_over_ranks(elapsed_ms, dev)
+    gemm_ms_max = rdist.max_over_ranks(gemm_ms, dev)
+    value = gb * args.steps / (max_ms / 1000.0)
+
+    # ---- the gathered logits against a recomputation: rank 0 runs the last
+    # rank's shard through its own replica (same shard size, so the same
+    # kernels and tile plans) and compares bit for bit.
+    gather_check = None
+    if gather is not None:
+        gathered = gather.out.clone()
+        if rank == 0:
+            t0_, t1_ = rdist.shard_range(gb, world, world - 1)
+            other = global_images(cfg, gb, t0_, t1_, dev)
+            mine = model(other)
+            torch.cuda.synchronize(dev)
+            gather_check = {"recomputed_rank": world - 1, "images": t1_ - t0_,
+                            "bit_identical": bool(torch.equal(mine, gathered[t0_:t1_])),
+                            "own_rows_bit_identical": bool(torch.equal(static_out if use_graph else model(images),
+                                                                       gathered[s0:s1]))}
+        barrier()
 
     # ---- end to end through the public API: pinned host images -> logits on host.
     # Every step copies its images in and its logits out inside the timed
     # region; the next step's images travel on a copy stream into the other of
     # two input buffers while the current step computes (a second graph reads
-    # the second buffer).
-    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    # the second buffer). Same step count as the device-timed leg.
+    e2e_steps = args.e2e_steps or args.steps
     host_imgs = images.cpu().pin_memory()
     host_outs = [torch.empty((B, cfg.classes), dtype=torch.float32).pin_memory() for _ in range(2)]
     images2 = torch.empty_like(images)
@@ -434,19 +632,22 @@ def run_b200(args):
         def step_on(buf):
             (graph if buf == 0 else graph2).replay()
             out = static_out if buf == 0 else static_out2
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, out)
+            if gather is not None:
+                gather(out)
             return out
     else:
         def step_on(buf):
             out = model(images if buf == 0 else images2)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, out)
+            if gather is not None:
+                gather(out)
             return out
     bufs = [images, images2]
     copy_stream = torch.cuda.Stream(dev)
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
+    for s_ in range(2):  # warm the second graph and the copy path
+        bufs[s_ % 2].copy_(host_imgs, non_blocking=True)
+        host_outs[s_ % 2].copy_(step_on(s_ % 2), non_blocking=True)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -472,44 +673,37 @@ def run_b200(args):
     e1.record()
     barrier()
     host_out = host_outs[(e2e_steps - 1) % 2]
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * e2e_steps / (float(te.item()) / 1000.0)
+    e2e_ms = rdist.max_over_ranks(e0.elapsed_time(e1), dev)
+    e2e_value = gb * e2e_steps / (e2e_ms / 1000.0)
 
     # sanity: the logits are finite
     finite = bool(torch.isfinite(host_out).all())
 
     if world > 1:
-        if graph is not None:
-            del graph
+        del graph, graph_t
+        if use_graph:
+            del graph2
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:
         return 0
 
     peaks, peak_src = load_peaks()
-    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    # The timed region lasts well under the seconds a power-capped loop needs
+    # to settle, so the GEMMs are held to the burst cuBLAS figure; the
+    # fraction of the sustained figure is reported beside it.
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
     flops_img = cfg.gemm_flops_per_image()
 
     cpu = None
-    if not args.no_cpu_baseline:
-        try:
-            threads = os.cpu_count() or 1
-            forward, kind = cpu_forward_factory(cfg, model, threads)
-            gc = torch.Generator().manual_seed(99)
-            sample = torch.randn(args.cpu_sample, 3, cfg.img, cfg.img, generator=gc).half()
-            with torch.no_grad():
-                times = time_cpu(forward, sample, steps=50, warmup=1, budget_s=args.cpu_seconds)
-            cpu = {"value": args.cpu_sample * len(times) / sum(times), "unit": "images/s", "cores": threads,
-                   "kind": kind,
-                   "sample": f"{len(times)} forward(s) of {args.cpu_sample} image(s) of {cfg.name}; packed linears "
-                             f"through {'the reference C++ fp16-cache runtime (oracle/_ref)' if kind == 'reference' else 'the oracle dense restatement'}, "
-                             "rest PyTorch CPU fp32"}
-        except Exception as e:  # the baseline is reported, never required
-            cpu = {"value": None, "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
-                   "sample": f"failed: {type(e).__name__}: {e}"}
+    legs = None
+    if not args.no_cpu_baseline and world == 1:
+        cpu, legs = cpu_baselines(cfg, model, args)
+    cublas = None
+    if args.torch_arm and world == 1:
+        cublas = torch_cublas_arm(cfg, model, images, args)
 
     traffic = _gemm_traffic(cfg, B, args)
     line = {
@@ -521,38 +715,47 @@ def run_b200(args):
         "warmup": args.warmup,
         "ms_per_step": max_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "f16",
-        "data": "synthetic: N(0,1) images (seeded per rank), random-init weights packed to 2-bit phase codes",
+        "data": "synthetic: one seeded N(0,1) global image batch sliced by rank, random-init weights packed to "
+                "2-bit phase codes",
         "config": {
             "workload": f"{cfg.name} inference, packed {args.code_bits}-bit complex-phase linears (2 residual "
-                        f"stages, {args.weights} weights), batch {B} per GPU",
+                        f"stages, {args.weights} weights), global batch {gb} over {world} GPU(s)",
             "code_bits": args.code_bits, "weights": args.weights,
-            "batch_per_gpu": B, "global_batch": world * B, "tokens": cfg.tokens, "act_bits": args.act_bits,
+            "global_batch": gb, "batch_per_gpu": B, "shards": rdist.shard_sizes(gb, world),
+            "tokens": cfg.tokens, "act_bits": args.act_bits,
             "act_quantizer": "vision-aware int8 (token saliency)" if args.vision_quant else
                              (f"ActivationQuantSTE {args.act_bits}-bit" if args.act_bits else "none"),
-            "parallelism": f"dp{world} (weight replica per rank, NCCL all-gather of logits)",
+            "parallelism": f"dp{world} (weight replica per rank, {scaling} scaling, NCCL all-gather of logits)",
             "l2": ("per-step working set (activations of the GEMMs, >= 77 MB each) far larger than the 126 MB L2"
                    if B * cfg.tokens * cfg.dim * 2 >= 64e6 else
-                   "small batch: activations and packed weights are L2-resident across steps (latency-bound regime)"),
+                   "small per-GPU batch: activations and packed weights partly L2-resident across steps"),
             "cuda_graph": use_graph,
         },
-        "gemm": {"tflops": achieved, "flops_per_image": flops_img,
-                 "ms_per_step": gemm_ms, "share_of_step": (gemm_ms / (max_ms / args.steps)) if gemm_ms else None},
+        "gemm": {"tflops": achieved, "flops_per_image": flops_img, "ms_per_step": gemm_ms,
+                 "ms_per_step_max_over_ranks": gemm_ms_max,
+                 "share_of_step": (gemm_ms / (max_ms / args.steps)) if gemm_ms else None},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if achieved else None,
+                     "frac_of_sustained": (achieved / peak_sus) if achieved else None,
                      "traffic": traffic["bytes_per_launch"] if traffic else None,
                      "traffic_detail": traffic,
-                     "peak_source": f"{peak_src} bf16_tflops_sustained (cuBLAS, power-capped loop)",
+                     "peak_source": f"{peak_src} bf16_tflops (burst cuBLAS; the timed region is "
+                                    f"{max_ms / 1000:.2f} s, shorter than the power-capped loop of the "
+                                    f"sustained figure {peak_sus:.0f})",
                      "kernel": "gemm_f16_sm100_kernel (tcgen05, 256x256 tiles on CTA pairs)"},
-        "e2e": {"value": e2e_value, "unit": "images/s",
-                "h2d_bytes_per_step": int(host_imgs.numel() * host_imgs.element_size()),
-                "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size())},
+        "e2e": {"value": e2e_value, "unit": "images/s", "steps": e2e_steps,
+                "h2d_bytes_per_step": int(host_imgs.numel() * host_imgs.element_size()) * world,
+                "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size()) * world},
         "gpu_launches": int(launches_per_step * args.steps),
         "clocks": clk,
         "logits_finite": finite,
+        "gather_check": gather_check,
         "cpu_baseline": cpu,
+        "cpu_baseline_legs": legs,
+        "torch_cublas_arm": cublas,
     }
     print(json.dumps(line))
     return 0

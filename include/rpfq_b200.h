@@ -78,7 +78,7 @@ typedef struct RpfqPackedLinear {
 /* K1 — decode a packed layer into the dense fp16 coefficient matrix
  * dense[2 n_c, 2 k_c] = [[rr, ir], [ri, ii]] (row-major), the B operand of
  * rpfq_gemm_sm100. Bit-exact with the reference's fp16 coefficient cache:
- * buildFusedWideLinearCache, RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.cpp:117-166
+ * buildFusedWideLinearCache, RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.cpp:84-133
  * (rounding = RPFQ_ROUND_TIES_AWAY reproduces its floatToHalfBits, :91-115;
  * RPFQ_ROUND_NEAREST_EVEN is the IEEE conversion). Runs once per layer. */
 int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32_t rounding,
@@ -213,7 +213,7 @@ int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* args, rpfq_stream_t stream)
 
 /* Whole layer — QATLinearComplexPhase.forward on packed weights
  * (RPFQ-ViT-main/quant_models/quant_i.py:513-554; Android wideLinear,
- * phase_linear.cpp:279-326): optional activation quantization, then the
+ * phase_linear.cpp:209-258): optional activation quantization, then the
  * tcgen05 GEMM over the dense coefficients `dense` (from rpfq_prepack_sm100),
  * bias and optional GELU / residual in the epilogue. With dense == NULL and
  * m <= 256 (2-bit codes, n_c and k_c multiples of 8) the layer runs the fused

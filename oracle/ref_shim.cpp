@@ -10,7 +10,7 @@
 //
 // The shim builds a SafeTensorStore in memory (the same struct the reference
 // fills from a safetensors file, safetensors_loader.h:10-18) and calls
-// loadWideParams (phase_linear.cpp:160-187) with the argument meaning used by
+// loadWideParams (phase_linear.cpp:90-117) with the argument meaning used by
 // the reference engine (rpfq_vit_engine.cpp:240-275): real dims, padded
 // complex dims, and the unpadded complex output count.
 
@@ -87,9 +87,9 @@ extern "C" {
 
 const char* rpfq_ref_last_error() { return g_error.c_str(); }
 
-// mode 0: wideLinearReference (scalar, fp32, phase_linear.cpp:236-277)
+// mode 0: wideLinearReference (scalar, fp32, phase_linear.cpp:166-207)
 // mode 1: wideLinearOptimized (fused scalar, phase_linear_fused.cpp:120-148)
-// mode 2: fp16 coefficient cache (wide_linear_cache_neon.cpp:237-327)
+// mode 2: fp16 coefficient cache (wide_linear_cache_neon.cpp:69-161)
 int rpfq_ref_wide_linear(const float* x, int tokens, int n_c, int k_c, int n_cp, int k_cp,
                          const uint8_t* const* codes, const uint16_t* const* gamma_re,
                          const uint16_t* const* gamma_im, const uint16_t* bias,
@@ -117,7 +117,7 @@ int rpfq_ref_wide_linear(const float* x, int tokens, int n_c, int k_c, int n_cp,
 }
 
 // Four fp16 coefficient planes [n_c, k_c] from buildFusedWideLinearCache
-// (phase_linear_cache.cpp:117-166): rr = XrToRe, ir = XiToRe, ri = XrToIm,
+// (phase_linear_cache.cpp:84-133): rr = XrToRe, ir = XiToRe, ri = XrToIm,
 // ii = XiToIm.
 int rpfq_ref_coefficient_planes(int n_c, int k_c, int n_cp, int k_cp,
                                 const uint8_t* const* codes, const uint16_t* const* gamma_re,
@@ -140,7 +140,7 @@ int rpfq_ref_coefficient_planes(int n_c, int k_c, int n_cp, int k_cp,
 
 // Prepared layer for repeated timing of the fp16-cache path (the CPU baseline):
 // the cache is built once, as the reference runtime does at load time
-// (phase_linear.cpp:183-185), and only the GEMM is timed.
+// (phase_linear.cpp:113-115), and only the GEMM is timed.
 void* rpfq_ref_prepare(int n_c, int k_c, int n_cp, int k_cp, const uint8_t* const* codes,
                        const uint16_t* const* gamma_re, const uint16_t* const* gamma_im,
                        const uint16_t* bias) {

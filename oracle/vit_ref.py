@@ -13,7 +13,7 @@ linear uses the dense weight reconstructed from its packed planes by
 
 ``fp16=True`` (``extract_weights``) rounds the dense coefficients through
 fp16, i.e. the reference runtime's fused fp16 coefficient cache
-(RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.cpp:117-166,
+(RPFQ-ViTAndroid/app/src/main/cpp/kernels/phase_linear_cache.cpp:84-133,
 round-to-nearest-even here); ``fp16_act=True`` (``vit_forward``) rounds the
 activations that configs[1] keeps in fp16 — every LayerNorm output (GEMM
 input), the qkv output, the softmax probabilities, the attention output and

@@ -4,11 +4,11 @@
 //
 // rr: x_re -> y_re, ir: x_im -> y_re, ri: x_re -> y_im, ii: x_im -> y_im.
 // Per element the stage values are decoded with a float32 reciprocal of the
-// fp16 gamma (phase_linear.cpp:152-153 of the reference Android runtime) and
+// fp16 gamma (phase_linear.cpp:82-83 of the reference Android runtime) and
 // summed left to right in float32 in the order of buildFusedWideLinearCache
-// (phase_linear_cache.cpp:152-159): U stages first, then W stages. The sum is
+// (phase_linear_cache.cpp:119-126): U stages first, then W stages. The sum is
 // rounded to fp16 either to nearest even (IEEE, default) or with ties away
-// from zero (the reference's floatToHalfBits, phase_linear_cache.cpp:91-115),
+// from zero (the reference's floatToHalfBits, phase_linear_cache.cpp:58-82),
 // so both are reproducible bit for bit.
 //
 // 2-bit codes use the reference codebook 0:-1, 1:+1, 2:-i, 3:+i

@@ -1260,12 +1260,15 @@ extern "C" int rpfq_wide_linear_noalloc_sm100(const RpfqWideLinearArgs* a, rpfq_
     RpfqWideLinearArgs local = *a;
     local.scratch = nullptr;
     if (a->act_bits != 0) {
-        const size_t need = static_cast<size_t>(a->m) * 2 * static_cast<size_t>(a->layer->k_c) * sizeof(uint16_t);
-        if (need > kNoAllocScratchBytes)
+        // rows that fit: compared by division, so no product of caller sizes can wrap
+        const int64_t row_bytes = 2 * static_cast<int64_t>(a->layer->k_c) * static_cast<int64_t>(sizeof(uint16_t));
+        const int64_t max_rows = static_cast<int64_t>(kNoAllocScratchBytes) / row_bytes;
+        if (a->m > max_rows)
             return fail(RPFQ_ERR_INVALID,
-                        "rpfq_wide_linear_noalloc_sm100: the quantized activations need %zu bytes (m=%lld x %d fp16) "
-                        "but the built-in scratch holds %zu; use rpfq_wide_linear_sm100 with a caller buffer",
-                        need, (long long)a->m, 2 * a->layer->k_c, kNoAllocScratchBytes);
+                        "rpfq_wide_linear_noalloc_sm100: the quantized activations of m=%lld rows x %d fp16 do not fit "
+                        "the built-in scratch of %zu bytes (at most %lld rows for this layer); use "
+                        "rpfq_wide_linear_sm100 with a caller buffer",
+                        (long long)a->m, 2 * a->layer->k_c, kNoAllocScratchBytes, (long long)max_rows);
         uint16_t* scratch = nullptr;
         rc = noalloc_scratch(&scratch);
         if (rc) return rc;

@@ -44,18 +44,66 @@ def shard_range(global_batch: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
-def gather_logits(local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """All-gather equal-sized per-rank logits ``[b, C]`` into ``[world * b, C]``
-    in rank order (one collective)."""
-    world = dist.get_world_size()
-    if out is None:
-        out = torch.empty((world * local.shape[0], *local.shape[1:]), dtype=local.dtype, device=local.device)
+def shard_sizes(global_batch: int, world: int) -> list[int]:
+    """Images per rank under :func:`shard_range`."""
+    return [e - s for s, e in (shard_range(global_batch, world, r) for r in range(world))]
+
+
+class LogitsGather:
+    """All-gather of per-rank logits ``[b_r, C]`` (rank r holding the rows
+    :func:`shard_range` gives it) into ``[global_batch, C]`` in image order,
+    with one collective per call.
+
+    Equal shards gather straight into the output. Uneven shards (a global
+    batch that ``world`` does not divide) are padded to ``ceil(B / world)``
+    rows in a staging buffer, gathered, and the padding rows dropped. All
+    buffers are allocated once, so a step can reuse them."""
+
+    def __init__(self, global_batch: int, classes: int, world: int, rank: int, dtype=torch.float32,
+                 device: torch.device | str = "cpu"):
+        self.global_batch, self.world, self.rank = global_batch, world, rank
+        self.sizes = shard_sizes(global_batch, world)
+        self.cap = max(self.sizes) if self.sizes else 0
+        self.even = all(s == self.cap for s in self.sizes)
+        self.out = torch.empty((global_batch, classes), dtype=dtype, device=device)
+        if self.even:
+            self.send = self.recv = None
+        else:
+            self.send = torch.zeros((self.cap, classes), dtype=dtype, device=device)
+            self.recv = torch.empty((world * self.cap, classes), dtype=dtype, device=device)
+
+    def __call__(self, local: torch.Tensor) -> torch.Tensor:
+        if local.shape[0] != self.sizes[self.rank]:
+            raise ValueError(f"rank {self.rank} holds {self.sizes[self.rank]} images of the global batch, "
+                             f"got logits for {local.shape[0]}")
+        if self.even:
+            _all_gather(self.out, local.contiguous(), self.world)
+            return self.out
+        self.send[: local.shape[0]].copy_(local)
+        _all_gather(self.recv, self.send, self.world)
+        start = 0
+        for r, n in enumerate(self.sizes):
+            self.out[start:start + n].copy_(self.recv[r * self.cap:r * self.cap + n])
+            start += n
+        return self.out
+
+
+def _all_gather(out: torch.Tensor, local: torch.Tensor, world: int) -> None:
     if dist.get_backend() == "nccl":
-        dist.all_gather_into_tensor(out, local.contiguous())
+        dist.all_gather_into_tensor(out, local)
     else:
-        parts = list(out.chunk(world, dim=0))
-        dist.all_gather(parts, local.contiguous())
-    return out
+        dist.all_gather(list(out.chunk(world, dim=0)), local)
+
+
+def gather_logits(local: torch.Tensor, global_batch: int | None = None) -> torch.Tensor:
+    """All-gather per-rank logits into ``[global_batch, C]`` in image order
+    (one collective). ``global_batch`` defaults to ``world * local rows``
+    (equal shards); with a global batch that does not divide by the world
+    size, each rank passes the rows :func:`shard_range` gave it."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if global_batch is None:
+        global_batch = world * local.shape[0]
+    return LogitsGather(global_batch, local.shape[1], world, rank, local.dtype, local.device)(local)
 
 
 def max_over_ranks(value: float, device: torch.device) -> float:

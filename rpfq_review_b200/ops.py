@@ -30,14 +30,18 @@ def _stream(device: torch.device) -> int:
 
 
 class LaunchTimer:
-    """Optional instrumentation: CUDA events around every GEMM launch and a
-    count of every kernel this library launches. Events are created with
-    ``external=True`` so that they become event-record nodes when the launches
-    are captured into a CUDA graph (timings are then those of the last replay)."""
+    """Optional instrumentation: a count of every kernel this library launches
+    and, with ``events=True``, CUDA events around every GEMM launch. Events
+    are created with ``external=True`` so that they become event-record nodes
+    when the launches are captured into a CUDA graph (timings are then those
+    of the last replay). Event nodes sit between the kernel nodes and so cut
+    the programmatic (PDL) chaining of consecutive launches: time a graph
+    captured with ``events=False`` and read GEMM times from a separate one."""
 
-    def __init__(self):
+    def __init__(self, events: bool = True):
         self.gemm_events: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
         self.launches = 0
+        self.events = events
 
     def gemm_ms_and_flops(self) -> tuple[float, int]:
         ms = sum(s.elapsed_time(e) for s, e, _ in self.gemm_events)
@@ -334,7 +338,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                           y=y2.data_ptr(), ldy=ldy, m=m, n=n, k=k, activation=_ACT[activation], block_n=block_n,
                           flags=_flags(out, r2, bias), cta_pair=cta_pair, split_k=split_k, workspace=ws,
                           workspace_bytes=ws_bytes)
-    timer = _timer
+    timer = _timer if _timer is not None and _timer.events else None
     with torch.cuda.device(x.device):
         if timer is not None:
             ev0 = torch.cuda.Event(enable_timing=True, external=True)
@@ -516,7 +520,7 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
                                 act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch),
                                 flags=_flags(out, r2, bias), split_k=split_k, workspace=ws,
                                 workspace_bytes=ws_bytes)
-    timer = _timer
+    timer = _timer if _timer is not None and _timer.events else None
     with torch.cuda.device(x.device):
         if timer is not None:
             # With act_bits > 0 the span also holds the quantization kernel.

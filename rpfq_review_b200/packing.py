@@ -3,7 +3,7 @@ layers, and the key/shape contract of the reference exporter.
 
 The layout is the one the reference exporter writes and its mobile runtimes
 read (RPFQ-ViTApple/scripts/export_rpfq_vit_to_mlx.py:148-159,189-224,384-423;
-RPFQ-ViTAndroid/app/src/main/cpp/ops/phase_linear.cpp:112-187):
+RPFQ-ViTAndroid/app/src/main/cpp/ops/phase_linear.cpp:42-117):
 
 * per residual stage ``s`` of U and of W:
   ``{u,w}_s{s}.codes`` uint8 ``[n_cp, k_cp * code_bits / 8]`` (codes LSB-first;
@@ -88,7 +88,7 @@ class PackedLayer:
     def from_state_dict(sd: dict, prefix: str, in_features: int, out_features: int,
                         code_bits: int = 2) -> "PackedLayer":
         """Read an exporter-layout layer and validate shapes like the reference
-        loader (phase_linear.cpp:112-158): codes ``[n_cp, k_cp/4]``, gammas
+        loader (phase_linear.cpp:42-88): codes ``[n_cp, k_cp/4]``, gammas
         ``[n_cp, k_cp/256]``, ``k_cp % 256 == 0``, no zero gamma."""
         if in_features % 2 or out_features % 2:
             raise ValueError("Complex-phase layers require even in/out features.")

@@ -170,3 +170,19 @@ def test_patch_unfold_wrapper_rejects_cpu_tensors():
     from rpfq_review_b200 import ops
     with pytest.raises(ValueError):
         ops.patch_unfold(torch.zeros(1, 3, 32, 32), 16)
+
+
+def test_noalloc_size_guard_on_host():
+    """rpfq_wide_linear_noalloc_sm100 refuses, before any device work, an m
+    whose quantized activations exceed its built-in scratch — including an m
+    so large that m * 2 k_c * 2 bytes would wrap a 64-bit product."""
+    L = _lib.lib()
+    s = _lib.RpfqPackedLinear(n_c=384, k_c=384, n_cp=512, k_cp=512, stages=2, code_bits=2)
+    for arr in (s.u, s.w):
+        for i in range(2):
+            arr[i].codes, arr[i].gamma_real, arr[i].gamma_imag = 4096, 8192, 12288
+    a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=16, x=32, ldx=768, y=48, ldy=768, act_bits=4)
+    for m in ((8 << 20) // (768 * 2) + 1, (1 << 64) // (768 * 2) + 1):
+        a.m = m
+        assert L.rpfq_wide_linear_noalloc_sm100(ctypes.byref(a), None) == _lib.RPFQ_ERR_INVALID
+        assert b"scratch" in L.rpfq_last_error()

@@ -27,18 +27,24 @@ def _toy_logits(images: torch.Tensor) -> torch.Tensor:
     return images.reshape(images.shape[0], -1) @ w
 
 
-def _worker(rank, world, port, mode, results):
+def _worker(rank, world, port, mode, results, batch=12):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     try:
         rdist.init("gloo", timeout_s=10 if mode == "fail" else 60)
         g = torch.Generator().manual_seed(1)
-        images = torch.randn(12, 3, 4, 4, generator=g)
+        images = torch.randn(batch, 3, 4, 4, generator=g)
         s, e = rdist.shard_range(images.shape[0], world, rank)
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the collective")
         local = _toy_logits(images[s:e])
-        gathered = rdist.gather_logits(local)
+        if mode == "reuse":
+            # the gather object of a step loop: buffers allocated once, two calls
+            gather = rdist.LogitsGather(batch, local.shape[1], world, rank)
+            gather(local * 0)
+            gathered = gather(local)
+        else:
+            gathered = rdist.gather_logits(local, batch)
         tmax = rdist.max_over_ranks(float(rank + 1), torch.device("cpu"))
         results[rank] = ("ok", torch.equal(gathered, _toy_logits(images)), tmax)
     except Exception as exc:  # reported to the parent
@@ -50,12 +56,12 @@ def _worker(rank, world, port, mode, results):
             pass
 
 
-def _run(world, mode):
+def _run(world, mode, batch=12):
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     results = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, results, batch)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -87,6 +93,23 @@ def test_gather_equals_single_process(world):
         status, equal, tmax = res[r]
         assert status == "ok" and equal
         assert tmax == float(world)  # max over ranks of (rank + 1)
+
+
+@pytest.mark.parametrize("world,batch,mode", [(4, 10, "ok"), (3, 7, "reuse"), (2, 12, "reuse")])
+def test_gather_uneven_shards(world, batch, mode):
+    """A global batch that the world size does not divide (10 images over 4
+    ranks: 3, 3, 2, 2) gathers into image order like the equal case."""
+    res = _run(world, mode, batch)
+    assert len(res) == world
+    for r in range(world):
+        status, equal, _ = res[r]
+        assert status == "ok" and equal
+
+
+def test_shard_sizes():
+    assert rdist.shard_sizes(10, 4) == [3, 3, 2, 2]
+    assert rdist.shard_sizes(256, 8) == [32] * 8
+    assert rdist.shard_sizes(2048, 8) == [256] * 8
 
 
 def test_failed_rank_is_detected_not_hung():

@@ -95,7 +95,7 @@ def test_oracle_vs_reference_cpp_golden():
 
 def test_exhaustive_code_decode():
     """All 256 byte values x 4 lanes: unpack matches get2BitCode
-    (phase_linear.cpp:85-89) and the codebook of dequantize_axis
+    (phase_linear.cpp:15-19, 145-153) and the codebook of dequantize_axis
     (export…py:236-247): 0:-1, 1:+1, 2:-i, 3:+i."""
     byte = np.arange(256, dtype=np.uint8).reshape(256, 1)
     codes = pr.unpack_codes(byte, 256, 4)
@@ -145,7 +145,7 @@ def test_synthetic_generator_seeded():
 
 
 def test_packed_state_dict_validation():
-    """from_state_dict validates like loadPhaseParams (phase_linear.cpp:112-158)."""
+    """from_state_dict validates like loadPhaseParams (phase_linear.cpp:42-88)."""
     from rpfq_review_b200.packing import PackedLayer, random_packed
     layer = random_packed(40, 72, seed=1)
     sd = layer.state_dict("blk.")
