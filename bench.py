@@ -608,11 +608,20 @@ def run_b200(args):
             t0_, t1_ = rdist.shard_range(gb, world, world - 1)
             other = global_images(cfg, gb, t0_, t1_, dev)
             mine = model(other)
+            # the whole global batch on this one GPU (the 1-GPU run's logits)
+            whole = torch.cat([model(global_images(cfg, gb, a, min(a + 256, gb), dev)) for a in range(0, gb, 256)])
             torch.cuda.synchronize(dev)
+            diff = (whole - gathered).abs().max() / whole.abs().max().clamp_min(1e-30)
             gather_check = {"recomputed_rank": world - 1, "images": t1_ - t0_,
                             "bit_identical": bool(torch.equal(mine, gathered[t0_:t1_])),
                             "own_rows_bit_identical": bool(torch.equal(static_out if use_graph else model(images),
-                                                                       gathered[s0:s1]))}
+                                                                       gathered[s0:s1])),
+                            "vs_one_gpu_batch": {"bit_identical": bool(torch.equal(whole, gathered)),
+                                                 "max_abs_diff_over_max": float(diff),
+                                                 "top1_agree": float((whole.argmax(1) == gathered.argmax(1))
+                                                                     .float().mean()),
+                                                 "one_gpu_batch": min(gb, 256)}}
+            del whole
         barrier()
 
     # ---- end to end through the public API: pinned host images -> logits on host.

@@ -96,11 +96,19 @@ int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32
  * Split-K: when few output tiles would leave most SMs idle (small m), the
  * K dimension of each tile is split over a cluster of up to 8 CTAs whose
  * fp32 partials meet in `workspace` (device memory, 16-byte aligned, at
- * least rpfq_gemm_workspace_bytes(m, n, k) bytes; it holds no state between
- * calls, but calls that run concurrently need their own). With workspace ==
- * NULL the call never splits. split_k: 0 = automatic, 1 = never, 2..8 = that
- * many splits (needs the workspace). The partials are summed in a fixed
- * order: results are deterministic. */
+ * least rpfq_gemm_workspace_bytes(m, n, k) bytes; calls that run
+ * concurrently need their own). Stream-K: when the 256 x 256 tiles of CTA
+ * pairs fill at least one wave but not a whole number of waves, the k-blocks
+ * of the last one to two waves are shared out evenly over all pairs and a
+ * tile cut between two pairs meets in the same workspace; its last 8192
+ * bytes are flag words that must be zero before the first call (allocate the
+ * workspace zeroed) and that every call which completes without a device
+ * error leaves zero. rpfq_gemm_workspace_bytes(0, 0, 0) is a size that fits
+ * every shape. With workspace == NULL the call neither splits nor uses
+ * stream-K. split_k: 0 = automatic, 1 = never, 2..8 = that many splits
+ * (needs the workspace). Partials are summed in a fixed order: results are
+ * deterministic for a given shape. RPFQ_STREAM_K=0 in the environment turns
+ * the stream-K tail off. */
 typedef struct RpfqGemmArgs {
     const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements)                */
     int64_t ldx;
@@ -118,7 +126,7 @@ typedef struct RpfqGemmArgs {
     int32_t cta_pair;         /* 0 = automatic; 1 = one CTA per tile; 2 = CTA pairs      */
     int32_t split_k;          /* 0 = automatic; 1 = off; 2..8 = K splits per tile       */
     int32_t reserved;
-    void* workspace;          /* split-K partials, or NULL (no split)                   */
+    void* workspace;          /* split-K / stream-K partials and flags, or NULL         */
     uint64_t workspace_bytes;
 } RpfqGemmArgs;
 int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
@@ -127,6 +135,20 @@ int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream);
  * largest amount any shape uses, so one buffer of that size serves every
  * call on a stream. */
 uint64_t rpfq_gemm_workspace_bytes(int64_t m, int32_t n, int32_t k);
+
+/* The tile plan rpfq_gemm_sm100 would run for these arguments (validated the
+ * same way; nothing is launched and no memory is touched). A diagnostic with
+ * no counterpart in the reference: benchmarks and tests read which schedule
+ * a shape takes. */
+typedef struct RpfqGemmPlan {
+    int32_t block_n;         /* tile width: 128 or 256                                    */
+    int32_t cta_pair;        /* 1: one CTA per 128-row tile, 2: CTA pairs, 256-row tiles  */
+    int32_t split_k;         /* K splits per tile (1: none)                               */
+    int32_t stream_k_tiles;  /* tiles of the stream-K tail (0: whole tiles only)          */
+    int32_t units;           /* persistent CTAs / CTA pairs (split-K: tiles)             */
+    int32_t tiles;           /* output tiles                                              */
+} RpfqGemmPlan;
+int rpfq_gemm_plan_sm100(const RpfqGemmArgs* args, RpfqGemmPlan* plan);
 
 /* Activation quantization of a complex input (per row, Re and Im halves
  * separately), fp16 in / fp16 out. Replaces ActivationQuantSTE.forward

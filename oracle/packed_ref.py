@@ -89,7 +89,7 @@ def pack_codes(codes: np.ndarray) -> np.ndarray:
 
 
 def unpack_codes(packed: np.ndarray, out_dim: int, in_dim: int) -> np.ndarray:
-    """Inverse of :func:`pack_codes` (EXP:234-240; PL:85-89 ``get2BitCode``)."""
+    """Inverse of :func:`pack_codes` (EXP:234-240; PL:15-19 ``get2BitCode``)."""
     p = packed.reshape(out_dim, in_dim // 4)
     c = np.stack([(p >> s) & 0x03 for s in (0, 2, 4, 6)], axis=-1)
     return c.reshape(out_dim, in_dim).astype(np.uint8)
@@ -221,7 +221,7 @@ def dense_weight_from_packed(packed: dict, n_c: int, k_c: int) -> np.ndarray:
 
 def f32_to_f16_ties_away(s: np.ndarray) -> np.ndarray:
     """float32 -> fp16 rounding ties away from zero, as the reference's
-    ``floatToHalfBits`` (PLC:91-115): truncate the mantissa and add one ulp
+    ``floatToHalfBits`` (PLC:58-82): truncate the mantissa and add one ulp
     when the first dropped bit is set; overflow -> inf; subnormals likewise."""
     bits = np.ascontiguousarray(s, dtype=np.float32).view(np.uint32).astype(np.int64)
     sign = (bits >> 16) & 0x8000
@@ -269,7 +269,7 @@ def phase_tables(code_bits: int):
 def decode_plane(packed: dict, name: str, n_c: int, k_c: int, code_bits: int = 2):
     """One plane -> float32 (re, im) on the valid region ``[n_c, k_c]``.
 
-    2-bit: the reference codebook with ``1.0f / gamma`` (PL:152-153, PL:218-223).
+    2-bit: the reference codebook with ``1.0f / gamma`` (PL:82-83, PL:145-153).
     3/4-bit extension: ``(cos_c / gamma_real, sin_c / gamma_imag)`` with
     ``cos_c = cos(2 pi c / 2^b)`` in float32, each product rounded once.
     """
@@ -293,11 +293,11 @@ def decode_plane(packed: dict, name: str, n_c: int, k_c: int, code_bits: int = 2
 
 def coefficient_planes(packed: dict, n_c: int, k_c: int, rounding: str = "rne",
                        code_bits: int = 2) -> dict[str, np.ndarray]:
-    """Four fp16 coefficient planes, the B200 B operand (PLC:117-166).
+    """Four fp16 coefficient planes, the B200 B operand (PLC:84-133).
 
     Follows ``buildFusedWideLinearCache``: per element the stage values are
-    decoded with ``1.0f / gamma`` in float32 (PL:152-153) and summed left to
-    right in float32 (PLC:152-159), U stages first, then W stages:
+    decoded with ``1.0f / gamma`` in float32 (PL:82-83) and summed left to
+    right in float32 (PLC:119-126), U stages first, then W stages:
 
     * ``rr = u0Re + u1Re + w0Re + w1Re``   (x_re -> y_re)
     * ``ir = -u0Im - u1Im + w0Im + w1Im`` (x_im -> y_re)
@@ -306,7 +306,7 @@ def coefficient_planes(packed: dict, n_c: int, k_c: int, rounding: str = "rne",
 
     (the reference fixes 2 stages; other stage counts extend the same order).
     The reference converts to fp16 with ties rounded away from zero
-    (``floatToHalfBits``, PLC:91-115): ``rounding="ties_away"`` reproduces it
+    (``floatToHalfBits``, PLC:58-82): ``rounding="ties_away"`` reproduces it
     bit for bit. ``rounding="rne"`` (default) rounds to nearest even, the IEEE
     default; the two differ only on exact ties.
     """
@@ -386,7 +386,7 @@ def wide_linear(x: np.ndarray, dense: np.ndarray, bias=None, act_bits: int | Non
 
 def max_rel_err(y: np.ndarray, ref: np.ndarray) -> float:
     """``max|y - ref| / max|ref|`` — the relative-error measure used by the
-    parity tests (the reference's own check is an absolute max, PL:295-307)."""
+    parity tests (the reference's own check is an absolute max, PL:225-245)."""
     ref = np.asarray(ref, np.float64)
     denom = max(float(np.abs(ref).max()), 1e-30)
     return float(np.abs(np.asarray(y, np.float64) - ref).max() / denom)

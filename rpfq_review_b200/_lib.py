@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "rpfq_prepack_sm100",
     "rpfq_gemm_sm100",
     "rpfq_gemm_workspace_bytes",
+    "rpfq_gemm_plan_sm100",
     "rpfq_act_quant_sm100",
     "rpfq_patch_unfold_sm100",
     "rpfq_layernorm_sm100",
@@ -50,6 +51,11 @@ EXPORTED_SYMBOLS = (
     "rpfq_device_error",
     "rpfq_version",
 )
+
+
+class RpfqGemmPlan(ctypes.Structure):
+    _fields_ = [("block_n", ctypes.c_int32), ("cta_pair", ctypes.c_int32), ("split_k", ctypes.c_int32),
+                ("stream_k_tiles", ctypes.c_int32), ("units", ctypes.c_int32), ("tiles", ctypes.c_int32)]
 
 
 class RpfqPhasePlane(ctypes.Structure):
@@ -139,6 +145,7 @@ def lib() -> ctypes.CDLL:
         L.rpfq_gemm_sm100.argtypes = [ctypes.POINTER(RpfqGemmArgs), P]
         L.rpfq_gemm_workspace_bytes.argtypes = [I64, I32, I32]
         L.rpfq_gemm_workspace_bytes.restype = ctypes.c_uint64
+        L.rpfq_gemm_plan_sm100.argtypes = [ctypes.POINTER(RpfqGemmArgs), ctypes.POINTER(RpfqGemmPlan)]
         L.rpfq_act_quant_sm100.argtypes = [P, I64, P, I64, I64, I32, I32, P]
         L.rpfq_patch_unfold_sm100.argtypes = [P, I32, I64, I32, I32, I32, I32, P, I64, P]
         L.rpfq_layernorm_sm100.argtypes = [P, I64, P, P, P, I64, I64, I32, ctypes.c_float, I32, P]
@@ -158,7 +165,8 @@ def lib() -> ctypes.CDLL:
                                              ctypes.POINTER(RpfqPhasePlaneOut), P, ctypes.c_uint64, P]
         L.rpfq_last_error.restype = ctypes.c_char_p
         L.rpfq_device_error.argtypes = [ctypes.POINTER(I32)]
-        for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_act_quant_sm100", "rpfq_layernorm_sm100",
+        for name in ("rpfq_prepack_sm100", "rpfq_gemm_sm100", "rpfq_gemm_plan_sm100", "rpfq_act_quant_sm100",
+                     "rpfq_layernorm_sm100",
                      "rpfq_layernorm_rows_sm100", "rpfq_layernorm_ex_sm100",
                      "rpfq_wide_linear_sm100", "rpfq_wide_linear_noalloc_sm100", "rpfq_pack_linear_sm100",
                      "rpfq_vision_act_quant_sm100", "rpfq_attention_sm100", "rpfq_window_attention_sm100",

@@ -40,6 +40,27 @@
 // barrier (release / acquire) each CTA reduces 1/S of the tile over the S
 // partials in the fixed order 0..S-1 (deterministic) and applies bias, GELU
 // and residual to it.
+//
+// Stream-K tail (p.sk_tiles > 0; CTA pairs or single CTAs, no split-K): when
+// the tiles do not fill whole waves of the persistent grid, the last
+// sk_tiles tiles (between one and two waves' worth) are not dealt out whole.
+// Their k-blocks, in tile order, are cut into one contiguous share per unit
+// (a CTA pair or a CTA): every unit first runs its data-parallel tiles, then
+// its share. A share is at least one tile long, so a tile is cut at most
+// once, into a head (its first k-blocks, the end of one unit's share) and a
+// tail (the rest, the start of the next unit's share). A unit runs its head
+// first (right after its data-parallel tiles), then its whole tiles, then its
+// tail. The head's unit writes its raw fp32 accumulator to its workspace
+// slot in the epilogue warps' own layout and raises one flag per epilogue
+// warp. For the tail, the epilogue warps wait for the flags (bounded, like
+// every wait here) and load that accumulator into the tail's TMEM buffer
+// (tcgen05.st) while the item before it is still in its main loop, and the
+// MMAs continue on it: a cut tile goes through exactly the operations of an
+// uncut one, so the result is the same bit for bit whatever the schedule (an
+// image's outputs do not depend on the batch around it). Then the usual
+// epilogue runs and the reader clears the flags. All units are resident at
+// once (the grid is the co-resident cluster count), and a head never waits
+// for anything, so every wait ends.
 #pragma once
 
 #include "ptx.cuh"
@@ -57,11 +78,119 @@ struct GemmParams {
     int32_t activation;
     int32_t bias_f32;        // bias holds fp32 values (no per-element conversion in the epilogue)
     int32_t splits;          // K splits per tile (1: none; > 1 only with PAIR = false, cluster = splits)
-    float* ws;               // split-K partials: [tiles * splits][128 * BN] fp32 (splits > 1)
+    float* ws;               // split-K partials: [tiles * splits][128 * BN] fp32 (splits > 1);
+                             // stream-K partials: [units * ranks][128 * BN] fp32 (sk_tiles > 0)
     void* y;                 // the output (y's dtype, row stride ldy): split-K stores it directly
     int64_t ldy;
     int* err;                // device error word
+    int32_t sk_tiles;        // stream-K: tiles shared out by k-blocks over all units (0: none)
+    int* sk_flags;           // stream-K: [units * ranks][8] flags (partial of an epilogue warp written); zero
+                             // between calls
 };
+
+// One unit's work list: data-parallel tiles (strided over the units), then
+// its contiguous share of the stream-K k-blocks. Every role of the CTA walks
+// the same list.
+struct WorkItem {
+    int tile;
+    int kb_lo, kb_hi;  // k-blocks [kb_lo, kb_hi) of the tile
+    int mode;          // kItemWhole, kItemHead or kItemTail
+};
+// kItemHead: k-blocks [0, kb_hi < num_k) of a cut tile, the accumulator goes to
+// the workspace; kItemTail: k-blocks [kb_lo > 0, num_k), the accumulator starts
+// from the head's and the epilogue follows.
+enum : int { kItemWhole = 0, kItemHead = 1, kItemTail = 2 };
+
+struct Schedule {
+    int units, num_k, dp_tiles, dp_kb_lo, dp_kb_hi;
+    int next_dp;
+    int64_t lo, hi;          // this unit's stream-K k-blocks [lo, hi)
+    int64_t whole, whole_end;  // whole tiles of the share: [whole, whole_end) in k-blocks
+    int phase;               // 0 data-parallel, 1 head, 2 whole tiles, 3 tail, 4 done
+
+    __device__ __forceinline__ Schedule(int unit, int units_, int num_tiles, int num_k_, int sk_tiles, int kb_lo,
+                                        int kb_hi)
+        : units(units_), num_k(num_k_), dp_tiles(num_tiles - sk_tiles), dp_kb_lo(kb_lo), dp_kb_hi(kb_hi),
+          next_dp(unit), phase(0) {
+        const int64_t total = static_cast<int64_t>(sk_tiles) * num_k;
+        lo = static_cast<int64_t>(unit) * total / units_;
+        hi = static_cast<int64_t>(unit + 1) * total / units_;
+        whole = (lo + num_k - 1) / num_k * num_k;  // first tile boundary at or after lo
+        whole_end = hi / num_k * num_k;            // last tile boundary at or before hi
+    }
+
+    __device__ __forceinline__ void set(WorkItem& w, int64_t a, int64_t b, int mode) const {
+        const int j = static_cast<int>(a / num_k);
+        w.tile = dp_tiles + j;
+        w.kb_lo = static_cast<int>(a - static_cast<int64_t>(j) * num_k);
+        w.kb_hi = static_cast<int>(b - static_cast<int64_t>(j) * num_k);
+        w.mode = mode;
+    }
+
+    // Order of a share: the head first (the next unit's tail waits for it), whole
+    // tiles, the tail last (it waits for the previous unit's head).
+    __device__ __forceinline__ bool next(WorkItem& w) {
+        if (phase == 0) {
+            if (next_dp < dp_tiles) {
+                w.tile = next_dp;
+                w.kb_lo = dp_kb_lo;
+                w.kb_hi = dp_kb_hi;
+                w.mode = kItemWhole;
+                next_dp += units;
+                return true;
+            }
+            phase = lo < hi ? 1 : 4;
+        }
+        if (phase == 1) {
+            phase = 2;
+            if (whole_end < hi) {  // ends inside a tile
+                set(w, whole_end, hi, kItemHead);
+                return true;
+            }
+        }
+        if (phase == 2) {
+            if (whole < whole_end) {
+                set(w, whole, whole + num_k, kItemWhole);
+                whole += num_k;
+                return true;
+            }
+            phase = 3;
+        }
+        if (phase == 3) {
+            phase = 4;
+            if (lo % num_k != 0) {  // starts inside a tile
+                set(w, lo, (lo / num_k + 1) * num_k, kItemTail);
+                return true;
+            }
+        }
+        return false;
+    }
+};
+
+// Stream-K flag handshake (one flag per epilogue warp and partial).
+__device__ __forceinline__ void sk_signal(int* flag) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
+}
+__device__ __forceinline__ int sk_poll(const int* flag) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+}
+// Bounded wait for a partial; false (error word = site, abort raised) when the
+// limit runs out or another role has raised abort.
+__device__ __forceinline__ bool sk_wait(const int* flag, volatile int* abort_flag, int* gerr, int site) {
+    if (sk_poll(flag)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (sk_poll(flag)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicCAS(gerr, 0, site);
+            return false;
+        }
+    }
+}
 
 // RES = residual slots per epilogue warp: 0 (no residual), 1 (the residual
 // step lands in the single staging slot just before it is used: fine when a
@@ -261,7 +390,8 @@ __global__ void __launch_bounds__(384, 1)
     uint64_t* tempty_bar = bars + 2 * C::STAGES + 2; // [2]
     uint64_t* drain_bar = bars + 2 * C::STAGES + 4;  // [1] teardown drain of MMAs
     uint64_t* res_bar = bars + 2 * C::STAGES + 5;    // [EPI_WARPS * 2] residual slot landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 5 + 2 * C::EPI_WARPS);
+    uint64_t* loaded_bar = bars + 2 * C::STAGES + 5 + 2 * C::EPI_WARPS;  // [1] stream-K tail: head loaded into TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 6 + 2 * C::EPI_WARPS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -281,6 +411,10 @@ __global__ void __launch_bounds__(384, 1)
     const int kb_lo = split * num_k / splits;
     const int kb_hi = (split + 1) * num_k / splits;
     const bool use_res = p.residual != nullptr && splits == 1;  // split-K adds the residual in its reduction
+    // units: CTA pairs or CTAs (split-K: tiles); stream-K only without split-K
+    constexpr int RANKS = PAIR ? 2 : 1;
+    const int sk_tiles = splits == 1 ? p.sk_tiles : 0;
+    auto schedule = [&]() { return Schedule(first_tile, tile_step, num_tiles, num_k, sk_tiles, kb_lo, kb_hi); };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -293,6 +427,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         mbar_init(drain_bar, 1);
         for (int b = 0; b < 2 * C::EPI_WARPS; ++b) mbar_init(&res_bar[b], 1);
+        mbar_init(loaded_bar, PAIR ? 2 * C::EPI_WARPS : C::EPI_WARPS);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&tm_x);
@@ -325,10 +460,13 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+            Schedule sched = schedule();
+            WorkItem w;
+            while (ok && sched.next(w)) {
+                const int tile = w.tile;
                 const int m0 = (tile / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
                 const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * C::B_ROWS;
-                for (int kb = kb_lo; kb < kb_hi; ++kb) {
+                for (int kb = w.kb_lo; kb < w.kb_hi; ++kb) {
                     if (!wait_bar(&empty_bar[stage], phase ^ 1, abort_flag, p.err, 101)) {
                         ok = false;
                         break;
@@ -385,11 +523,17 @@ __global__ void __launch_bounds__(384, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+            Schedule sched = schedule();
+            WorkItem w;
+            while (ok && sched.next(w)) {
                 if (!wait_bar<PAIR>(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, 201)) break;
+                // a stream-K tail continues from the head's accumulator, which the
+                // epilogue warps (of both CTAs of a pair) load into this buffer first
+                const bool cont = w.mode == kItemTail;
+                if (cont && !wait_bar<PAIR>(loaded_bar, 0, abort_flag, p.err, 204)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = kb_lo; kb < kb_hi; ++kb) {
+                for (int kb = w.kb_lo; kb < w.kb_hi; ++kb) {
                     if (!wait_bar(&full_bar[stage], phase, abort_flag, p.err, 202)) {
                         ok = false;
                         break;
@@ -401,10 +545,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                     for (int kk = 0; kk < C::BK / 16; ++kk) {
                         // +32 B per K step of 16 fp16 inside the 128-B swizzle row
+                        const bool accumulate = cont || (kb - w.kb_lo) + kk != 0;
                         if constexpr (PAIR)
-                            umma_f16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb - kb_lo) + kk != 0);
+                            umma_f16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, accumulate);
                         else
-                            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb - kb_lo) + kk != 0);
+                            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, accumulate);
                     }
                     commit_both(&empty_bar[stage]);
                     if (++stage == C::STAGES) {
@@ -432,20 +577,24 @@ __global__ void __launch_bounds__(384, 1)
             // box per column half) when tile i's accumulator is complete, i.e.
             // about two main loops before the epilogue reads it.
             constexpr int PCW = OUT_F32 ? 32 : 64;  // residual box: 32 rows x 128 B
-            auto prefetch_tile = [&](int t) {
-                if (t >= num_tiles) return;
+            auto prefetch_item = [&](const WorkItem& it) {
+                if (it.mode == kItemHead) return;  // no epilogue output
+                const int t = it.tile;
                 const int r0 = (t / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
                 const int c0 = (t % num_n) * BN;
                 for (int c = c0; c < c0 + BN && c < p.n; c += PCW)
                     for (int r = r0; r < r0 + C::BM && r < p.m; r += 32) tma_prefetch_l2_2d(&tm_r, c, r);
             };
-            prefetch_tile(first_tile);
-            prefetch_tile(first_tile + tile_step);
+            Schedule lead = schedule();  // two items ahead of the accumulators
+            WorkItem wl;
+            for (int i = 0; i < 2 && lead.next(wl); ++i) prefetch_item(wl);
+            Schedule sched = schedule();
+            WorkItem w;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+            while (sched.next(w)) {
                 if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 401)) break;
-                prefetch_tile(tile + 2 * tile_step);
+                if (lead.next(wl)) prefetch_item(wl);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1;
@@ -481,29 +630,104 @@ __global__ void __launch_bounds__(384, 1)
         // the accumulator is released to the leader's MMA warp (both CTAs' warps)
         const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
         const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
-        for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+        // stream-K partials and flags of this CTA's unit (slot = unit * RANKS + rank)
+        constexpr int NS = HALF / 32;  // 32-column partial steps per warp
+        const size_t sk_slot = static_cast<size_t>(first_tile) * RANKS + rank;
+        // the previous unit's head (same rank, rows and columns, same layout) into
+        // accumulator buffer `buf`; false when the bounded wait gave up
+        auto preload_tail = [&](int buf) -> bool {
+            const size_t hslot = sk_slot - RANKS;
+            int* hflag = p.sk_flags + hslot * C::EPI_WARPS + ew;
+            const float4* src = reinterpret_cast<const float4*>(p.ws) + hslot * (C::BM * BN / 4) +
+                                static_cast<size_t>(ew) * NS * 256 + lane;
+            const uint32_t t_dst = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                                   static_cast<uint32_t>(buf * BN + col_half * HALF);
+            bool got = true;
+            if (lane == 0) got = sk_wait(hflag, abort_flag, p.err, 303);
+            if (__shfl_sync(0xffffffffu, got ? 1 : 0, 0) == 0) return false;
+#pragma unroll 1
+            for (int c = 0; c < NS; ++c) {
+                float4 pv[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g) pv[g] = __ldcg(src + (c * 8 + g) * 32);
+                uint32_t r0[16], r1[16];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    r0[4 * g + 0] = __float_as_uint(pv[g].x);
+                    r0[4 * g + 1] = __float_as_uint(pv[g].y);
+                    r0[4 * g + 2] = __float_as_uint(pv[g].z);
+                    r0[4 * g + 3] = __float_as_uint(pv[g].w);
+                    r1[4 * g + 0] = __float_as_uint(pv[g + 4].x);
+                    r1[4 * g + 1] = __float_as_uint(pv[g + 4].y);
+                    r1[4 * g + 2] = __float_as_uint(pv[g + 4].z);
+                    r1[4 * g + 3] = __float_as_uint(pv[g + 4].w);
+                }
+                tmem_st_32x32b_x16(t_dst + 32 * c, r0);
+                tmem_st_32x32b_x16(t_dst + 32 * c + 16, r1);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                *reinterpret_cast<volatile int*>(hflag) = 0;  // read: zero again for the next call
+                if constexpr (PAIR)
+                    mbar_arrive_cluster(mapa_shared(smem_u32(loaded_bar), 0));
+                else
+                    mbar_arrive(loaded_bar);
+            }
+            return true;
+        };
+        bool tail_loaded = false;
+        Schedule sched = schedule();
+        WorkItem w;
+        while (sched.next(w)) {
+            const int tile = w.tile;
             const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::TILE_M + static_cast<int64_t>(rank) * C::BM;
             const int c_begin = (tile % num_n) * BN + col_half * HALF;
             const int64_t row0 = m0 + 32 * q;
             const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
             const int nsteps = (valid > 0 && row0 < p.m) ? (valid + CW - 1) / CW : 0;
+            // raw accumulator out instead of an epilogue: split-K, or the head of a cut stream-K tile
+            const bool partial = splits > 1 || w.mode == kItemHead;
             if constexpr (RES > 0) {
                 // first residual step of the tile lands while the main loop runs
-                if (lane == 0 && nsteps > 0 && splits == 1) {
+                if (lane == 0 && nsteps > 0 && !partial) {
                     bulk_wait_group_read<0>();
                     load_residual(RES == 2 ? (j & 1) : 0, c_begin, row0);
                 }
             }
-            if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
-            tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
                                    static_cast<uint32_t>(acc * BN + col_half * HALF);
+            // stream-K tail: the previous unit's head goes into the tail's TMEM buffer
+            // before the tail's MMAs start, while the item before it is still being
+            // computed (that buffer was freed by this warp's previous epilogue). When
+            // the item before the tail is this unit's own head, the load waits until
+            // that head is written and flagged, so no unit's head ever waits.
+            bool preload_after_head = false;
+            if (splits == 1) {
+                if (w.mode == kItemTail && !tail_loaded) {
+                    if (!preload_tail(acc)) break;
+                    tail_loaded = true;
+                }
+                WorkItem nx;
+                Schedule look = sched;
+                if (look.next(nx) && nx.mode == kItemTail) {
+                    if (w.mode == kItemHead) {
+                        preload_after_head = true;
+                    } else {
+                        if (!preload_tail(acc ^ 1)) break;
+                        tail_loaded = true;
+                    }
+                }
+            }
+            if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 301)) break;
+            tc_fence_after();
             bool ok = true;
-            if (splits > 1) {
-                // split-K partial: the raw accumulator, 32 columns per step; granule
-                // (ew, step, g) of lane l at float4 ((ew * NS + step) * 8 + g) * 32 + l
-                constexpr int NS = HALF / 32;
-                float4* dst = reinterpret_cast<float4*>(p.ws) + static_cast<size_t>(blockIdx.x) * (C::BM * BN / 4) +
+            if (partial) {
+                // the raw accumulator, 32 columns per step; granule (ew, step, g) of
+                // lane l at float4 ((ew * NS + step) * 8 + g) * 32 + l of the slot
+                const size_t slot = splits > 1 ? static_cast<size_t>(blockIdx.x) : sk_slot;
+                float4* dst = reinterpret_cast<float4*>(p.ws) + slot * (C::BM * BN / 4) +
                               static_cast<size_t>(ew) * NS * 256 + lane;
 #pragma unroll 1
                 for (int c = 0; c < NS; ++c) {
@@ -515,9 +739,19 @@ __global__ void __launch_bounds__(384, 1)
                         __stcg(dst + (c * 8 + g) * 32, make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
                                                                    __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
                 }
+                if (splits == 1) {
+                    // stream-K: every lane's stores are visible device-wide before the flag
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) sk_signal(p.sk_flags + sk_slot * C::EPI_WARPS + ew);
+                    if (preload_after_head) {
+                        ok = preload_tail(acc ^ 1);
+                        tail_loaded = true;
+                    }
+                }
             }
 #pragma unroll 1
-            for (int c = 0; c < (splits > 1 ? 0 : nsteps); ++c, ++j) {
+            for (int c = 0; c < (partial ? 0 : nsteps); ++c, ++j) {
                 const int col0 = c_begin + c * CW;
                 if constexpr (RES == 2) {
                     // next residual step into the other slot, once that slot's

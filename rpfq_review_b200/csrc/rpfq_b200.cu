@@ -247,19 +247,69 @@ int make_tmap_codes(CUtensorMap* m, const void* base, int64_t rows, int64_t byte
 }
 
 // ---------------------------------------------------------------- GEMM launch
+// Stream-K tail length for `tiles` tiles over `units` co-resident units: the
+// last wave plus one full wave (so every unit's share is at least one tile),
+// when the last wave is at most 85 % full; 0 = data-parallel only.
+int sk_tail(int64_t tiles, int units) {
+    if (units <= 0 || tiles <= units || tiles % units == 0) return 0;
+    const double fill = static_cast<double>(tiles % units) / units;
+    if (fill > 0.85) return 0;
+    return static_cast<int>(tiles - (tiles / units - 1) * units);
+}
+
+// Workspace: split-K / stream-K partials, then the stream-K flag words.
+uint64_t ws_partial_bytes(const DeviceState* st) { return static_cast<uint64_t>(st->sm_count) * 128u * 256u * 4u; }
+constexpr uint64_t kSkFlagBytes = 8192;  // >= SMs x 8 epilogue warps x 4 B
+
+// Units of the persistent grid that are resident at once: CTA pairs (queried
+// once per device and kernel variant) or CTAs (one per SM). 0 on error.
 template <int BN, bool OUT_F32, int RES, bool PAIR>
-int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits) {
+int gemm_units(DeviceState* st) {
+    using C = GemmCfg<BN, RES, PAIR>;
+    if constexpr (!PAIR) {
+        return st->sm_count;
+    } else {
+        static int max_pairs[kMaxDevices] = {};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+        if (max_pairs[dev] == 0) {
+            cudaLaunchConfig_t q = {};
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = 2;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.gridDim = dim3(st->sm_count);
+            q.blockDim = dim3(C::THREADS);
+            q.dynamicSmemBytes = C::SMEM_BYTES;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, &q) != cudaSuccess) {
+                cudaGetLastError();
+                return 0;
+            }
+            max_pairs[dev] = n > 0 ? n : 1;
+        }
+        return max_pairs[dev];
+    }
+}
+
+// Stream-K tail of a launch: only when every unit of the grid can be resident
+// together (owners wait for their peers).
+template <int BN, bool OUT_F32, int RES, bool PAIR>
+int gemm_sk_tiles(int64_t tiles, DeviceState* st) {
+    const int units = gemm_units<BN, OUT_F32, RES, PAIR>(st);
+    if (units <= 0 || (PAIR ? 2 * units : units) > st->sm_count) return 0;
+    return sk_tail(tiles, units);
+}
+
+template <int BN, bool OUT_F32, int RES, bool PAIR>
+int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits, bool stream_k,
+                RpfqGemmPlan* dry) {
     using C = GemmCfg<BN, RES, PAIR>;
     constexpr int CW = OUT_F32 ? 32 : 64;   // output / residual columns per 128-B step
     constexpr int ESZ = OUT_F32 ? 4 : 2;
-    CUtensorMap tx, tw, ty, tr;
-    int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
-    if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, C::B_ROWS, C::BK);
-    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, CW, ESZ);
-    // residual: same [32 rows x 128 B] boxes as the output (TMA loads + L2 prefetches)
-    if (!rc && RES > 0) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
-    if (rc) return rc;
-    if (RES == 0) tr = ty;
     GemmParams p;
     p.bias = a->bias;
     p.bias_f32 = (a->flags & RPFQ_GEMM_BIAS_F32) ? 1 : 0;
@@ -274,40 +324,47 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int
     p.y = a->y;
     p.ldy = a->ldy;
     p.err = st->err_word;
+    p.sk_tiles = 0;
+    p.sk_flags = stream_k ? reinterpret_cast<int*>(static_cast<uint8_t*>(a->workspace) + ws_partial_bytes(st))
+                          : nullptr;
     const int64_t tiles = ((a->m + C::TILE_M - 1) / C::TILE_M) * ((a->n + BN - 1) / BN);
+    if (stream_k) p.sk_tiles = gemm_sk_tiles<BN, OUT_F32, RES, PAIR>(tiles, st);
+    // grid: persistent units (CTA pairs or CTAs, as many as are resident at once; with a
+    // stream-K tail exactly that many), or tiles x splits CTAs for split-K
+    int units;
     if constexpr (PAIR) {
-        // as many CTA pairs as can be resident at once (queried once per device)
-        static int max_pairs[kMaxDevices] = {};
-        int dev = 0;
-        RPFQ_CUDA(cudaGetDevice(&dev));
-        cudaLaunchConfig_t cfg = {};
-        if (max_pairs[dev] == 0) {
-            cudaLaunchConfig_t q = {};
-            cudaLaunchAttribute qa[1];
-            qa[0].id = cudaLaunchAttributeClusterDimension;
-            qa[0].val.clusterDim.x = 2;
-            qa[0].val.clusterDim.y = 1;
-            qa[0].val.clusterDim.z = 1;
-            q.gridDim = dim3(st->sm_count);
-            q.blockDim = dim3(C::THREADS);
-            q.dynamicSmemBytes = C::SMEM_BYTES;
-            q.attrs = qa;
-            q.numAttrs = 1;
-            int n = 0;
-            RPFQ_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, &q));
-            max_pairs[dev] = n > 0 ? n : 1;
-        }
-        const int pairs = static_cast<int>(tiles < max_pairs[dev] ? tiles : max_pairs[dev]);
-        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, dim3(2 * pairs), dim3(C::THREADS),
-                                C::SMEM_BYTES, stream, 2, tx, tw, ty, tr, p));
+        const int max_pairs = gemm_units<BN, OUT_F32, RES, true>(st);
+        if (max_pairs <= 0) return fail(RPFQ_ERR_CUDA, "rpfq_gemm_sm100: occupancy query for CTA pairs failed");
+        units = p.sk_tiles ? max_pairs : static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
     } else if (p.splits > 1) {
-        // split-K: one CTA per (tile, split), the splits of a tile in one cluster
-        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(static_cast<int>(tiles) * p.splits),
-                                dim3(C::THREADS), C::SMEM_BYTES, stream, p.splits, tx, tw, ty, tr, p));
+        units = static_cast<int>(tiles);
     } else {
-        const int grid = static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
-        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(grid), dim3(C::THREADS),
-                                C::SMEM_BYTES, stream, 1, tx, tw, ty, tr, p));
+        units = p.sk_tiles ? st->sm_count : static_cast<int>(tiles < st->sm_count ? tiles : st->sm_count);
+    }
+    if (dry) {
+        dry->block_n = BN;
+        dry->cta_pair = PAIR ? 2 : 1;
+        dry->split_k = p.splits;
+        dry->stream_k_tiles = p.sk_tiles;
+        dry->units = units;
+        dry->tiles = static_cast<int32_t>(tiles);
+        return RPFQ_OK;
+    }
+    CUtensorMap tx, tw, ty, tr;
+    int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
+    if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, C::B_ROWS, C::BK);
+    if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, CW, ESZ);
+    // residual: same [32 rows x 128 B] boxes as the output (TMA loads + L2 prefetches)
+    if (!rc && RES > 0) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
+    if (rc) return rc;
+    if (RES == 0) tr = ty;
+    if constexpr (PAIR) {
+        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, dim3(2 * units), dim3(C::THREADS),
+                                C::SMEM_BYTES, stream, 2, tx, tw, ty, tr, p));
+    } else {
+        // split-K: one CTA per (tile, split), the splits of a tile in one cluster
+        RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(units * p.splits),
+                                dim3(C::THREADS), C::SMEM_BYTES, stream, p.splits, tx, tw, ty, tr, p));
     }
     return RPFQ_OK;
 }
@@ -355,17 +412,18 @@ uint64_t splitk_bytes(int64_t m, int n, int bn, int s) {
 // and the epilogue must hide the residual latency itself; one otherwise.
 // Split-K reads the residual in its reduction: no staging slots.
 template <int BN, bool PAIR>
-int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits) {
+int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits, bool sk,
+                   RpfqGemmPlan* dry) {
     const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
     const int res = (a->residual == nullptr || splits > 1) ? 0 : (a->k <= 1024 ? 2 : 1);
     if (f32) {
-        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream, splits);
-        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream, splits);
-        return launch_gemm<BN, true, 0, PAIR>(a, st, stream, splits);
+        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream, splits, sk, dry);
+        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream, splits, sk, dry);
+        return launch_gemm<BN, true, 0, PAIR>(a, st, stream, splits, sk, dry);
     }
-    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream, splits);
-    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream, splits);
-    return launch_gemm<BN, false, 0, PAIR>(a, st, stream, splits);
+    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream, splits, sk, dry);
+    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream, splits, sk, dry);
+    return launch_gemm<BN, false, 0, PAIR>(a, st, stream, splits, sk, dry);
 }
 
 // ---------------------------------------------------------------- K3 fused decode launch
@@ -483,10 +541,22 @@ int pick_block_n(int64_t m, int n, int sm_count) {
 }
 
 struct GemmPlan {
-    int bn;      // tile width
-    bool pair;   // CTA pairs (256 x 256 tiles)
-    int splits;  // K splits per tile (one CTA per tile)
+    int bn;          // tile width
+    bool pair;       // CTA pairs (256 x 256 tiles)
+    int splits;      // K splits per tile (one CTA per tile)
+    bool stream_k;   // a stream-K tail when the tiles do not fill whole waves
 };
+
+constexpr double kSkMinIdleKBlocks = 24.0;  // see plan_gemm
+
+// Stream-K on by default; RPFQ_STREAM_K=0 turns it off (data-parallel waves only).
+bool stream_k_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("RPFQ_STREAM_K");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 // Time (us) of a one-CTA-per-tile plan when few tiles leave SMs idle, fitted
 // to CUDA-event timings on B200 (M = 198..1584, K = 384..4096): a fixed
@@ -514,10 +584,35 @@ double small_m_cost(int64_t m, int n, int k, int bn, int s, DeviceState* st) {
 // split_k = 1) the tile width comes from the wave-quantisation model of
 // pick_block_n; with one, shapes whose 128-wide tiles do not fill the SMs are
 // planned by small_m_cost over tile widths and split counts.
-GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split_k, bool have_ws, DeviceState* st) {
+GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split_k, bool have_ws, DeviceState* st,
+                   bool sk_ws = false) {
     GemmPlan g;
-    g.bn = block_n ? block_n : pick_block_n(m, n, st->sm_count);
+    g.stream_k = false;
     const int64_t pair_tiles = ((m + 255) / 256) * ((n + 255) / 256);
+    // A stream-K tail turns the last, partly idle wave of 256 x 256 pair tiles into
+    // an even share per pair, at the price of moving each cut tile's fp32
+    // accumulator (128 KiB per CTA) through L2 before its second part can start:
+    // about 10 us on B200 (CUDA events, m = 6304). A pair k-block takes about
+    // 0.5 us, so the tail is taken only when the idle part of the last wave is at
+    // least 24 k-blocks long (ViT-B fc2 at 32 images: 0.99 x 48; qkv, fc1 and proj
+    // with K = 768 lose).
+    if (sk_ws && stream_k_enabled() && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
+        pair_tiles >= st->sm_count / 2) {
+        const int units = gemm_units<256, false, 0, true>(st);
+        const int num_k = (k + 63) / 64;
+        if (units > 0 && sk_tail(pair_tiles, units) > 0) {
+            const int64_t waves = (pair_tiles + units - 1) / units;
+            const double idle = static_cast<double>(waves) - static_cast<double>(pair_tiles) / units;
+            if (idle * num_k >= kSkMinIdleKBlocks) {
+                g.bn = 256;
+                g.pair = true;
+                g.splits = 1;
+                g.stream_k = true;
+                return g;
+            }
+        }
+    }
+    g.bn = block_n ? block_n : pick_block_n(m, n, st->sm_count);
     g.pair = g.bn == 256 && (cta_pair == 2 || (cta_pair == 0 && split_k <= 1 && pair_tiles >= st->sm_count / 2));
     g.splits = 1;
     if (g.pair || !have_ws || split_k == 1) return g;
@@ -542,7 +637,7 @@ GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split
     return g;
 }
 
-int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
+int gemm(const RpfqGemmArgs* a, cudaStream_t stream, RpfqGemmPlan* dry = nullptr) {
     if (!a) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: null args");
     if (!a->x || !a->w || !a->y) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: x, w and y are required");
     if (a->m < 0 || a->n <= 0 || a->k <= 0) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: bad shape m=%lld n=%d k=%d", (long long)a->m, a->n, a->k);
@@ -570,7 +665,7 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
     if (a->split_k > 1 && !a->workspace)
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: split_k %d needs a workspace", a->split_k);
     if (a->m > (int64_t(1) << 31) - 256) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_gemm_sm100: m too large");
-    if (a->m == 0) return RPFQ_OK;
+    if (a->m == 0 && !dry) return RPFQ_OK;
     DeviceState* st;
     int rc = device_state(&st);
     if (rc) return rc;
@@ -580,7 +675,8 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: block_n must be 0, 128 or 256 (got %d)", a->block_n);
     // CTA pairs (256 x 256 tiles over two SMs) when the 256-wide tile is chosen
     // and there are enough row pairs to fill the GPU; cta_pair forces either way.
-    GemmPlan g = plan_gemm(a->m, a->n, a->k, a->block_n, a->cta_pair, a->split_k, a->workspace != nullptr, st);
+    const bool sk_ws = a->workspace != nullptr && a->workspace_bytes >= ws_partial_bytes(st) + kSkFlagBytes;
+    GemmPlan g = plan_gemm(a->m, a->n, a->k, a->block_n, a->cta_pair, a->split_k, a->workspace != nullptr, st, sk_ws);
     if (a->split_k == 0 && g.splits > 1 && splitk_bytes(a->m, a->n, g.bn, g.splits) > a->workspace_bytes)
         g = plan_gemm(a->m, a->n, a->k, a->block_n, a->cta_pair, 1, false, st);  // too small a workspace: no split
     const int splits = g.splits;
@@ -588,8 +684,9 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream) {
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: %d K splits need a workspace of %llu bytes (got %llu)", splits,
                     (unsigned long long)splitk_bytes(a->m, a->n, g.bn, splits), (unsigned long long)a->workspace_bytes);
     if (g.bn == 256)
-        return g.pair ? launch_gemm_bn<256, true>(a, st, stream, 1) : launch_gemm_bn<256, false>(a, st, stream, splits);
-    return launch_gemm_bn<128, false>(a, st, stream, splits);
+        return g.pair ? launch_gemm_bn<256, true>(a, st, stream, 1, g.stream_k, dry)
+                      : launch_gemm_bn<256, false>(a, st, stream, splits, false, dry);
+    return launch_gemm_bn<128, false>(a, st, stream, splits, false, dry);
 }
 
 // ---------------------------------------------------------------- packed-layer validation
@@ -690,12 +787,26 @@ int rpfq_gemm_sm100(const RpfqGemmArgs* args, rpfq_stream_t stream) {
     return gemm(args, static_cast<cudaStream_t>(stream));
 }
 
+int rpfq_gemm_plan_sm100(const RpfqGemmArgs* args, RpfqGemmPlan* plan) {
+    if (!plan) return fail(RPFQ_ERR_INVALID, "rpfq_gemm_plan_sm100: null plan");
+    std::memset(plan, 0, sizeof(*plan));
+    return gemm(args, nullptr, plan);
+}
+
 uint64_t rpfq_gemm_workspace_bytes(int64_t m, int32_t n, int32_t k) {
     DeviceState* st;
     if (device_state(&st)) return 0;
-    if (m == 0) return static_cast<uint64_t>(st->sm_count) * 128u * 256u * 4u;  // tiles x splits <= SMs
+    // split-K partials (tiles x splits <= SMs) or stream-K partials (units x ranks
+    // <= SMs), then the stream-K flags
+    if (m == 0) return ws_partial_bytes(st) + kSkFlagBytes;
     if (m < 0 || n <= 0 || k <= 0) return 0;
-    const GemmPlan g = plan_gemm(m, n, k, 0, 0, 0, true, st);
+    const GemmPlan g = plan_gemm(m, n, k, 0, 0, 0, true, st, true);
+    if (g.stream_k) {
+        // the tail exists only when the pair tiles do not fill whole waves (every
+        // pair-kernel variant has the same resident pair count)
+        const int64_t tiles = ((m + 255) / 256) * ((n + 255) / 256);
+        return gemm_sk_tiles<256, false, 0, true>(tiles, st) ? ws_partial_bytes(st) + kSkFlagBytes : 0;
+    }
     return g.splits > 1 ? splitk_bytes(m, n, g.bn, g.splits) : 0;
 }
 

@@ -87,7 +87,9 @@ def _workspace(device: torch.device, split_k: int) -> tuple[int | None, int]:
     if ws is None:
         with torch.cuda.device(device):
             nbytes = int(_lib.lib().rpfq_gemm_workspace_bytes(0, 0, 0))
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        # zeroed: the stream-K flag words at its end start at zero (the library
+        # leaves them zero after every call)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws.data_ptr(), ws.numel()
 
@@ -353,6 +355,28 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     return out
 
 
+def gemm_plan(m: int, n: int, k: int, *, out_dtype: torch.dtype = torch.float16, residual: bool = False,
+              block_n: int = 0, cta_pair: int = 0, split_k: int | None = None,
+              device: torch.device | None = None) -> dict:
+    """The tile plan :func:`gemm` runs for an ``[m, k] x [n, k]`` product on
+    ``device`` with the same choices (``rpfq_gemm_plan_sm100``; nothing is
+    launched): tile width, CTA pairs, K splits, stream-K tail, grid units."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    split_k = SPLIT_K if split_k is None else int(split_k)
+    ws, ws_bytes = _workspace(device, split_k)
+    f = (_lib.GEMM_OUT_F32 if out_dtype == torch.float32 else 0)
+    if residual:
+        f |= _lib.GEMM_RESIDUAL_F32 if out_dtype == torch.float32 else 0
+    # placeholders: only alignment and strides are validated, nothing is read
+    a = _lib.RpfqGemmArgs(x=256, ldx=k, w=256, bias=None, residual=256 if residual else None, ldr=n if residual else 0,
+                          y=256, ldy=n, m=m, n=n, k=k, activation=0, block_n=block_n, flags=f, cta_pair=cta_pair,
+                          split_k=split_k, workspace=ws, workspace_bytes=ws_bytes)
+    plan = _lib.RpfqGemmPlan()
+    with torch.cuda.device(device):
+        _lib.check(_lib.lib().rpfq_gemm_plan_sm100(ctypes.byref(a), ctypes.byref(plan)), "rpfq_gemm_plan_sm100")
+    return {f: getattr(plan, f) for f, _ in _lib.RpfqGemmPlan._fields_}
+
+
 def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, act_bits: int = 0,
               out: torch.Tensor | None = None, rows: torch.Tensor | None = None) -> torch.Tensor:
     """LayerNorm of an fp32 ``x[..., d]`` into fp16, with the activation
@@ -545,7 +569,12 @@ _LIB.define("gemm(Tensor x, Tensor w, Tensor? bias=None, Tensor? residual=None, 
 _LIB.define("act_quant(Tensor x, int num_bits) -> Tensor")
 _LIB.define("prepack(Tensor[] codes, Tensor[] gamma_real, Tensor[] gamma_imag, int n_c, int k_c, "
             "int code_bits=2, int rounding=0) -> Tensor")
-_LIB.define("wide_linear(Tensor x, Tensor dense, Tensor? bias, int n_c, int k_c, int act_bits=0, "
+# The packed layer as the reference stores it: codes / gammas of the U stages
+# then the W stages (export_rpfq_vit_to_mlx.py:384-423 key order), exactly the
+# tensors a caller of QATLinearComplexPhase's packed form holds.
+_LIB.define("wide_linear(Tensor x, Tensor[] codes, Tensor[] gamma_re, Tensor[] gamma_im, Tensor? bias, int n_c, "
+            "int k_c, int act_bits=0, bool gelu=False) -> Tensor")
+_LIB.define("wide_linear_dense(Tensor x, Tensor dense, Tensor? bias, int n_c, int k_c, int act_bits=0, "
             "int activation=0, Tensor? residual=None) -> Tensor")
 
 
@@ -557,15 +586,15 @@ def _op_act_quant(x, num_bits):
     return act_quant(x, int(num_bits))
 
 
-def _planes_from_lists(codes, gamma_real, gamma_imag, n_c, k_c, code_bits):
-    if len(codes) % 2 or not (len(codes) == len(gamma_real) == len(gamma_imag)):
+def _planes_from_lists(codes, gamma_real, gamma_imag, n_c, k_c, code_bits, bias=None):
+    if len(codes) % 2 or not (len(codes) == len(gamma_real) == len(gamma_imag)) or not codes:
         raise ValueError("codes / gammas must list the U stages then the W stages")
     stages = len(codes) // 2
     planes = {}
     for i in range(stages):
         planes[f"u_s{i}"] = (codes[i], gamma_real[i], gamma_imag[i])
         planes[f"w_s{i}"] = (codes[stages + i], gamma_real[stages + i], gamma_imag[stages + i])
-    return PackedLayer(int(n_c), int(k_c), stages, int(code_bits), planes, None)
+    return PackedLayer(int(n_c), int(k_c), stages, int(code_bits), planes, bias)
 
 
 def _op_prepack(codes, gamma_real, gamma_imag, n_c, k_c, code_bits=2, rounding=0):
@@ -573,7 +602,68 @@ def _op_prepack(codes, gamma_real, gamma_imag, n_c, k_c, code_bits=2, rounding=0
     return prepack(layer, "rne" if int(rounding) == 0 else "ties_away")
 
 
-def _op_wide_linear(x, dense, bias, n_c, k_c, act_bits=0, activation=0, residual=None):
+# Decoded coefficient matrices of packed layers called through the packed op
+# with more rows than the fused decode path takes: keyed by the planes'
+# storage and version counters (a plane written in place decodes again). An
+# entry holds its plane tensors, so their storage cannot be handed to another
+# layer while the entry exists; the oldest entry goes first past the limit.
+_DENSE_CACHE: dict = {}
+_DENSE_CACHE_MAX = 256
+dense_cache_stats = {"hits": 0, "decodes": 0}
+
+
+def _cached_dense(layer: PackedLayer, tensors) -> torch.Tensor:
+    key = (layer.n_c, layer.k_c, layer.stages, layer.code_bits,
+           tuple((t.data_ptr(), t._version, tuple(t.shape), t.dtype) for t in tensors))
+    entry = _DENSE_CACHE.get(key)
+    if entry is not None:
+        dense_cache_stats["hits"] += 1
+        return entry[1]
+    while len(_DENSE_CACHE) >= _DENSE_CACHE_MAX:
+        _DENSE_CACHE.pop(next(iter(_DENSE_CACHE)))
+    dense = prepack(layer)
+    dense_cache_stats["decodes"] += 1
+    _DENSE_CACHE[key] = (list(tensors), dense)
+    return dense
+
+
+def _op_wide_linear(x, codes, gamma_re, gamma_im, bias, n_c, k_c, act_bits=0, gelu=False):
+    """The packed layer ``y = act(Q(W) x + b)`` straight from the reference's
+    packed tensors: codes uint8 ``[n_cp, k_cp * b / 8]`` and fp16 gammas
+    ``[n_cp, k_cp / 256]`` per stage (U stages, then W stages; the code width
+    b follows from the codes' shape), optional fp16 bias ``[2 n_c]``, fp16
+    ``x[..., 2 k_c]`` -> fp16 ``[..., 2 n_c]``. ``act_bits`` > 0 quantizes x
+    first (ActivationQuantSTE); ``gelu`` applies exact GELU to the output.
+
+    Up to ``FUSED_DECODE_MAX_ROWS`` rows (2-bit codes, ``n_c``, ``k_c``
+    multiples of 8) the codes are decoded inside the GEMM and no dense matrix
+    exists; otherwise the planes are decoded once into the fp16 coefficient
+    matrix (kept for later calls with the same planes) and the tcgen05 GEMM
+    runs over it."""
+    _require(x, "x")
+    from .packing import BLOCK_SIZE, round_up
+    n_c, k_c = int(n_c), int(k_c)
+    if n_c <= 0 or k_c <= 0:
+        raise ValueError(f"n_c and k_c must be positive, got {n_c}, {k_c}")
+    k_cp = round_up(k_c, BLOCK_SIZE)
+    if not codes or codes[0].dim() != 2 or (codes[0].shape[1] * 8) % k_cp:
+        raise ValueError("codes must be [n_cp, k_cp * code_bits / 8] uint8 tensors")
+    code_bits = codes[0].shape[1] * 8 // k_cp
+    if bias is not None:
+        _require(bias, "bias")
+        if bias.numel() != 2 * n_c:
+            raise ValueError(f"bias must hold {2 * n_c} values, got {bias.numel()}")
+    layer = _planes_from_lists(codes, gamma_re, gamma_im, n_c, k_c, code_bits,
+                               bias if bias is not None else torch.zeros(2 * n_c, dtype=torch.float16,
+                                                                          device=x.device))
+    m = x.numel() // x.shape[-1] if x.dim() else 0
+    act = "gelu" if gelu else "none"
+    fused = m <= FUSED_DECODE_MAX_ROWS and code_bits == 2 and n_c % 8 == 0 and k_c % 8 == 0
+    dense = None if fused else _cached_dense(layer, [*codes, *gamma_re, *gamma_im])
+    return wide_linear(x, layer, dense, int(act_bits), activation=act)
+
+
+def _op_wide_linear_dense(x, dense, bias, n_c, k_c, act_bits=0, activation=0, residual=None):
     _require(x, "x")
     if tuple(dense.shape) != (2 * int(n_c), 2 * int(k_c)):
         raise ValueError(f"dense must be [{2 * int(n_c)}, {2 * int(k_c)}], got {tuple(dense.shape)}")
@@ -586,3 +676,4 @@ _LIB.impl("gemm", _op_gemm, "CUDA")
 _LIB.impl("act_quant", _op_act_quant, "CUDA")
 _LIB.impl("prepack", _op_prepack, "CUDA")
 _LIB.impl("wide_linear", _op_wide_linear, "CUDA")
+_LIB.impl("wide_linear_dense", _op_wide_linear_dense, "CUDA")

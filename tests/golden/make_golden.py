@@ -25,8 +25,17 @@ run time. Fixtures:
   module imports timm at its top, which this container lacks, so the class
   definition (and ``EPS``) is taken out of the file with ``ast`` and executed
   alone, unchanged.
+* ``golden_vitref.npz`` — the reference's pure-torch runtime forward,
+  ``forward_runtime_path`` with ``capture_runtime_block_trace``
+  (RPFQ-ViTApple/scripts/audit_rpfq_vit_ios_parity.py:588-688), on a small
+  3-block ViT (so that block 0, block 1 and the later-block branch all run)
+  whose quantized linears are rebuilt by the script's own
+  ``reconstruct_export_weight`` (:328-383) and ``quantized_forward_weight``
+  (head), as its ``build_runtime_state`` (:439-515) does. The script imports
+  timm and PIL at its top, so these functions are taken out of it with
+  ``ast`` and executed unchanged next to the exporter module they import.
 
-``--only NAME`` regenerates one fixture (exporter, actquant, qat, refcpp, vision).
+``--only NAME`` regenerates one fixture (exporter, actquant, qat, refcpp, vision, vitref).
 """
 
 from __future__ import annotations
@@ -46,10 +55,13 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RPFQ_REFERENCE_ROOT", "/root/reference"))
-    ap.add_argument("--only", default=None, choices=["exporter", "actquant", "qat", "refcpp", "vision"])
+    ap.add_argument("--only", default=None, choices=["exporter", "actquant", "qat", "refcpp", "vision", "vitref"])
     args = ap.parse_args()
     if args.only == "vision":
         make_vision(args.ref)
+        return
+    if args.only == "vitref":
+        make_vitref(args.ref)
         return
     sys.path.insert(0, os.path.join(args.ref, "RPFQ-ViTApple", "scripts"))
     sys.path.insert(0, os.path.join(args.ref, "RPFQ-ViT-main", "quant_models"))
@@ -137,6 +149,7 @@ def main() -> None:
         rc[f"plane.{key}"] = val
     np.savez_compressed(os.path.join(HERE, "golden_refcpp.npz"), **rc)
     make_vision(args.ref)
+    make_vitref(args.ref)
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 
@@ -193,6 +206,80 @@ def make_vision(ref: str) -> None:
         out[f"{name}.mask"] = (np.ones(xr.shape[:-1], bool) if mask is None
                                else mask.squeeze(-1).numpy()).astype(np.uint8)
     np.savez_compressed(os.path.join(HERE, "golden_vision.npz"), **out)
+
+
+
+# Small ViT of the vitref fixture: hidden 64 (32 complex, padded to 256), 2
+# heads, 3 blocks, MLP 128, 16 x 16 images of 8 x 8 patches (5 tokens), 10
+# classes, LayerNorm eps 1e-6 (timm ViT).
+VITREF = dict(hidden=64, heads=2, depth=3, mlp=128, img=16, patch=8, classes=10, eps=1e-6, batch=2)
+
+
+def _reference_runtime_functions(ref: str):
+    """forward_runtime_path and the helpers it calls, executed from the
+    reference audit script's own source without its module-level imports
+    (timm, PIL), next to the exporter functions that script imports."""
+    import ast
+    from dataclasses import dataclass
+    from typing import Any
+    sys.path.insert(0, os.path.join(ref, "RPFQ-ViTApple", "scripts"))
+    import export_rpfq_vit_to_mlx as ex  # noqa: E402
+    path = os.path.join(ref, "RPFQ-ViTApple", "scripts", "audit_rpfq_vit_ios_parity.py")
+    tree = ast.parse(open(path).read(), path)
+    names = {"RuntimeLayer", "patchify_tensor", "reconstruct_export_weight", "layer_norm", "linear",
+             "capture_runtime_block_trace", "forward_runtime_path"}
+    keep = [n for n in tree.body if isinstance(n, (ast.ClassDef, ast.FunctionDef)) and n.name in names]
+    assert {n.name for n in keep} == names
+    ns = {"torch": torch, "F": F, "dataclass": dataclass, "Any": Any, "__name__": "audit_extract"}
+    for k in ("widely_linear_decompose", "residual_phase_quantize", "legacy_residual_phase_quantize",
+              "dequantize_axis"):
+        ns[k] = getattr(ex, k)
+    exec(compile(ast.Module(body=keep, type_ignores=[]), path, "exec"), ns)
+    return ns, ex
+
+
+def make_vitref(ref: str) -> None:
+    ns, ex = _reference_runtime_functions(ref)
+    RL = ns["RuntimeLayer"]
+    c = VITREF
+    d, mlp = c["hidden"], c["mlp"]
+    g = torch.Generator().manual_seed(4242)
+
+    def rnd(*shape, std=0.05):
+        return torch.randn(*shape, generator=g) * std
+
+    state = {"patch_w": rnd(d, 3 * c["patch"] ** 2, std=0.02), "patch_b": rnd(d, std=0.02),
+             "cls_token": rnd(1, 1, d, std=0.02), "pos_embed": rnd(1, 1 + (c["img"] // c["patch"]) ** 2, d, std=0.02),
+             "norm_w": 1 + rnd(d, std=0.1), "norm_b": rnd(d, std=0.1),
+             "head_w": rnd(c["classes"], d), "head_b": rnd(c["classes"], std=0.02)}
+    pad = lambda n: -(-n // ex.BLOCK_SIZE) * ex.BLOCK_SIZE  # noqa: E731
+    layers = []
+    for i in range(c["depth"]):
+        for name, (n_out, n_in) in (("qkv", (3 * d, d)), ("proj", (d, d)), ("fc1", (mlp, d)), ("fc2", (d, mlp))):
+            state[f"blocks.{i}.{name}.w"] = rnd(n_out, n_in)
+            state[f"blocks.{i}.{name}.b"] = rnd(n_out, std=0.02)
+        for nm in ("norm1", "norm2"):
+            state[f"blocks.{i}.{nm}.w"] = 1 + rnd(d, std=0.1)
+            state[f"blocks.{i}.{nm}.b"] = rnd(d, std=0.1)
+        lay = {nm: RL(state[f"blocks.{i}.{nm}.w"], state[f"blocks.{i}.{nm}.b"]) for nm in ("norm1", "norm2")}
+        for name in ("qkv", "proj", "fc1", "fc2"):
+            w = state[f"blocks.{i}.{name}.w"]
+            wq = ns["reconstruct_export_weight"](w, pad(w.shape[1] // 2), pad(w.shape[0] // 2), 2, legacy=False)
+            lay[name] = RL(wq, state[f"blocks.{i}.{name}.b"])
+        layers.append(lay)
+    runtime = {"patch_embed": RL(state["patch_w"], state["patch_b"]), "cls_token": state["cls_token"],
+               "pos_embed": state["pos_embed"], "norm": RL(state["norm_w"], state["norm_b"]),
+               "head": RL(ex.quantized_forward_weight(state["head_w"], stages=2).float(), state["head_b"]),
+               "layers": layers}
+    images = torch.randn(c["batch"], 3, c["img"], c["img"], generator=g)
+    patches = torch.cat([ns["patchify_tensor"](im, c["patch"]) for im in images], dim=0)
+    caps = ns["forward_runtime_path"](runtime, patches, c["heads"], c["eps"])
+    out = {f"state.{k}": v.numpy() for k, v in state.items()}
+    out["images"] = images.numpy()
+    for k in ("patch_embed", "block0", "block1", "final_norm", "logits"):
+        out[f"ref.{k}"] = caps[k].numpy()
+    out["config"] = np.array([c[k] for k in ("hidden", "heads", "depth", "mlp", "img", "patch", "classes")], np.int64)
+    np.savez_compressed(os.path.join(HERE, "golden_vitref.npz"), **out)
 
 
 if __name__ == "__main__":

@@ -34,6 +34,17 @@ def from_numpy_packed(d: dict, n_c: int, k_c: int, device, code_bits: int = 2):
 
 
 def rel_err(y, ref) -> float:
+    """The parity tests' normalised measure: max|y - ref| / max|ref|."""
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def elem_rel_err(y, ref, floor: float = 1e-3) -> float:
+    """Element-wise relative error: max over elements of
+    |y - ref| / max(|ref|, floor * max|ref|). The floor keeps elements that
+    cancel to near zero from dividing by their own rounding noise."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = np.maximum(np.abs(ref), floor * max(np.abs(ref).max(), 1e-30))
+    return float((np.abs(y - ref) / den).max())

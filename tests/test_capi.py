@@ -96,11 +96,19 @@ def test_act_quant_validation():
 def test_torch_ops_registered():
     import torch
     import rpfq_review_b200.ops  # noqa: F401
-    for name in ("gemm", "act_quant", "prepack", "wide_linear"):
+    for name in ("gemm", "act_quant", "prepack", "wide_linear", "wide_linear_dense"):
         assert hasattr(torch.ops.rpfq, name)
     # CUDA-only: a CPU call fails in the dispatcher instead of falling back
     with pytest.raises(Exception):
         torch.ops.rpfq.act_quant(torch.zeros(2, 8, dtype=torch.float16), 4)
+    # the packed-layer op takes the reference's packed tensors (SURVEY contract schema)
+    schema = str(torch.ops.rpfq.wide_linear.default._schema)
+    assert ("wide_linear(Tensor x, Tensor[] codes, Tensor[] gamma_re, Tensor[] gamma_im, Tensor? bias, int n_c, "
+            "int k_c, int act_bits=0, bool gelu=False) -> Tensor") in schema
+    with pytest.raises(Exception):
+        torch.ops.rpfq.wide_linear(torch.zeros(2, 8, dtype=torch.float16), [torch.zeros(256, 64, dtype=torch.uint8)] * 2,
+                                   [torch.zeros(256, 1, dtype=torch.float16)] * 2,
+                                   [torch.zeros(256, 1, dtype=torch.float16)] * 2, None, 4, 4)
 
 
 def test_pack_linear_validation():
