@@ -13,7 +13,13 @@
 // prepacked one without ever writing the dense matrix to HBM.
 //
 // Work item = one block of RB complex output rows over all of K; persistent
-// CTAs loop over items. M <= 256 (two 128-row sub-tiles). 10 warps:
+// CTAs loop over items. M <= 256 (two 128-row sub-tiles).
+// Split-K (p.splits = S > 1, for layers whose row blocks alone leave most SMs
+// idle): a cluster of S CTAs per item, CTA s takes k-blocks
+// [s num_k / S, (s + 1) num_k / S) and writes its raw fp32 accumulator to the
+// workspace; after a cluster barrier each CTA reduces 1/S of the item's
+// outputs over the S partials in the fixed order 0..S-1 (deterministic) and
+// applies bias / GELU / residual. 10 warps:
 //   warp 0    TMA producer (x_re, x_im per sub-tile + the code planes per stage)
 //   warp 1    TMEM owner + MMA issuer
 //   warps 2-9 decode in two groups that take alternate stages (one 16-byte
@@ -41,6 +47,8 @@ struct DecodeGemmParams {
     int64_t m;
     int32_t activation;
     int32_t out_f32;
+    int32_t splits;         // K splits per item (cluster size), 1 = none
+    float* ws;              // split-K partials [items * splits][nsub * 128][2 RB] fp32
     int* err;
 };
 
@@ -68,6 +76,78 @@ struct DecodeCfg {
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
+// Split-K reduction of item `item` by split `split` of S: float4 granules
+// [split E / S, (split + 1) E / S) of the item's m x 2 RB outputs (E = m RB / 2)
+// are summed over the S partials in the order 0..S-1, then bias, GELU and
+// residual are applied and the four outputs of each granule stored (256
+// threads, tid 0..255). Accumulator column j < RB is output column r0 + j
+// (y_re), j >= RB is n_c + r0 + j - RB (y_im).
+template <int RB>
+__device__ __forceinline__ void decode_splitk_reduce(const DecodeGemmParams& p, int item, int split, int nsub, int tid) {
+    constexpr int G = 2 * RB / 4;  // granules per row
+    const int S = p.splits;
+    const int64_t E = p.m * G;
+    const int r0 = item * RB;
+    const int valid = min(RB, p.n_c - r0);
+    const float4* base = reinterpret_cast<const float4*>(p.ws) + static_cast<size_t>(item) * S * nsub * 128 * G;
+    const size_t part_stride = static_cast<size_t>(nsub) * 128 * G;  // float4 per partial
+    for (int64_t e = split * E / S + tid; e < (split + 1) * E / S; e += 256) {
+        const int64_t row = e / G;
+        const int jg = static_cast<int>(e - row * G);
+        const int j = 4 * jg;                       // accumulator column
+        const int half = j >= RB ? 1 : 0;
+        const int jc = j - half * RB;               // column within the half
+        if (jc >= valid) continue;
+        const int64_t col = static_cast<int64_t>(half) * p.n_c + r0 + jc;
+        float4 a = __ldcg(base + static_cast<size_t>(row) * G + jg);
+        for (int s = 1; s < S; ++s) {
+            const float4 b = __ldcg(base + s * part_stride + static_cast<size_t>(row) * G + jg);
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        float v[4] = {a.x, a.y, a.z, a.w};
+        if (p.bias != nullptr) {
+            if (p.bias_f32) {
+                const float4 bb = *reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + col);
+                v[0] += bb.x; v[1] += bb.y; v[2] += bb.z; v[3] += bb.w;
+            } else {
+                const uint2 h = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p.bias) + col);
+                const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                v[0] += b0.x; v[1] += b0.y; v[2] += b1.x; v[3] += b1.y;
+            }
+        }
+        if (p.activation == kActGelu) {
+            gelu_erf_pair(v[0], v[1]);
+            gelu_erf_pair(v[2], v[3]);
+        }
+        if (p.out_f32) {
+            float* y = static_cast<float*>(p.y) + row * p.ldy + col;
+            if (p.residual != nullptr) {
+                const float4 r = *reinterpret_cast<const float4*>(static_cast<const float*>(p.residual) + row * p.ldr + col);
+                v[0] += r.x; v[1] += r.y; v[2] += r.z; v[3] += r.w;
+            }
+            *reinterpret_cast<float4*>(y) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+            __half* y = static_cast<__half*>(p.y) + row * p.ldy + col;
+            if (p.residual != nullptr) {
+                const uint2 h = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p.residual) + row * p.ldr + col);
+                const float2 r0f = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                const float2 r1f = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                v[0] += r0f.x; v[1] += r0f.y; v[2] += r1f.x; v[3] += r1f.y;
+            }
+            __half2 h0 = __floats2half2_rn(v[0], v[1]);
+            __half2 h1 = __floats2half2_rn(v[2], v[3]);
+            uint2 o;
+            o.x = *reinterpret_cast<uint32_t*>(&h0);
+            o.y = *reinterpret_cast<uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(y) = o;
+        }
+    }
+}
+
 template <int RB>
 __global__ void __launch_bounds__(320, 1)
     decode_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ DecodeCodeMaps cm,
@@ -89,8 +169,15 @@ __global__ void __launch_bounds__(320, 1)
     const int lane = threadIdx.x & 31;
     const int nsub = p.m > 128 ? 2 : 1;
     const int num_items = (p.n_c + RB - 1) / RB;
-    const int num_k = (p.k_c + C::KB - 1) / C::KB;
+    const int num_k_all = (p.k_c + C::KB - 1) / C::KB;
     const int planes = 2 * p.stages;
+    // split-K: one item per cluster, this CTA's k-blocks [kb_lo, kb_lo + num_k)
+    const int S = p.splits;
+    const int split = S > 1 ? static_cast<int>(blockIdx.x) % S : 0;
+    const int first_item = S > 1 ? static_cast<int>(blockIdx.x) / S : static_cast<int>(blockIdx.x);
+    const int item_step = S > 1 ? num_items : static_cast<int>(gridDim.x);
+    const int kb_lo = split * num_k_all / S;
+    const int num_k = (split + 1) * num_k_all / S - kb_lo;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -120,15 +207,15 @@ __global__ void __launch_bounds__(320, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ------------------------------------------------------------ producer
+            // ------------------------------------------------------------ producer (split-K: see the end of the branch)
             int stage = 0;
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
             const uint32_t bytes = static_cast<uint32_t>(2 * nsub * C::A_BYTES + planes * C::CODE_BYTES);
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+            for (int item = first_item; item < num_items && ok; item += item_step) {
                 const int r0 = item * RB;
-                for (int kb = 0; kb < num_k; ++kb) {
+                for (int kb = kb_lo; kb < kb_lo + num_k; ++kb) {
                     if (!wait_bar(&empty_bar[stage], phase ^ 1, abort_flag, p.err, 501)) {
                         ok = false;
                         break;
@@ -162,6 +249,10 @@ __global__ void __launch_bounds__(320, 1)
                 wait_bar(&full_bar[s], ph, &no_abort, p.err, 502);
             }
         }
+        if (S > 1) {
+            __syncwarp();
+            cluster_sync();  // the split-K exchange barrier
+        }
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
@@ -170,10 +261,10 @@ __global__ void __launch_bounds__(320, 1)
             uint32_t phase = 0;
             uint32_t item_phase = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+            for (int item = first_item; item < num_items && ok; item += item_step) {
                 if (!wait_bar(tempty_bar, item_phase ^ 1, abort_flag, p.err, 601)) break;
                 tc_fence_after();
-                for (int kb = 0; kb < num_k; ++kb) {
+                for (int kb = kb_lo; kb < kb_lo + num_k; ++kb) {
                     // the x tiles come from TMA (full), the weight tiles from the decode warps (dec)
                     if (!wait_bar(&full_bar[stage], phase, abort_flag, p.err, 604) ||
                         !wait_bar(&dec_bar[stage], phase, abort_flag, p.err, 602)) {
@@ -189,7 +280,8 @@ __global__ void __launch_bounds__(320, 1)
                         const uint64_t a_re = umma_desc_sw128_kmajor(base + (2 * sub) * C::A_BYTES);
                         const uint64_t a_im = umma_desc_sw128_kmajor(base + (2 * sub + 1) * C::A_BYTES);
 #pragma unroll
-                        for (int kk = 0; kk < C::KB / 16; ++kk) umma_f16(d, a_re + 2 * kk, b_re + 2 * kk, idesc, (kb | kk) != 0);
+                        for (int kk = 0; kk < C::KB / 16; ++kk)
+                            umma_f16(d, a_re + 2 * kk, b_re + 2 * kk, idesc, ((kb - kb_lo) | kk) != 0);
 #pragma unroll
                         for (int kk = 0; kk < C::KB / 16; ++kk) umma_f16(d, a_im + 2 * kk, b_im + 2 * kk, idesc, 1);
                     }
@@ -207,6 +299,10 @@ __global__ void __launch_bounds__(320, 1)
             volatile int no_abort = 0;
             wait_bar(drain_bar, 0, &no_abort, p.err, 603);
         }
+        if (S > 1) {
+            __syncwarp();
+            cluster_sync();  // the split-K exchange barrier, which every thread of the cluster joins
+        }
     } else {
         // -------------------------------------------------------------- decode + epilogue
         // Two groups of four warps take alternate ring stages (more warps in
@@ -222,10 +318,10 @@ __global__ void __launch_bounds__(320, 1)
         // 1/gamma of this thread's rows for the current 256-column block, all
         // planes, as fp32 bit patterns; reloaded when the block changes
         uint32_t inv_r[ROWS_PER_THREAD][8], inv_i[ROWS_PER_THREAD][8];
-        for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        for (int item = first_item; item < num_items && ok; item += item_step) {
             const int r0 = item * RB;
             int cached_blk = -1;
-            for (int kb = 0; kb < num_k; ++kb) {
+            for (int kb = kb_lo; kb < kb_lo + num_k; ++kb) {
                 const int it = n++;
                 if ((it & 1) != group) continue;
                 const int stage = it % C::STAGES;
@@ -342,6 +438,33 @@ __global__ void __launch_bounds__(320, 1)
             tc_fence_after();
             const int valid = min(RB, p.n_c - r0);
             const int64_t col0 = static_cast<int64_t>(group) * p.n_c + r0;
+            if (S > 1) {
+                // split-K partial: this warp's 32 rows x RB columns of each sub-tile, raw
+                float* part = p.ws + (static_cast<size_t>(blockIdx.x) * nsub * 128) * (2 * RB) + group * RB;
+                for (int sub = 0; sub < nsub; ++sub) {
+                    uint32_t r[RB];
+                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                                           static_cast<uint32_t>(sub * C::NT + group * RB);
+                    if constexpr (RB == 16) {
+                        tmem_ld_32x32b_x16(taddr, r);
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < RB / 32; ++h)
+                            tmem_ld_32x32b_x32(taddr + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * h]));
+                    }
+                    tmem_ld_wait();
+                    float4* dst = reinterpret_cast<float4*>(part + static_cast<size_t>(sub * 128 + 32 * q + lane) * (2 * RB));
+#pragma unroll
+                    for (int j = 0; j < RB / 4; ++j)
+                        __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar);
+                item_phase ^= 1;
+                continue;
+            }
             for (int sub = 0; sub < nsub; ++sub) {
                 const int64_t row = static_cast<int64_t>(sub) * 128 + 32 * q + lane;
                 uint32_t r[RB];
@@ -423,6 +546,11 @@ __global__ void __launch_bounds__(320, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar);
             item_phase ^= 1;
+        }
+        if (S > 1) {
+            __syncwarp();
+            cluster_sync();  // every split's partial is written (release) and visible (acquire)
+            if (first_item < num_items) decode_splitk_reduce<RB>(p, first_item, split, nsub, threadIdx.x - 64);
         }
     }
 

@@ -430,7 +430,8 @@ int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, 
 constexpr int64_t kDecodeMaxRows = 256;
 
 template <int RB>
-int launch_decode(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx, DeviceState* st, cudaStream_t stream) {
+int launch_decode(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx, DeviceState* st, cudaStream_t stream,
+                  int splits_forced) {
     using C = DecodeCfg<RB>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_status[kMaxDevices];
@@ -474,8 +475,21 @@ int launch_decode(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx,
     p.out_f32 = (a->flags & RPFQ_GEMM_OUT_F32) ? 1 : 0;
     p.err = st->err_word;
     const int items = (L->n_c + RB - 1) / RB;
-    const int grid = items < st->sm_count ? items : st->sm_count;
-    RPFQ_CUDA(launch_kernel(decode_gemm_sm100_kernel<RB>, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, 1, tx,
+    // Split-K when the row blocks alone leave most SMs idle (fewer than a third
+    // of the SMs: ViT-B proj / fc2 at one image, 24 blocks; measured slower for
+    // qkv's 72): S CTAs per item (a cluster), at least two k-blocks each, items x
+    // S within the SM count, the partials within the caller's workspace.
+    const int num_k = (L->k_c + DecodeCfg<RB>::KB - 1) / DecodeCfg<RB>::KB;
+    const int nsub = a->m > 128 ? 2 : 1;
+    int S = std::min({kMaxSplits, num_k / 2, st->sm_count / items});
+    if (S < 2 || splits_forced == 1 || (splits_forced == 0 && 3 * items >= st->sm_count)) S = 1;
+    if (splits_forced > 1) S = std::min(splits_forced, num_k);
+    const uint64_t part_bytes = static_cast<uint64_t>(items) * S * nsub * 128 * 2 * RB * 4;
+    if (S > 1 && (!a->workspace || part_bytes > std::min<uint64_t>(a->workspace_bytes, ws_partial_bytes(st)))) S = 1;
+    p.splits = S;
+    p.ws = S > 1 ? static_cast<float*>(a->workspace) : nullptr;
+    const int grid = S > 1 ? items * S : (items < st->sm_count ? items : st->sm_count);
+    RPFQ_CUDA(launch_kernel(decode_gemm_sm100_kernel<RB>, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, S, tx,
                             cm, p));
     return RPFQ_OK;
 }
@@ -494,6 +508,10 @@ int decode_path(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx, c
         return fail(RPFQ_ERR_INVALID, "fused decode path: 16-byte aligned pointers and strides required");
     if (a->residual && (((a->flags & RPFQ_GEMM_RESIDUAL_F32) != 0) != ((a->flags & RPFQ_GEMM_OUT_F32) != 0)))
         return fail(RPFQ_ERR_UNSUPPORTED, "fused decode path: the residual must have the output's dtype");
+    if (a->split_k < 0 || a->split_k > kMaxSplits)
+        return fail(RPFQ_ERR_INVALID, "fused decode path: split_k must be 0..%d (got %d)", kMaxSplits, a->split_k);
+    if (a->workspace && !aligned16(a->workspace))
+        return fail(RPFQ_ERR_INVALID, "fused decode path: the workspace must be 16-byte aligned");
     for (int s = 0; s < L->stages; ++s) {
         const RpfqPhasePlane* ps[2] = {&L->u[s], &L->w[s]};
         for (const RpfqPhasePlane* pl : ps)
@@ -515,9 +533,11 @@ int decode_path(const RpfqWideLinearArgs* a, const uint16_t* xin, int64_t ldx, c
         const int64_t n_c = L->n_c;
         rb = (n_c + 63) / 64 >= st->sm_count ? 64 : ((n_c + 31) / 32 >= st->sm_count ? 32 : 16);
     }
-    if (rb == 64) return launch_decode<64>(a, xin, ldx, st, stream);
-    if (rb == 32) return launch_decode<32>(a, xin, ldx, st, stream);
-    return launch_decode<16>(a, xin, ldx, st, stream);
+    // split_k as for the GEMM: 0 automatic, 1 never, 2..8 forced
+    const int sf = a->split_k;
+    if (rb == 64) return launch_decode<64>(a, xin, ldx, st, stream, sf);
+    if (rb == 32) return launch_decode<32>(a, xin, ldx, st, stream, sf);
+    return launch_decode<16>(a, xin, ldx, st, stream, sf);
 }
 
 int pick_block_n(int64_t m, int n, int sm_count) {

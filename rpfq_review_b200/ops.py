@@ -516,7 +516,9 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
 
     ``bias`` (optional) replaces ``layer.bias`` for this call, e.g. the same
     values widened to fp32 once, which the epilogue adds without converting.
-    ``split_k`` as in :func:`gemm` (dense path)."""
+    ``split_k`` as in :func:`gemm` (both paths: the fused decode splits K over
+    a cluster of CTAs per block of output rows when those blocks alone leave
+    most SMs idle)."""
     _require(x, "x")
     if dense is not None:
         _require(dense, "dense")
@@ -538,7 +540,7 @@ def wide_linear(x: torch.Tensor, layer: PackedLayer, dense: torch.Tensor | None,
     scratch = torch.empty((m, K), dtype=torch.float16, device=x.device) if act_bits else None
     s = layer_struct(layer)
     split_k = SPLIT_K if split_k is None else int(split_k)
-    ws, ws_bytes = _workspace(x.device, split_k) if dense is not None else (None, 0)
+    ws, ws_bytes = _workspace(x.device, split_k)
     a = _lib.RpfqWideLinearArgs(layer=ctypes.pointer(s), dense=_p(dense), x=x2.data_ptr(), ldx=ldx,
                                 bias=_p(bias), residual=_p(r2), ldr=ldr, y=y2.data_ptr(), ldy=ldy, m=m,
                                 act_bits=int(act_bits), activation=_ACT[activation], scratch=_p(scratch),

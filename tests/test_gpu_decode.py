@@ -153,3 +153,44 @@ def test_fused_decode_no_device_errors(cuda):
     from rpfq_review_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
+
+
+# ViT-B layers at one image (m = 197) and shapes whose row blocks leave most
+# SMs idle: the fused decode splits K over a cluster of CTAs per row block.
+SPLIT_SHAPES = [
+    (197, 384, 1536, 2, "residual"),  # fc2: 24 row blocks x 6 splits
+    (197, 384, 384, 2, "residual"),   # proj: 24 x 3
+    (197, 1152, 384, 2, "none"),      # qkv: 72 x 2
+    (198, 192, 768, 2, "gelu"),       # DeiT-S fc1-like, 12 blocks
+    (5, 64, 520, 2, "none"),          # K tail inside a stage, ragged rows
+    (256, 40, 1024, 1, "residual"),   # one stage, ragged last block
+]
+
+
+@pytest.mark.parametrize("m,n_c,k_c,stages,epi", SPLIT_SHAPES)
+@pytest.mark.parametrize("split_k", [0, 2, 8])
+def test_fused_decode_split_k(cuda, m, n_c, k_c, stages, epi, split_k):
+    """Split-K against the oracle and the unsplit kernel (the partials are
+    summed in a fixed order: two calls are bit-identical)."""
+    ops = _ops()
+    layer = _layer(n_c, k_c, stages, seed=m * 7 + n_c + k_c, device=cuda)
+    g = torch.Generator().manual_seed(m + k_c)
+    x = torch.randn((m, 2 * k_c), generator=g).half().to(cuda)
+    res = torch.randn((m, 2 * n_c), generator=g).float().to(cuda) if epi == "residual" else None
+    act = "gelu" if epi == "gelu" else "none"
+
+    def run(split):
+        out = res.clone() if res is not None else None
+        return ops.wide_linear(x, layer, None, residual=out, out=out, activation=act,
+                               out_dtype=torch.float32 if res is not None else torch.float16, split_k=split)
+
+    y = run(split_k)
+    y2 = run(split_k)
+    y1 = run(1)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    ref = _reference(layer, x, gelu=epi == "gelu", residual=res)
+    assert rel_err(y.cpu().numpy(), ref) <= TOL
+    assert rel_err(y.cpu().double().numpy(), y1.cpu().double().numpy()) <= TOL
+    from rpfq_review_b200 import _lib
+    assert _lib.device_error() == 0
