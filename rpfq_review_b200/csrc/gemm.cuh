@@ -49,8 +49,8 @@
 // its share. A share is at least one tile long, so a tile is cut at most
 // once, into a head (its first k-blocks, the end of one unit's share) and a
 // tail (the rest, the start of the next unit's share). A unit runs its head
-// first (right after its data-parallel tiles), then its whole tiles, then its
-// tail. The head's unit writes its raw fp32 accumulator to its workspace
+// first of all (before its data-parallel tiles), then its data-parallel and
+// whole tiles, then its tail. The head's unit writes its raw fp32 accumulator to its workspace
 // slot in the epilogue warps' own layout and raises one flag per epilogue
 // warp. For the tail, the epilogue warps wait for the flags (bounded, like
 // every wait here) and load that accumulator into the tail's TMEM buffer
@@ -106,7 +106,7 @@ struct Schedule {
     int next_dp;
     int64_t lo, hi;          // this unit's stream-K k-blocks [lo, hi)
     int64_t whole, whole_end;  // whole tiles of the share: [whole, whole_end) in k-blocks
-    int phase;               // 0 data-parallel, 1 head, 2 whole tiles, 3 tail, 4 done
+    int phase;               // 0 head, 1 data-parallel, 2 whole tiles, 3 tail, 4 done
 
     __device__ __forceinline__ Schedule(int unit, int units_, int num_tiles, int num_k_, int sk_tiles, int kb_lo,
                                         int kb_hi)
@@ -127,10 +127,19 @@ struct Schedule {
         w.mode = mode;
     }
 
-    // Order of a share: the head first (the next unit's tail waits for it), whole
-    // tiles, the tail last (it waits for the previous unit's head).
+    // Order: the head first of all (the next unit's tail waits for it, and its
+    // accumulator store then overlaps the main loops that follow), the
+    // data-parallel tiles, the share's whole tiles, the tail last (it waits for
+    // the previous unit's head, loaded while the item before it computes).
     __device__ __forceinline__ bool next(WorkItem& w) {
         if (phase == 0) {
+            phase = 1;
+            if (lo < hi && whole_end < hi) {  // the share ends inside a tile
+                set(w, whole_end, hi, kItemHead);
+                return true;
+            }
+        }
+        if (phase == 1) {
             if (next_dp < dp_tiles) {
                 w.tile = next_dp;
                 w.kb_lo = dp_kb_lo;
@@ -139,14 +148,7 @@ struct Schedule {
                 next_dp += units;
                 return true;
             }
-            phase = lo < hi ? 1 : 4;
-        }
-        if (phase == 1) {
-            phase = 2;
-            if (whole_end < hi) {  // ends inside a tile
-                set(w, whole_end, hi, kItemHead);
-                return true;
-            }
+            phase = lo < hi ? 2 : 4;
         }
         if (phase == 2) {
             if (whole < whole_end) {

@@ -569,13 +569,15 @@ struct GemmPlan {
 
 constexpr double kSkMinIdleKBlocks = 24.0;  // see plan_gemm
 
-// Stream-K on by default; RPFQ_STREAM_K=0 turns it off (data-parallel waves only).
-bool stream_k_enabled() {
-    static const bool on = [] {
+// Stream-K: RPFQ_STREAM_K=0 off (data-parallel waves only), 1 (default) by the
+// cost rule of plan_gemm, 2 whenever the tiles leave a tail (measurement).
+int stream_k_mode() {
+    static const int mode = [] {
         const char* e = std::getenv("RPFQ_STREAM_K");
-        return !(e && e[0] == '0');
+        if (!e || !e[0]) return 1;
+        return e[0] == '0' ? 0 : (e[0] == '2' ? 2 : 1);
     }();
-    return on;
+    return mode;
 }
 
 // Time (us) of a one-CTA-per-tile plan when few tiles leave SMs idle, fitted
@@ -616,14 +618,14 @@ GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split
     // 0.5 us, so the tail is taken only when the idle part of the last wave is at
     // least 24 k-blocks long (ViT-B fc2 at 32 images: 0.99 x 48; qkv, fc1 and proj
     // with K = 768 lose).
-    if (sk_ws && stream_k_enabled() && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
+    if (sk_ws && stream_k_mode() > 0 && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
         pair_tiles >= st->sm_count / 2) {
         const int units = gemm_units<256, false, 0, true>(st);
         const int num_k = (k + 63) / 64;
         if (units > 0 && sk_tail(pair_tiles, units) > 0) {
             const int64_t waves = (pair_tiles + units - 1) / units;
             const double idle = static_cast<double>(waves) - static_cast<double>(pair_tiles) / units;
-            if (idle * num_k >= kSkMinIdleKBlocks) {
+            if (stream_k_mode() == 2 || idle * num_k >= kSkMinIdleKBlocks) {
                 g.bn = 256;
                 g.pair = true;
                 g.splits = 1;

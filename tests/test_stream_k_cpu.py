@@ -2,8 +2,8 @@
 rpfq_b200.cu ``sk_tail``, restated here line for line): over many tile /
 unit / k-block counts every (tile, k-block) is computed exactly once, a tile
 is cut at most once into a head (k-blocks from 0) and a tail (the rest); a
-unit's head is its first stream-K item and its tail its last, and the tail's
-head is the previous unit's. The kernel loads a tail's head while the item
+unit's head is its first item of all (before its data-parallel tiles) and its
+tail its last, and the tail's head is the previous unit's. The kernel loads a tail's head while the item
 before the tail runs, or right after flagging its own head when that is the
 item before — so a unit's head never waits, and no wait chains through
 units."""
@@ -21,19 +21,20 @@ def sk_tail(tiles: int, units: int) -> int:
 
 def schedule(unit: int, units: int, num_tiles: int, num_k: int, sk_tiles: int):
     dp_tiles = num_tiles - sk_tiles
-    items = [(t, 0, num_k, "whole") for t in range(unit, dp_tiles, units)]
     total = sk_tiles * num_k
     lo, hi = unit * total // units, (unit + 1) * total // units
-    if lo >= hi:
-        return items
     whole, whole_end = -(-lo // num_k) * num_k, hi // num_k * num_k
 
     def seg(a, b, mode):
         j = a // num_k
         return (dp_tiles + j, a - j * num_k, b - j * num_k, mode)
 
-    if whole_end < hi:
+    items = []
+    if lo < hi and whole_end < hi:
         items.append(seg(whole_end, hi, "head"))
+    items += [(t, 0, num_k, "whole") for t in range(unit, dp_tiles, units)]
+    if lo >= hi:
+        return items
     for a in range(whole, whole_end, num_k):
         items.append(seg(a, a + num_k, "whole"))
     if lo % num_k:
@@ -67,7 +68,7 @@ def test_schedule_invariants(tiles, units, num_k):
                 heads = [x for x in prev if x[3] == "head"]
                 assert heads == [(t, 0, lo, "head")], "the previous unit holds the head"
             if mode == "head":
-                assert i == n_dp, "a head is the unit's first stream-K item"
+                assert i == 0, "a head is the unit's first item"
                 assert per_unit[u + 1][-1] == (t, hi, num_k, "tail")
     assert len(seen) == tiles * num_k
 
