@@ -108,7 +108,11 @@ int rpfq_prepack_sm100(const RpfqPackedLinear* layer, uint16_t* dense_out, int32
  * stream-K. split_k: 0 = automatic, 1 = never, 2..8 = that many splits
  * (needs the workspace). Partials are summed in a fixed order: results are
  * deterministic for a given shape. RPFQ_STREAM_K=0 in the environment turns
- * the stream-K tail off. */
+ * the stream-K tail off. Narrow tail (no workspace needed, takes precedence):
+ * when the CTA-pair tiles leave a last wave at most half full, those tiles
+ * are cut into 2 or 4 column pieces dealt out over the idle pairs; every
+ * output is still accumulated over all of K in one pass, so the results are
+ * those of whole tiles. RPFQ_NARROW_TAIL=0 turns it off. */
 typedef struct RpfqGemmArgs {
     const uint16_t* x;        /* fp16 [m, k], row stride ldx (elements)                */
     int64_t ldx;
@@ -147,6 +151,8 @@ typedef struct RpfqGemmPlan {
     int32_t stream_k_tiles;  /* tiles of the stream-K tail (0: whole tiles only)          */
     int32_t units;           /* persistent CTAs / CTA pairs (split-K: tiles)             */
     int32_t tiles;           /* output tiles                                              */
+    int32_t tail_tiles;      /* narrow tail: last-wave tiles cut into column pieces      */
+    int32_t pieces;          /* narrow tail: pieces per such tile (0: none; 2 or 4)      */
 } RpfqGemmPlan;
 int rpfq_gemm_plan_sm100(const RpfqGemmArgs* args, RpfqGemmPlan* plan);
 

@@ -55,7 +55,8 @@ EXPORTED_SYMBOLS = (
 
 class RpfqGemmPlan(ctypes.Structure):
     _fields_ = [("block_n", ctypes.c_int32), ("cta_pair", ctypes.c_int32), ("split_k", ctypes.c_int32),
-                ("stream_k_tiles", ctypes.c_int32), ("units", ctypes.c_int32), ("tiles", ctypes.c_int32)]
+                ("stream_k_tiles", ctypes.c_int32), ("units", ctypes.c_int32), ("tiles", ctypes.c_int32),
+                ("tail_tiles", ctypes.c_int32), ("pieces", ctypes.c_int32)]
 
 
 class RpfqPhasePlane(ctypes.Structure):

@@ -61,6 +61,14 @@
 // epilogue runs and the reader clears the flags. All units are resident at
 // once (the grid is the co-resident cluster count), and a head never waits
 // for anything, so every wait ends.
+//
+// Narrow tail (p.pieces = P > 0; CTA pairs): when the tiles leave a last wave
+// at most half full, the last p.tail_tiles tiles are cut into P column pieces
+// of BN / P (64 or 128) columns each — one MMA of N = BN / P per k-block, the
+// weight rows through a second tensor map with that box — and the pieces are
+// dealt out over the units after their whole tiles. Every output element is
+// still accumulated over all of K in one TMEM buffer, in the same order, so
+// the results are those of whole tiles; no exchange between units.
 #pragma once
 
 #include "ptx.cuh"
@@ -84,6 +92,8 @@ struct GemmParams {
     int64_t ldy;
     int* err;                // device error word
     int32_t sk_tiles;        // stream-K: tiles shared out by k-blocks over all units (0: none)
+    int32_t tail_tiles;      // narrow tail: the last tail_tiles tiles are cut into `pieces` column pieces
+    int32_t pieces;          // 0: none; else 2 or 4 (BN / pieces columns per piece)
     int* sk_flags;           // stream-K: [units * ranks][8] flags (partial of an epilogue warp written); zero
                              // between calls
 };
@@ -95,42 +105,50 @@ struct WorkItem {
     int tile;
     int kb_lo, kb_hi;  // k-blocks [kb_lo, kb_hi) of the tile
     int mode;          // kItemWhole, kItemHead or kItemTail
+    int n_off;         // first column of the item within the tile (narrow-tail pieces)
+    int width;         // columns of the item: BN, or BN / pieces
 };
 // kItemHead: k-blocks [0, kb_hi < num_k) of a cut tile, the accumulator goes to
 // the workspace; kItemTail: k-blocks [kb_lo > 0, num_k), the accumulator starts
 // from the head's and the epilogue follows.
 enum : int { kItemWhole = 0, kItemHead = 1, kItemTail = 2 };
 
+template <int BN>
 struct Schedule {
     int units, num_k, dp_tiles, dp_kb_lo, dp_kb_hi;
     int next_dp;
-    int64_t lo, hi;          // this unit's stream-K k-blocks [lo, hi)
-    int64_t whole, whole_end;  // whole tiles of the share: [whole, whole_end) in k-blocks
-    int phase;               // 0 head, 1 data-parallel, 2 whole tiles, 3 tail, 4 done
+    int pieces, piece_items, next_piece;  // narrow tail
+    int lo, hi;              // this unit's stream-K k-blocks [lo, hi) (tiles x k-blocks < 2^31)
+    int whole, whole_end;    // whole tiles of the share: [whole, whole_end) in k-blocks
+    int phase;               // 0 head, 1 data-parallel and pieces, 2 whole tiles, 3 tail, 4 done
 
     __device__ __forceinline__ Schedule(int unit, int units_, int num_tiles, int num_k_, int sk_tiles, int kb_lo,
-                                        int kb_hi)
-        : units(units_), num_k(num_k_), dp_tiles(num_tiles - sk_tiles), dp_kb_lo(kb_lo), dp_kb_hi(kb_hi),
-          next_dp(unit), phase(0) {
+                                        int kb_hi, int tail_tiles = 0, int pieces_ = 0)
+        : units(units_), num_k(num_k_), dp_tiles(num_tiles - sk_tiles - (pieces_ > 0 ? tail_tiles : 0)),
+          dp_kb_lo(kb_lo), dp_kb_hi(kb_hi), next_dp(unit), pieces(pieces_),
+          piece_items(pieces_ > 0 ? tail_tiles * pieces_ : 0), next_piece(unit), phase(0) {
         const int64_t total = static_cast<int64_t>(sk_tiles) * num_k;
-        lo = static_cast<int64_t>(unit) * total / units_;
-        hi = static_cast<int64_t>(unit + 1) * total / units_;
+        lo = static_cast<int>(static_cast<int64_t>(unit) * total / units_);
+        hi = static_cast<int>(static_cast<int64_t>(unit + 1) * total / units_);
         whole = (lo + num_k - 1) / num_k * num_k;  // first tile boundary at or after lo
         whole_end = hi / num_k * num_k;            // last tile boundary at or before hi
     }
 
-    __device__ __forceinline__ void set(WorkItem& w, int64_t a, int64_t b, int mode) const {
-        const int j = static_cast<int>(a / num_k);
+    __device__ __forceinline__ void set(WorkItem& w, int a, int b, int mode) const {
+        const int j = a / num_k;
         w.tile = dp_tiles + j;
-        w.kb_lo = static_cast<int>(a - static_cast<int64_t>(j) * num_k);
-        w.kb_hi = static_cast<int>(b - static_cast<int64_t>(j) * num_k);
+        w.kb_lo = a - j * num_k;
+        w.kb_hi = b - j * num_k;
         w.mode = mode;
+        w.n_off = 0;
+        w.width = BN;
     }
 
     // Order: the head first of all (the next unit's tail waits for it, and its
     // accumulator store then overlaps the main loops that follow), the
-    // data-parallel tiles, the share's whole tiles, the tail last (it waits for
-    // the previous unit's head, loaded while the item before it computes).
+    // data-parallel tiles and narrow-tail pieces, the share's whole tiles, the
+    // tail last (it waits for the previous unit's head, loaded while the item
+    // before it computes).
     __device__ __forceinline__ bool next(WorkItem& w) {
         if (phase == 0) {
             phase = 1;
@@ -145,7 +163,20 @@ struct Schedule {
                 w.kb_lo = dp_kb_lo;
                 w.kb_hi = dp_kb_hi;
                 w.mode = kItemWhole;
+                w.n_off = 0;
+                w.width = BN;
                 next_dp += units;
+                return true;
+            }
+            if (next_piece < piece_items) {  // narrow tail: pieces after the whole tiles
+                const int pw = BN / pieces;
+                w.tile = dp_tiles + next_piece / pieces;
+                w.kb_lo = dp_kb_lo;
+                w.kb_hi = dp_kb_hi;
+                w.mode = kItemWhole;
+                w.n_off = (next_piece % pieces) * pw;
+                w.width = pw;
+                next_piece += units;
                 return true;
             }
             phase = lo < hi ? 2 : 4;
@@ -379,7 +410,7 @@ template <int BN, bool OUT_F32, int RES, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_f16_sm100_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r,
-                          const GemmParams p) {
+                          const __grid_constant__ CUtensorMap tm_wp, const GemmParams p) {
     using C = GemmCfg<BN, RES, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -416,7 +447,10 @@ __global__ void __launch_bounds__(384, 1)
     // units: CTA pairs or CTAs (split-K: tiles); stream-K only without split-K
     constexpr int RANKS = PAIR ? 2 : 1;
     const int sk_tiles = splits == 1 ? p.sk_tiles : 0;
-    auto schedule = [&]() { return Schedule(first_tile, tile_step, num_tiles, num_k, sk_tiles, kb_lo, kb_hi); };
+    const int pieces = (PAIR && splits == 1 && sk_tiles == 0) ? p.pieces : 0;
+    auto schedule = [&]() {
+        return Schedule<BN>(first_tile, tile_step, num_tiles, num_k, sk_tiles, kb_lo, kb_hi, p.tail_tiles, pieces);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -434,6 +468,7 @@ __global__ void __launch_bounds__(384, 1)
         fence_barrier_init();
         prefetch_tmap(&tm_x);
         prefetch_tmap(&tm_w);
+        if (pieces) prefetch_tmap(&tm_wp);
         prefetch_tmap(&tm_y);
         if (use_res) prefetch_tmap(&tm_r);
     }
@@ -462,12 +497,17 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            Schedule sched = schedule();
+            auto sched = schedule();
             WorkItem w;
             while (ok && sched.next(w)) {
                 const int tile = w.tile;
+                const bool piece = w.width != BN;
+                // a piece's weight rows: width / 2 per CTA of a pair, through tm_wp
+                const int b_rows = PAIR ? w.width / 2 : w.width;
+                const uint32_t stage_bytes = static_cast<uint32_t>(C::A_BYTES + b_rows * C::BK * 2);
                 const int m0 = (tile / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
-                const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * C::B_ROWS;
+                const int n0 = (tile % num_n) * BN + w.n_off + static_cast<int>(rank) * b_rows;
+                const CUtensorMap* tw = piece ? &tm_wp : &tm_w;
                 for (int kb = w.kb_lo; kb < w.kb_hi; ++kb) {
                     if (!wait_bar(&empty_bar[stage], phase ^ 1, abort_flag, p.err, 101)) {
                         ok = false;
@@ -476,14 +516,14 @@ __global__ void __launch_bounds__(384, 1)
                     uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
                     if constexpr (PAIR) {
                         // both CTAs' bytes complete on the leader's full barrier
-                        if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+                        if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * stage_bytes);
                         const uint32_t leader_full = mapa_shared(smem_u32(&full_bar[stage]), 0);
                         tma_load_2d_pair(sa, &tm_x, leader_full, kb * C::BK, m0);
-                        tma_load_2d_pair(sa + C::A_BYTES, &tm_w, leader_full, kb * C::BK, n0);
+                        tma_load_2d_pair(sa + C::A_BYTES, tw, leader_full, kb * C::BK, n0);
                     } else {
-                        mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+                        mbar_arrive_expect_tx(&full_bar[stage], stage_bytes);
                         tma_load_2d(sa, &tm_x, &full_bar[stage], kb * C::BK, m0);
-                        tma_load_2d(sa + C::A_BYTES, &tm_w, &full_bar[stage], kb * C::BK, n0);
+                        tma_load_2d(sa + C::A_BYTES, tw, &full_bar[stage], kb * C::BK, n0);
                     }
                     ++issued;
                     if (++stage == C::STAGES) {
@@ -509,7 +549,7 @@ __global__ void __launch_bounds__(384, 1)
             }
         } else if (warp == 1 && lane == 0 && rank == 0) {
             // -------------------------------------------------------- MMA issuer
-            constexpr uint32_t idesc = umma_idesc_f16(C::TILE_M, BN);
+            constexpr uint32_t idesc_full = umma_idesc_f16(C::TILE_M, BN);
             // commits go to this CTA's barrier and, for pairs, to the peer's as well
             auto commit_both = [&](uint64_t* bar) {
                 if constexpr (PAIR) {
@@ -525,7 +565,7 @@ __global__ void __launch_bounds__(384, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            Schedule sched = schedule();
+            auto sched = schedule();
             WorkItem w;
             while (ok && sched.next(w)) {
                 if (!wait_bar<PAIR>(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.err, 201)) break;
@@ -535,6 +575,8 @@ __global__ void __launch_bounds__(384, 1)
                 if (cont && !wait_bar<PAIR>(loaded_bar, 0, abort_flag, p.err, 204)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                // a narrow-tail piece: N = its width (the accumulator's first columns)
+                const uint32_t idesc = w.width == BN ? idesc_full : umma_idesc_f16(C::TILE_M, w.width);
                 for (int kb = w.kb_lo; kb < w.kb_hi; ++kb) {
                     if (!wait_bar(&full_bar[stage], phase, abort_flag, p.err, 202)) {
                         ok = false;
@@ -583,14 +625,14 @@ __global__ void __launch_bounds__(384, 1)
                 if (it.mode == kItemHead) return;  // no epilogue output
                 const int t = it.tile;
                 const int r0 = (t / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
-                const int c0 = (t % num_n) * BN;
-                for (int c = c0; c < c0 + BN && c < p.n; c += PCW)
+                const int c0 = (t % num_n) * BN + it.n_off;
+                for (int c = c0; c < c0 + it.width && c < p.n; c += PCW)
                     for (int r = r0; r < r0 + C::BM && r < p.m; r += 32) tma_prefetch_l2_2d(&tm_r, c, r);
             };
-            Schedule lead = schedule();  // two items ahead of the accumulators
+            auto lead = schedule();  // two items ahead of the accumulators
             WorkItem wl;
             for (int i = 0; i < 2 && lead.next(wl); ++i) prefetch_item(wl);
-            Schedule sched = schedule();
+            auto sched = schedule();
             WorkItem w;
             int acc = 0;
             uint32_t acc_phase = 0;
@@ -680,14 +722,17 @@ __global__ void __launch_bounds__(384, 1)
             return true;
         };
         bool tail_loaded = false;
-        Schedule sched = schedule();
+        auto sched = schedule();
         WorkItem w;
         while (sched.next(w)) {
             const int tile = w.tile;
             const int64_t m0 = static_cast<int64_t>(tile / num_n) * C::TILE_M + static_cast<int64_t>(rank) * C::BM;
-            const int c_begin = (tile % num_n) * BN + col_half * HALF;
+            // a narrow-tail piece (width <= HALF) is drained by the first column half's warps
+            const bool piece = w.width != BN;
+            const int c_begin = (tile % num_n) * BN + w.n_off + (piece ? 0 : col_half * HALF);
             const int64_t row0 = m0 + 32 * q;
-            const int valid = min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
+            const int valid = piece ? (col_half == 0 ? min(w.width, p.n - c_begin) : 0)
+                                    : min(HALF, p.n - c_begin);  // may be <= 0 for the last tile
             const int nsteps = (valid > 0 && row0 < p.m) ? (valid + CW - 1) / CW : 0;
             // raw accumulator out instead of an epilogue: split-K, or the head of a cut stream-K tile
             const bool partial = splits > 1 || w.mode == kItemHead;
@@ -699,7 +744,7 @@ __global__ void __launch_bounds__(384, 1)
                 }
             }
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
-                                   static_cast<uint32_t>(acc * BN + col_half * HALF);
+                                   static_cast<uint32_t>(acc * BN + (piece ? 0 : col_half * HALF));
             // stream-K tail: the previous unit's head goes into the tail's TMEM buffer
             // before the tail's MMAs start, while the item before it is still being
             // computed (that buffer was freed by this warp's previous epilogue). When
@@ -712,7 +757,7 @@ __global__ void __launch_bounds__(384, 1)
                     tail_loaded = true;
                 }
                 WorkItem nx;
-                Schedule look = sched;
+                auto look = sched;
                 if (look.next(nx) && nx.mode == kItemTail) {
                     if (w.mode == kItemHead) {
                         preload_after_head = true;

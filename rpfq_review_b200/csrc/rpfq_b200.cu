@@ -257,6 +257,25 @@ int sk_tail(int64_t tiles, int units) {
     return static_cast<int>(tiles - (tiles / units - 1) * units);
 }
 
+// Narrow tail for `tiles` tiles over `units` units: when the last wave is at
+// most half full, its tiles are cut into pieces (4 of BN / 4 columns, or 2 of
+// BN / 2 when four would exceed the units); 0 = none.
+int narrow_pieces(int64_t tiles, int units) {
+    if (units <= 0 || tiles < units) return 0;
+    const int64_t rem = tiles % units;
+    if (rem == 0 || 2 * rem > units) return 0;
+    return 4 * rem <= units ? 4 : 2;
+}
+
+// Narrow tail on by default; RPFQ_NARROW_TAIL=0 turns it off (measurement).
+bool narrow_tail_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("RPFQ_NARROW_TAIL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 // Workspace: split-K / stream-K partials, then the stream-K flag words.
 uint64_t ws_partial_bytes(const DeviceState* st) { return static_cast<uint64_t>(st->sm_count) * 128u * 256u * 4u; }
 constexpr uint64_t kSkFlagBytes = 8192;  // >= SMs x 8 epilogue warps x 4 B
@@ -306,7 +325,7 @@ int gemm_sk_tiles(int64_t tiles, DeviceState* st) {
 
 template <int BN, bool OUT_F32, int RES, bool PAIR>
 int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits, bool stream_k,
-                RpfqGemmPlan* dry) {
+                bool narrow, RpfqGemmPlan* dry) {
     using C = GemmCfg<BN, RES, PAIR>;
     constexpr int CW = OUT_F32 ? 32 : 64;   // output / residual columns per 128-B step
     constexpr int ESZ = OUT_F32 ? 4 : 2;
@@ -327,8 +346,18 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int
     p.sk_tiles = 0;
     p.sk_flags = stream_k ? reinterpret_cast<int*>(static_cast<uint8_t*>(a->workspace) + ws_partial_bytes(st))
                           : nullptr;
+    p.tail_tiles = 0;
+    p.pieces = 0;
     const int64_t tiles = ((a->m + C::TILE_M - 1) / C::TILE_M) * ((a->n + BN - 1) / BN);
-    if (stream_k) p.sk_tiles = gemm_sk_tiles<BN, OUT_F32, RES, PAIR>(tiles, st);
+    if constexpr (PAIR) {
+        // narrow tail first (no exchange between units); stream-K otherwise
+        if (narrow && splits <= 1) {
+            const int units = gemm_units<BN, OUT_F32, RES, true>(st);
+            p.pieces = narrow_pieces(tiles, units);
+            if (p.pieces) p.tail_tiles = static_cast<int32_t>(tiles % units);
+        }
+    }
+    if (stream_k && !p.pieces) p.sk_tiles = gemm_sk_tiles<BN, OUT_F32, RES, PAIR>(tiles, st);
     // grid: persistent units (CTA pairs or CTAs, as many as are resident at once; with a
     // stream-K tail exactly that many), or tiles x splits CTAs for split-K
     int units;
@@ -348,23 +377,28 @@ int launch_gemm(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int
         dry->stream_k_tiles = p.sk_tiles;
         dry->units = units;
         dry->tiles = static_cast<int32_t>(tiles);
+        dry->tail_tiles = p.tail_tiles;
+        dry->pieces = p.pieces;
         return RPFQ_OK;
     }
-    CUtensorMap tx, tw, ty, tr;
+    CUtensorMap tx, tw, ty, tr, twp;
     int rc = make_tmap_f16(&tx, a->x, a->m, a->k, a->ldx, C::BM, C::BK);
     if (!rc) rc = make_tmap_f16(&tw, a->w, a->n, a->k, a->k, C::B_ROWS, C::BK);
+    // narrow-tail pieces: BN / pieces columns, half of them per CTA of a pair
+    if (!rc && p.pieces) rc = make_tmap_f16(&twp, a->w, a->n, a->k, a->k, C::B_ROWS / p.pieces, C::BK);
     if (!rc) rc = make_tmap_f16(&ty, a->y, a->m, a->n, a->ldy, 32, CW, ESZ);
     // residual: same [32 rows x 128 B] boxes as the output (TMA loads + L2 prefetches)
     if (!rc && RES > 0) rc = make_tmap_f16(&tr, a->residual, a->m, a->n, a->ldr, 32, CW, ESZ);
     if (rc) return rc;
     if (RES == 0) tr = ty;
+    if (!p.pieces) twp = tw;
     if constexpr (PAIR) {
         RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, true>, dim3(2 * units), dim3(C::THREADS),
-                                C::SMEM_BYTES, stream, 2, tx, tw, ty, tr, p));
+                                C::SMEM_BYTES, stream, 2, tx, tw, ty, tr, twp, p));
     } else {
         // split-K: one CTA per (tile, split), the splits of a tile in one cluster
         RPFQ_CUDA(launch_kernel(gemm_f16_sm100_kernel<BN, OUT_F32, RES, false>, dim3(units * p.splits),
-                                dim3(C::THREADS), C::SMEM_BYTES, stream, p.splits, tx, tw, ty, tr, p));
+                                dim3(C::THREADS), C::SMEM_BYTES, stream, p.splits, tx, tw, ty, tr, twp, p));
     }
     return RPFQ_OK;
 }
@@ -412,18 +446,18 @@ uint64_t splitk_bytes(int64_t m, int n, int bn, int s) {
 // and the epilogue must hide the residual latency itself; one otherwise.
 // Split-K reads the residual in its reduction: no staging slots.
 template <int BN, bool PAIR>
-int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits, bool sk,
+int launch_gemm_bn(const RpfqGemmArgs* a, DeviceState* st, cudaStream_t stream, int splits, bool sk, bool narrow,
                    RpfqGemmPlan* dry) {
     const bool f32 = (a->flags & RPFQ_GEMM_OUT_F32) != 0;
     const int res = (a->residual == nullptr || splits > 1) ? 0 : (a->k <= 1024 ? 2 : 1);
     if (f32) {
-        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream, splits, sk, dry);
-        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream, splits, sk, dry);
-        return launch_gemm<BN, true, 0, PAIR>(a, st, stream, splits, sk, dry);
+        if (res == 2) return launch_gemm<BN, true, 2, PAIR>(a, st, stream, splits, sk, narrow, dry);
+        if (res == 1) return launch_gemm<BN, true, 1, PAIR>(a, st, stream, splits, sk, narrow, dry);
+        return launch_gemm<BN, true, 0, PAIR>(a, st, stream, splits, sk, narrow, dry);
     }
-    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream, splits, sk, dry);
-    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream, splits, sk, dry);
-    return launch_gemm<BN, false, 0, PAIR>(a, st, stream, splits, sk, dry);
+    if (res == 2) return launch_gemm<BN, false, 2, PAIR>(a, st, stream, splits, sk, narrow, dry);
+    if (res == 1) return launch_gemm<BN, false, 1, PAIR>(a, st, stream, splits, sk, narrow, dry);
+    return launch_gemm<BN, false, 0, PAIR>(a, st, stream, splits, sk, narrow, dry);
 }
 
 // ---------------------------------------------------------------- K3 fused decode launch
@@ -565,6 +599,7 @@ struct GemmPlan {
     bool pair;       // CTA pairs (256 x 256 tiles)
     int splits;      // K splits per tile (one CTA per tile)
     bool stream_k;   // a stream-K tail when the tiles do not fill whole waves
+    bool narrow;     // a narrow tail (last-wave tiles cut into column pieces)
 };
 
 constexpr double kSkMinIdleKBlocks = 24.0;  // see plan_gemm
@@ -610,6 +645,7 @@ GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split
                    bool sk_ws = false) {
     GemmPlan g;
     g.stream_k = false;
+    g.narrow = false;
     const int64_t pair_tiles = ((m + 255) / 256) * ((n + 255) / 256);
     // A stream-K tail turns the last, partly idle wave of 256 x 256 pair tiles into
     // an even share per pair, at the price of moving each cut tile's fp32
@@ -618,6 +654,16 @@ GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split
     // 0.5 us, so the tail is taken only when the idle part of the last wave is at
     // least 24 k-blocks long (ViT-B fc2 at 32 images: 0.99 x 48; qkv, fc1 and proj
     // with K = 768 lose).
+    // A last wave at most half full: CTA pairs with the narrow tail (the last
+    // wave's tiles cut into column pieces), which needs no workspace.
+    if (narrow_tail_enabled() && block_n == 0 && cta_pair == 0 && split_k <= 1 && pair_tiles >= st->sm_count / 2 &&
+        narrow_pieces(pair_tiles, gemm_units<256, false, 0, true>(st)) > 0) {
+        g.bn = 256;
+        g.pair = true;
+        g.splits = 1;
+        g.narrow = true;
+        return g;
+    }
     if (sk_ws && stream_k_mode() > 0 && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
         pair_tiles >= st->sm_count / 2) {
         const int units = gemm_units<256, false, 0, true>(st);
@@ -706,9 +752,9 @@ int gemm(const RpfqGemmArgs* a, cudaStream_t stream, RpfqGemmPlan* dry = nullptr
         return fail(RPFQ_ERR_INVALID, "rpfq_gemm_sm100: %d K splits need a workspace of %llu bytes (got %llu)", splits,
                     (unsigned long long)splitk_bytes(a->m, a->n, g.bn, splits), (unsigned long long)a->workspace_bytes);
     if (g.bn == 256)
-        return g.pair ? launch_gemm_bn<256, true>(a, st, stream, 1, g.stream_k, dry)
-                      : launch_gemm_bn<256, false>(a, st, stream, splits, false, dry);
-    return launch_gemm_bn<128, false>(a, st, stream, splits, false, dry);
+        return g.pair ? launch_gemm_bn<256, true>(a, st, stream, 1, g.stream_k, g.narrow, dry)
+                      : launch_gemm_bn<256, false>(a, st, stream, splits, false, false, dry);
+    return launch_gemm_bn<128, false>(a, st, stream, splits, false, false, dry);
 }
 
 // ---------------------------------------------------------------- packed-layer validation

@@ -161,25 +161,45 @@ class PackedViT(nn.Module):
             yield "head_dist", self.head_dist
 
     # ------------------------------------------------------------------ forward
-    def _token_index(self, B: int, device) -> tuple[torch.Tensor, torch.Tensor]:
-        """int32 tables over the B x tokens rows of the residual stream: the
-        source row of each token (class tokens first, then image b's patch
-        embeddings at ntok + b * patches) and its position index. Kept per
-        batch size; built without caching while a CUDA graph is captured (the
-        graph's memory pool must not back a cached tensor)."""
-        key = (B, str(device))
+    def _token_index(self, B: int, device):
+        """Per-batch-size tables and buffers of the forward, kept across calls
+        (built without caching while a CUDA graph is captured: the graph's
+        memory pool must not back a cached tensor):
+
+        * ``rows`` / ``tok``: int32 over the B x tokens rows of the residual
+          stream, the source row of each token (class tokens first, then image
+          b's patch embeddings at ntok + b * patches) and its position index;
+        * ``cls_rows``: int32 over the B x ntok class-token rows of the stream;
+        * ``src``: the fp32 token sources, the class-token rows filled once
+          (the patch GEMM writes the rows below them on every call);
+        * ``pos``: the position table in fp32.
+        Constant per model, so the forward launches no cast or copy kernel
+        (each would also cut the programmatic launch chain). Entries live as
+        long as the model (a CUDA graph captured at one batch size keeps using
+        its entry's buffers while other sizes run); only entries of an older
+        class-token or position table are dropped."""
+        versions = (self.cls_tokens._version, self.pos_embed._version)
+        key = (B, str(device), versions)
         cache = self.__dict__.setdefault("_token_index_cache", {})
         if key in cache:
             return cache[key]
         L, n_p = self.cfg.tokens, (self.cfg.img // self.cfg.patch) ** 2
         ntok = L - n_p
+        d = self.cfg.dim
         t = torch.arange(L, dtype=torch.int32, device=device).repeat(B)
         b = torch.arange(B, dtype=torch.int32, device=device).repeat_interleave(L)
         rows = torch.where(t < ntok, t, ntok + b * n_p + (t - ntok)).to(torch.int32)
+        cls_rows = (torch.arange(B, dtype=torch.int32, device=device).repeat_interleave(ntok) * L +
+                    torch.arange(ntok, dtype=torch.int32, device=device).repeat(B)).to(torch.int32)
+        src = torch.empty((ntok + B * n_p, d), dtype=torch.float32, device=device)
+        src[:ntok].copy_(self.cls_tokens[0])
+        pos = self.pos_embed[0].float().contiguous()
+        entry = (rows, t, cls_rows, src, pos)
         if torch.device(device).type != "cuda" or not torch.cuda.is_current_stream_capturing():
-            cache.clear()
-            cache[key] = (rows, t)
-        return rows, t
+            for k in [k for k in cache if k[2] != versions]:
+                del cache[k]
+            cache[key] = entry
+        return entry
 
     @torch.no_grad()
     def forward(self, images: torch.Tensor) -> torch.Tensor:
@@ -204,15 +224,12 @@ class PackedViT(nn.Module):
         L = cfg.tokens
         # token sources: the class (+ distillation) token rows, then the patch
         # embeddings, which the patch GEMM writes straight below them
-        src = torch.empty((ntok + B * n_p, d), dtype=torch.float32, device=patches.device)
-        src[:ntok].copy_(self.cls_tokens[0])
+        rows, tok, cls_rows, src, pos = self._token_index(B, patches.device)
         ops.gemm(patches, self.patch_w, self.patch_b, out=src[ntok:].view(B, n_p, d))
         # residual stream x = [cls (+ dist), patches] + position embedding
         # (reference forward_runtime_path, audit_rpfq_vit_ios_parity.py:638-645),
         # assembled by the first LayerNorm pass: it gathers each token's source
         # row, adds its position row, writes x and normalizes it
-        rows, tok = self._token_index(B, patches.device)
-        pos = self.pos_embed[0].float()
         x = torch.empty((B, L, d), dtype=torch.float32, device=patches.device)
         for i, blk in enumerate(self.blocks):
             if i == 0:
@@ -229,7 +246,9 @@ class PackedViT(nn.Module):
             blk.proj(a, residual=x, out=x)
             h = ops.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, ab)
             blk.fc2(blk.fc1(h, prequantized=pre), residual=x, out=x)
-        cls = ops.layernorm(x[:, :ntok], self.norm_w, self.norm_b, cfg.eps, ab)
+        # final norm of the class-token rows only (a row gather, no strided copy)
+        cls = ops.layernorm(x, self.norm_w, self.norm_b, cfg.eps, ab, rows=cls_rows,
+                            out=torch.empty((B, ntok, d), dtype=torch.float16, device=x.device))
         logits = self.head(cls[:, 0], out_dtype=torch.float32, prequantized=pre)
         if self.head_dist is not None:
             logits = (logits + self.head_dist(cls[:, 1], out_dtype=torch.float32, prequantized=pre)) / 2

@@ -222,8 +222,9 @@ def test_gemm_split_k_automatic_choice(cuda):
     small = L.rpfq_gemm_workspace_bytes(198, 768, 3072)
     assert 0 < small <= full
     assert L.rpfq_gemm_workspace_bytes(50432, 768, 768) == 0  # 591 pair tiles: last wave 99 % full
-    assert L.rpfq_gemm_workspace_bytes(6304, 768, 3072) == full  # 75 pair tiles, long K: stream-K tail
-    assert L.rpfq_gemm_workspace_bytes(6304, 768, 768) == 0  # short K: whole tiles
+    assert L.rpfq_gemm_workspace_bytes(9728, 768, 4096) == full  # 114 pair tiles, long K: stream-K tail
+    assert L.rpfq_gemm_workspace_bytes(6304, 768, 3072) == 0  # 75 pair tiles: narrow tail, no workspace
+    assert L.rpfq_gemm_workspace_bytes(9728, 768, 768) == 0  # short K: whole tiles
     assert L.rpfq_gemm_workspace_bytes(198, 768, 128) == 0  # two k-blocks: nothing to split
 
 

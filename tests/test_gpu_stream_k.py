@@ -17,17 +17,16 @@ from tests.helpers import rel_err
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
-# (m, n, k, epilogue): shapes whose last wave of pair tiles idles long enough
-# for the tail (rpfq_b200.cu plan_gemm): ViT-B fc2 at 32 and 64 images (m =
-# 6304 / 12608: 75 / 150 pair tiles on 74 pairs), ragged m, a 32-k-block K,
-# fp32 output with K = 4096 and 600 tiles (tail of 82).
+# (m, n, k, epilogue): shapes whose last wave of pair tiles is more than half
+# full (the narrow tail takes the emptier ones) and idles long enough for the
+# tail (rpfq_b200.cu plan_gemm): 114 pair tiles on 74 pairs with K = 4096
+# (idle 0.46 of a 64-k-block wave), ragged m, GELU, and fp32 output over 416
+# tiles.
 CASES = [
-    (6304, 768, 3072, "residual_f32"),
-    (12608, 768, 3072, "residual_f32"),
-    (6301, 768, 3072, "none"),
-    (6304, 1536, 3072, "gelu"),
-    (6304, 768, 2048, "none"),
-    (19000, 2048, 4096, "f32"),
+    (9728, 768, 4096, "residual_f32"),
+    (9700, 768, 4096, "none"),
+    (4864, 1536, 4096, "gelu"),
+    (13312, 2048, 4096, "f32"),
 ]
 
 
@@ -78,12 +77,15 @@ def test_stream_k_tail(cuda, m, n, k, epi):
 
 
 def test_stream_k_only_where_it_pays(cuda):
-    """K = 768 layers at 32 images keep whole tiles (the tail's fixup costs more
-    than their short last wave); without a workspace nothing takes the tail."""
+    """A last wave at most half full takes the narrow tail instead; a short K
+    keeps whole tiles (the tail's fixup costs more than its short wave);
+    without a workspace nothing takes the tail."""
     from rpfq_review_b200 import ops
     for n in (768, 2304, 3072):
-        assert ops.gemm_plan(6304, n, 768, device=cuda)["stream_k_tiles"] == 0
-    assert ops.gemm_plan(6304, 768, 3072, split_k=1, device=cuda)["stream_k_tiles"] == 0
+        plan = ops.gemm_plan(6304, n, 768, device=cuda)
+        assert plan["stream_k_tiles"] == 0 and plan["pieces"] > 0
+    assert ops.gemm_plan(9728, 768, 768, device=cuda)["stream_k_tiles"] == 0  # K = 768
+    assert ops.gemm_plan(9728, 768, 4096, split_k=1, device=cuda)["stream_k_tiles"] == 0
     assert ops.gemm_plan(50432, 768, 3072, device=cuda)["stream_k_tiles"] == 0  # 591 tiles: last wave 99 % full
 
 
@@ -91,9 +93,9 @@ def test_stream_k_in_cuda_graph(cuda):
     """The tail replays from a CUDA graph: the flags are cleared inside every
     replay, so consecutive replays stay bit-identical."""
     from rpfq_review_b200 import ops
-    x, w, b, r = _inputs(6304, 768, 3072, "none", cuda)
-    assert ops.gemm_plan(6304, 768, 3072, device=cuda)["stream_k_tiles"] > 0
-    out = torch.empty(6304, 768, dtype=torch.float16, device=cuda)
+    x, w, b, r = _inputs(9728, 768, 4096, "none", cuda)
+    assert ops.gemm_plan(9728, 768, 4096, device=cuda)["stream_k_tiles"] > 0
+    out = torch.empty(9728, 768, dtype=torch.float16, device=cuda)
     ref = ops.gemm(x, w, b).clone()
     side = torch.cuda.Stream(cuda)
     side.wait_stream(torch.cuda.current_stream(cuda))
