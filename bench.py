@@ -103,6 +103,9 @@ def parse():
                     help="--gemm: the fused decode path (packed planes only, M <= 256), rotating over enough "
                          "layer copies that the packed weights stream from HBM")
     ap.add_argument("--gemm-breakdown", action="store_true", help="print per-GEMM event times (stderr)")
+    ap.add_argument("--vs-cublas", action="store_true",
+                    help="the four ViT-B layer GEMMs at 256 and 32 images: the library's fused GEMM against cuBLAS "
+                         "addmm + torch's separate GELU / residual add")
     ap.add_argument("--weights", default="random_init", choices=["random_init", "synthetic"],
                     help="model weights: exporter packing of random init, or synthetic codes + lognormal scales")
     ap.add_argument("--code-bits", type=int, default=2, help="phase code width b (3, 4 need --weights synthetic)")
@@ -1107,6 +1110,67 @@ def run_wattn(args):
     return 0
 
 
+def run_vs_cublas(args):
+    """--vs-cublas: the four ViT-B/16 layer GEMMs at 256 and 32 images (m =
+    50432, 6304) through the library's fused GEMM and through cuBLAS as the
+    reference's PyTorch path runs them (fp16 addmm, then torch's GELU or
+    residual add as separate kernels); CUDA events over one graph of --steps
+    launches alternating two input sets, best of three replays."""
+    import torch
+
+    from rpfq_review_b200 import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    out = {"metric": "ViT-B layer GEMM us per launch, library vs cuBLAS + torch epilogue"}
+    for m in (50432, 6304):
+        for name, n, k, epi in (("qkv", 2304, 768, "none"), ("proj", 768, 768, "res"), ("fc1", 3072, 768, "gelu"),
+                                ("fc2", 768, 3072, "res")):
+            g = torch.Generator(device=dev).manual_seed(1)
+            xs = [torch.randn(m, k, device=dev, generator=g).half() for _ in range(2)]
+            w = (torch.randn(n, k, device=dev, generator=g) / k ** 0.5).half()
+            b = torch.randn(n, device=dev, generator=g).half()
+            b32 = b.float()
+            rs = [torch.randn(m, n, device=dev, generator=g) for _ in range(2)]
+            ys = [torch.empty(m, n, device=dev, dtype=torch.float16) for _ in range(2)]
+
+            def ours(i):
+                if epi == "res":
+                    ops.gemm(xs[i & 1], w, b32, residual=rs[i & 1], out=rs[i & 1])
+                else:
+                    ops.gemm(xs[i & 1], w, b32, activation="gelu" if epi == "gelu" else "none", out=ys[i & 1])
+
+            def cublas(i):
+                y = torch.addmm(b, xs[i & 1], w.t())
+                if epi == "gelu":
+                    y = torch.nn.functional.gelu(y)
+                if epi == "res":
+                    rs[i & 1].add_(y)
+
+            for tag, fn in (("ours", ours), ("cublas", cublas)):
+                s_ = torch.cuda.Stream(dev)
+                with torch.cuda.stream(s_):
+                    for i in range(3):
+                        fn(i)
+                    torch.cuda.synchronize(dev)
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=s_):
+                        for i in range(args.steps):
+                            fn(i)
+                    gr.replay()
+                    torch.cuda.synchronize(dev)
+                    best = float("inf")
+                    for _ in range(3):
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(s_)
+                        gr.replay()
+                        e1.record(s_)
+                        torch.cuda.synchronize(dev)
+                        best = min(best, e0.elapsed_time(e1) * 1000 / args.steps)
+                out[f"{name}_m{m}_{tag}_us"] = best
+    print(json.dumps(out))
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1127,6 +1191,8 @@ def main():
                 args.gemm, args.epilogue, args.split_k = shape, epi, split
                 run_gemm(args)
         return 0
+    if args.vs_cublas:
+        return run_vs_cublas(args)
     if args.gemm:
         return run_gemm(args)
     if args.attn:

@@ -654,17 +654,21 @@ GemmPlan plan_gemm(int64_t m, int n, int k, int block_n, int cta_pair, int split
     // 0.5 us, so the tail is taken only when the idle part of the last wave is at
     // least 24 k-blocks long (ViT-B fc2 at 32 images: 0.99 x 48; qkv, fc1 and proj
     // with K = 768 lose).
+    // The tails below force 256-wide pair tiles, so they apply only when n
+    // fills such tiles (Swin's 96- to 576-column layers keep the width chosen by
+    // pick_block_n: forcing 256 there cost 6 % of the Swin-T step).
+    const bool full_width = n % 256 == 0;
     // A last wave at most half full: CTA pairs with the narrow tail (the last
     // wave's tiles cut into column pieces), which needs no workspace.
-    if (narrow_tail_enabled() && block_n == 0 && cta_pair == 0 && split_k <= 1 && pair_tiles >= st->sm_count / 2 &&
-        narrow_pieces(pair_tiles, gemm_units<256, false, 0, true>(st)) > 0) {
+    if (full_width && narrow_tail_enabled() && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
+        pair_tiles >= st->sm_count / 2 && narrow_pieces(pair_tiles, gemm_units<256, false, 0, true>(st)) > 0) {
         g.bn = 256;
         g.pair = true;
         g.splits = 1;
         g.narrow = true;
         return g;
     }
-    if (sk_ws && stream_k_mode() > 0 && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
+    if (full_width && sk_ws && stream_k_mode() > 0 && block_n == 0 && cta_pair == 0 && split_k <= 1 &&
         pair_tiles >= st->sm_count / 2) {
         const int units = gemm_units<256, false, 0, true>(st);
         const int num_k = (k + 63) / 64;

@@ -63,3 +63,13 @@ def test_narrow_tail(cuda, m, n, k, epi, pieces):
     assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < TOL
     assert torch.equal(y, y_whole), "narrow tail and whole tiles differ"
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(401408, 384, 96), (401408, 288, 96), (100352, 576, 192)])
+def test_partial_width_keeps_block_n_picker(cuda, m, n, k):
+    """Swin-T stage-1/2 layers (n not a multiple of 256) whose pair tiles would
+    leave a short last wave keep the tile width of the wave model: 256-wide
+    tiles over 288 or 384 columns waste a quarter or more of every tile."""
+    from rpfq_review_b200 import ops
+    plan = ops.gemm_plan(m, n, k, device=cuda)
+    assert plan["pieces"] == 0 and plan["stream_k_tiles"] == 0, plan
