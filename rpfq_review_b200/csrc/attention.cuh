@@ -17,8 +17,9 @@
 //               O_g = P_g V     M=128, N=64, K=lk   -> TMEM cols [256 g + 128, 256 g + 192)
 //             (P_g is the TMEM A operand; V the B operand in its natural
 //             [key][dim] layout: MN-major)
-//   warps 2-9 group g = query tile g, one query row per thread: row max over
-//             the valid keys, p = 2^((s - max) c) (SFU ex2), row sum of the
+//   warps 2-9 group g = query tile g, one query row per thread, one pass over
+//             S: p = 2^((s - m) c) (SFU ex2) against a reference m raised only
+//             when a chunk of keys exceeds it by 2^12, row sum of the
 //             fp16-rounded p, P as packed fp16 over the first lk/2 columns of
 //             S_g, then O_g / sum to global.
 // Every wait is bounded (wait_bar) and reports through the device error word.
@@ -206,44 +207,74 @@ __global__ void __launch_bounds__(320, 1)
             tc_fence_after();
             float inv_sum = 0.0f;
             if (warp_live) {
-                // pass 1: row max over the valid keys (two TMEM chunks per wait, eight
-                // independent running maxima)
-                float m8[8];
+                // One pass over S, 32 keys per TMEM load. The weights are taken
+                // relative to a reference m (p = 2^((s - m) c)) that starts at the
+                // first chunk's maximum and is raised only when a later chunk
+                // exceeds it by more than 2^kLazyLog2 (p then stays <= 4096, well
+                // inside fp16): softmax is invariant to m, and fp16's relative
+                // rounding does not depend on the scale. When a lane's m is raised
+                // the warp rescales the P chunks already written (rare: never for
+                // keys whose scaled logits stay within 8.3 of the first chunk's).
+                constexpr float kLazyLog2 = 12.0f;
+                const float lazy = kLazyLog2 / p.scale_log2;  // the same bound on raw S
+                float m_run = -INFINITY;
+                uint64_t m2 = f2_pack(INFINITY, INFINITY);
+                float s8[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
-                for (int c0 = 0; c0 < nchunk; c0 += 2) {
-                    uint32_t r[2][32];
-                    tmem_ld_32x32b_x32(t_row + 32 * c0, r[0]);
-                    if (c0 + 1 < nchunk) tmem_ld_32x32b_x32(t_row + 32 * (c0 + 1), r[1]);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int c = c0 + j;
-                        if (c >= nchunk) break;
-                        if (32 * c + 32 <= p.L) {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(r[j][e]));
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e)
-                                if (32 * c + e < p.L) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(r[j][e]));
-                        }
-                    }
-                }
-                const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-                const float nmx = -mx * p.scale_log2;
-                const uint64_t m2 = f2_pack(nmx, nmx);
-                // pass 2: p = 2^(s c - max c) (fp32x2 fma, ex2 on the SFU), packed as fp16
-                // pairs over the first columns of S (chunk c -> columns 16 c .. 16 c + 15, all
-                // of whose S values this thread has already read); the row sum adds the
-                // fp16-rounded weights the MMA sees
-                float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int u = 0; u < 8; ++u) s8[u] = 0.0f;
                 for (int c = 0; c < nchunk; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + 32 * c, r);
                     tmem_ld_wait();
                     const bool full = 32 * c + 32 <= p.L;
+                    float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    if (full) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2)
+                            cm[(e >> 1) & 3] = fmax3(cm[(e >> 1) & 3], __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const float v0 = 32 * c + e < p.L ? __uint_as_float(r[e]) : -INFINITY;
+                            const float v1 = 32 * c + e + 1 < p.L ? __uint_as_float(r[e + 1]) : -INFINITY;
+                            cm[(e >> 1) & 3] = fmax3(cm[(e >> 1) & 3], v0, v1);
+                        }
+                    }
+                    const float cmax = fmaxf(fmax3(cm[0], cm[1], cm[2]), cm[3]);
+                    const bool raise = cmax > m_run + lazy;  // always for chunk 0
+                    if (__any_sync(0xffffffffu, raise)) {
+                        const float m_new = raise ? cmax : m_run;
+                        if (c > 0) {
+                            // P of chunks 0 .. c-1 (columns 0 .. 16 c - 1) times
+                            // 2^((m_run - m_new) c), re-rounded to fp16; the row sum
+                            // is rebuilt from the re-rounded weights
+                            const float f = raise ? ex2_approx((m_run - m_new) * p.scale_log2) : 1.0f;
+                            tmem_st_wait();
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) s8[u] = 0.0f;
+                            for (int cc = 0; cc < c; ++cc) {
+                                uint32_t pw[16];
+                                tmem_ld_32x32b_x16(t_row + 16 * cc, pw);
+                                tmem_ld_wait();
+#pragma unroll
+                                for (int u = 0; u < 16; ++u) {
+                                    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&pw[u]));
+                                    const __half2 hh = __floats2half2_rn(v.x * f, v.y * f);
+                                    s8[2 * (u & 3)] = add_f32_f16(__low2half(hh), s8[2 * (u & 3)]);
+                                    s8[2 * (u & 3) + 1] = add_f32_f16(__high2half(hh), s8[2 * (u & 3) + 1]);
+                                    pw[u] = *reinterpret_cast<const uint32_t*>(&hh);
+                                }
+                                tmem_st_32x32b_x16(t_row + 16 * cc, pw);
+                            }
+                        }
+                        m_run = m_new;
+                        const float nm = -m_run * p.scale_log2;
+                        m2 = f2_pack(nm, nm);
+                    }
+                    // p = 2^(s c - m c) (fp32x2 fma, ex2 on the SFU), packed as fp16 pairs
+                    // over the first columns of S (chunk c -> columns 16 c .. 16 c + 15,
+                    // all of whose S values this thread has already read); the row sum
+                    // adds the fp16-rounded weights the MMA sees
                     uint32_t pw[16];
 #pragma unroll
                     for (int u = 0; u < 16; ++u) {
@@ -257,25 +288,32 @@ __global__ void __launch_bounds__(320, 1)
                             if (32 * c + e + 1 >= p.L) a1 = 0.0f;
                         }
                         const __half2 hh = __floats2half2_rn(a0, a1);
-                        const float2 f = __half22float2(hh);
-                        s4[u & 3] += f.x + f.y;
+                        s8[2 * (u & 3)] = add_f32_f16(__low2half(hh), s8[2 * (u & 3)]);
+                        s8[2 * (u & 3) + 1] = add_f32_f16(__high2half(hh), s8[2 * (u & 3) + 1]);
                         pw[u] = *reinterpret_cast<const uint32_t*>(&hh);
                     }
                     tmem_st_32x32b_x16(t_row + 16 * c, pw);
                 }
                 tmem_st_wait();
-                inv_sum = 1.0f / ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+                inv_sum = 1.0f / (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
             }
             tc_fence_before();  // P is in TMEM; O will land next to it
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[g]);
             if (!wait_bar(&o_full[g], k & 1, abort_flag, p.err, 818)) break;
             tc_fence_after();
+            uint32_t r0[32], r1[32];
             if (warp_live) {
-                uint32_t r0[32], r1[32];
                 tmem_ld_32x32b_x32(t_row + C::O_COL, r0);
                 tmem_ld_32x32b_x32(t_row + C::O_COL + 32, r1);
                 tmem_ld_wait();
+            }
+            // O is in registers: the tile's TMEM may take the next item's S now,
+            // while this item's output is scaled and stored
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_free[g]);
+            if (warp_live) {
                 if (l < p.L) {
                     __half* orow = p.out + (static_cast<int64_t>(b) * p.L + l) * p.ldo + h * C::HD;
 #pragma unroll
@@ -292,9 +330,6 @@ __global__ void __launch_bounds__(320, 1)
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_free[g]);
         }
     }
     tc_fence_before();

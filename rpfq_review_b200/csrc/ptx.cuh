@@ -235,6 +235,18 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+// float(h) + c in one mixed-precision add (sm_100): exact widening, one fp32 rounding.
+__device__ __forceinline__ float add_f32_f16(__half h, float c) {
+    float r;
+    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(r) : "h"(__half_as_ushort(h)), "f"(c));
+    return r;
+}
 __device__ __forceinline__ float rcp_approx(float x) {
     float r;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));

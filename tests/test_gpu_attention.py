@@ -49,3 +49,29 @@ def test_attention_strided_output_and_errors(cuda):
     from rpfq_review_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("L,H,plants", [(197, 2, ((150, 8.0),)), (197, 3, ((40, 4.0), (170, 8.0))),
+                                        (256, 1, ((100, 1.1), (230, 1.25))), (129, 2, ((128, 6.0),))])
+def test_attention_raised_reference(cuda, L, H, plants):
+    """Keys after the first chunk of 32 whose logits exceed that chunk's by far
+    more than the one-pass softmax's 2^12 margin, for half of the query rows
+    (q = +u + noise) and not for the other half (q = -u + noise): the rows that
+    raise their reference rescale the weights already written, the others keep
+    theirs, within one warp. plants: (key, a) sets k[key] = a u for every head."""
+    from rpfq_review_b200 import ops
+    g = torch.Generator().manual_seed(L * 7 + H)
+    B, d = 2, 64 * H
+    u = torch.where(torch.rand(64, generator=g) < 0.5, -1.0, 1.0)
+    sign = torch.where(torch.arange(L) % 2 == 0, 1.0, -1.0)
+    x = torch.randn(B, L, 3, H, 64, generator=g) * 0.7
+    x[:, :, 0] += sign.view(1, L, 1, 1) * u
+    for key, a in plants:
+        x[:, key, 1] = a * u
+    qkv = x.reshape(B, L, 3 * d).half()
+    out = ops.attention(qkv.to(cuda), H)
+    ref = _ref(qkv, H)
+    assert rel_err(out.cpu().numpy(), ref.numpy()) <= 3e-3
+    from rpfq_review_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
