@@ -84,8 +84,9 @@ def parse():
     ap.add_argument("--cta-pair", type=int, default=0, help="--gemm: 0 automatic, 1 one CTA per tile, 2 CTA pairs")
     ap.add_argument("--no-bias", action="store_true", help="--gemm: run the epilogue without the bias add")
     ap.add_argument("--cpu-layer", action="store_true",
-                    help="--gemm: also time the same layer on the host cores (the reference's C++ fp16-cache runtime "
-                         "and torch F.linear on the dense fp32 weight) and through the C ABI with host buffers "
+                    help="--gemm: also time the same layer on the host cores (the reference's C++ fp16-cache runtime, "
+                         "its PyTorch QAT forward and torch F.linear on the dense fp32 weight) and through the C ABI "
+                         "with host buffers "
                          "(configs[0]: 1576,768,768)")
     ap.add_argument("--split-k", type=int, default=None,
                     help="--gemm: K splits per tile (0 automatic, 1 never, 2..8 forced; default: the library's)")
@@ -890,7 +891,9 @@ def layer_cpu_legs(args, layer, mod, x_dev, y_dev, step):
     the reference's own C++ fp16-cache runtime (oracle/_ref, all host threads,
     when built), torch F.linear on the export-dequantized fp32 weight (all
     host threads: the dense contraction of the reference's PyTorch path,
-    without its per-call weight quantization), and the GPU layer end to end
+    without its per-call weight quantization), the reference's PyTorch layer
+    forward with that quantization (act-quant off and 4-bit), and the GPU
+    layer end to end
     through the public call with host buffers (pinned upload of x, the layer,
     download of y, timed with CUDA events). Each leg runs for about a second."""
     import numpy as np
@@ -924,6 +927,14 @@ def layer_cpu_legs(args, layer, mod, x_dev, y_dev, step):
     w = torch.from_numpy(pr.dense_weight_from_packed(np_layer, n_c, k_c))
     b = torch.from_numpy(np_layer["bias"].astype(np.float32))
     out["torch_cpu_dense_fp32_us"] = timed(lambda: F.linear(x_cpu, w, b))
+    # the reference's PyTorch layer itself (QATLinearComplexPhase.forward,
+    # restated in oracle/qat_ref.py): the float weight is re-quantized on every
+    # call, then F.linear; here the float weight is the dequantized one, so
+    # the quantizer reproduces it
+    from oracle import qat_ref
+    w_np, b_np, x_np = w.numpy(), b.numpy(), x_cpu.numpy()
+    for bits in (0, 4):
+        out[f"reference_qat_forward_act{bits}_us"] = timed(lambda: qat_ref.forward(w_np, b_np, x_np, act_bits=bits))
     # the GPU layer with host buffers: pinned x up, layer, y down
     x_host = x_dev.cpu().pin_memory()
     y_host = torch.empty(y_dev.shape, dtype=y_dev.dtype).pin_memory()
