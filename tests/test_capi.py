@@ -101,7 +101,7 @@ def test_torch_ops_registered():
     # CUDA-only: a CPU call fails in the dispatcher instead of falling back
     with pytest.raises(Exception):
         torch.ops.rpfq.act_quant(torch.zeros(2, 8, dtype=torch.float16), 4)
-    # the packed-layer op takes the reference's packed tensors (SURVEY contract schema)
+    # the packed-layer op takes the reference's packed tensors (codes, gammas, bias, n_c, k_c, act_bits, gelu)
     schema = str(torch.ops.rpfq.wide_linear.default._schema)
     assert ("wide_linear(Tensor x, Tensor[] codes, Tensor[] gamma_re, Tensor[] gamma_im, Tensor? bias, int n_c, "
             "int k_c, int act_bits=0, bool gelu=False) -> Tensor") in schema
