@@ -8,14 +8,26 @@
 //   act_bits > 0:  per Re / Im half of h: s = fl(fl(1 / max(amax, 1e-5)) * qmax),
 //                  h' = fl(clamp(rint(fl(h * s)), qmin, qmax) / s)
 //
-// Loads: VW = 4, 2 or 1 consecutive floats per lane and step (by row length).
+// Layout: G lanes per row (a warp takes 32 / G rows), VW = 4, 2 or 1
+// consecutive floats per lane and step (by row length).
 #pragma once
 
 #include "ptx.cuh"
 
 namespace rpfq {
 
-constexpr int kLnQtab = 264;  // quotient table slots per half: 2^8 values of q, -0, padding
+// Lanes per row: Swin's 96- and 192-wide rows get 8 / 16 lanes (three 16-byte
+// loads per lane, a 3- / 4-level shuffle reduction; a warp takes 4 / 2 rows),
+// every other row length a whole warp. The layout depends on the row length
+// only, so every variant of a given length (plain, gathered, fused quantizer)
+// sums in the same order and their outputs agree bit for bit.
+__host__ __device__ constexpr int ln_lanes_per_row(int d) { return d == 96 ? 8 : (d == 192 ? 16 : 32); }
+
+// Dynamic shared memory of the fused quantizer: per row of a block, both
+// halves' tables of fl(q / s) for the 2^act_bits values of q and -0.
+__host__ __device__ constexpr int ln_qtab_floats(int d, int warps, int act_bits) {
+    return warps * (32 / ln_lanes_per_row(d)) * 2 * ((1 << act_bits) + 1);
+}
 
 struct LayerNormParams {
     const float* x;       // [x_rows, ldx] fp32
@@ -72,28 +84,37 @@ __device__ __forceinline__ void load_row_part(const float* p, float (&v)[VW]) {
 template <int D, bool PLAIN, bool QUANT>
 __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormParams p) {
     static_assert(D % 32 == 0, "row length must be a multiple of 32");
-    // VW consecutive floats per lane and step: element e of step j of lane l
-    // sits at column 32 VW j + VW l + e (coalesced, 16-/8-/4-byte loads)
-    constexpr int VW = D % 128 == 0 ? 4 : (D % 64 == 0 ? 2 : 1);
-    constexpr int J = D / (32 * VW);
+    constexpr int G = ln_lanes_per_row(D);
+    constexpr int R = 32 / G;  // rows per warp
+    // VW consecutive floats per lane and step: element e of step j of lane l of
+    // a row group sits at column G VW j + VW l + e (coalesced, 16-/8-/4-byte loads)
+    constexpr int VW = G < 32 ? 4 : (D % 128 == 0 ? 4 : (D % 64 == 0 ? 2 : 1));
+    constexpr int J = D / (G * VW);
+    static_assert(J * G * VW == D, "row layout");
     const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rg = lane / G;  // this lane's row within the warp
+    const int sl = lane % G;  // this lane within its row
     // Rows are taken last to first: the GEMM that wrote x finished with its
     // highest row blocks, which are the ones still in L2, and the GEMM that
     // reads y starts with the lowest rows, the ones written last here.
-    // per warp: the activation quantizer's fl(q / s), see below (dynamic shared
-    // memory, present only when act_bits > 0)
-    extern __shared__ float ln_qtab[];
-    float(*qtab)[kLnQtab] = reinterpret_cast<float(*)[kLnQtab]>(ln_qtab + (threadIdx.x >> 5) * 2 * kLnQtab);
-    const int64_t slot = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
+    const int64_t slot = (static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5)) * R + rg;
     const int64_t row = p.m - 1 - slot;
-    const int lane = threadIdx.x & 31;
+    // per row: the activation quantizer's fl(q / s) for both halves, see below
+    // (dynamic shared memory, present only when act_bits > 0)
+    extern __shared__ float ln_qtab[];
+    const int qstride = (1 << p.act_bits) + 1;
+    float* qtab_re = ln_qtab + (static_cast<int>(threadIdx.x >> 5) * R + rg) * 2 * qstride;
+    float* qtab_im = qtab_re + qstride;
     pdl_wait();
     pdl_launch_dependents();
-    if (slot >= p.m) return;
+    // a row group past the last row stays in the warp's shuffles without touching memory
+    bool live = slot < p.m;
+    if (!__any_sync(0xffffffffu, live)) return;
     // source row of each quarter of the output row (all four equal unless merging)
     int64_t src[4] = {row, row, row, row};
     const float* ar = nullptr;
-    if constexpr (!PLAIN) {
+    if (!PLAIN && live) {
         if (p.merge_side > 0) {
             const int64_t half = p.merge_side >> 1;
             const int64_t img = row / (half * half), t = row - img * half * half;
@@ -108,19 +129,21 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
             if (p.rows != nullptr) {
                 s0 = p.rows[row];
                 if (s0 < 0 || s0 >= p.x_rows) {  // bad gather index: report, touch nothing
-                    if (lane == 0) atomicCAS(p.err, 0, 901);
-                    return;
+                    if (sl == 0) atomicCAS(p.err, 0, 901);
+                    live = false;
+                    s0 = 0;
                 }
             }
             src[0] = src[1] = src[2] = src[3] = s0;
         }
-        if (p.add != nullptr) {
+        if (live && p.add != nullptr) {
             const int64_t a = p.add_rows != nullptr ? p.add_rows[row] : row;
             if (a < 0 || a >= p.add_bound) {
-                if (lane == 0) atomicCAS(p.err, 0, 902);
-                return;
+                if (sl == 0) atomicCAS(p.err, 0, 902);
+                live = false;
+            } else {
+                ar = p.add + a * p.ld_add;
             }
-            ar = p.add + a * p.ld_add;
         }
     }
     // every load of the row is issued before the first use (x, then the add
@@ -128,16 +151,21 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     float v[J][VW];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-        const int col = 32 * VW * j + VW * lane;
+        const int col = G * VW * j + VW * sl;
         const int q = col / (D / 4);  // quarter (VW divides D / 4 whenever merging is allowed)
         const int64_t sq = PLAIN ? row : (q == 0 ? src[0] : (q == 1 ? src[1] : (q == 2 ? src[2] : src[3])));
         const float* xr = p.x + sq * p.ldx + (!PLAIN && p.merge_side > 0 ? col - q * (D / 4) : col);
-        load_row_part<VW>(xr, v[j]);
+        if (live) {
+            load_row_part<VW>(xr, v[j]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) v[j][e] = 0.0f;
+        }
     }
     if (!PLAIN && ar != nullptr) {
         float u[J][VW];
 #pragma unroll
-        for (int j = 0; j < J; ++j) load_row_part<VW>(ar + 32 * VW * j + VW * lane, u[j]);
+        for (int j = 0; j < J; ++j) load_row_part<VW>(ar + G * VW * j + VW * sl, u[j]);
 #pragma unroll
         for (int j = 0; j < J; ++j)
 #pragma unroll
@@ -153,12 +181,12 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
         else
             sum += v[j][0];
     }
-    if (!PLAIN && p.y32 != nullptr && p.y32_prenorm) {
-        // the updated residual row (in place when y32 == x: this warp has read its whole row)
+    if (!PLAIN && live && p.y32 != nullptr && p.y32_prenorm) {
+        // the updated residual row (in place when y32 == x: these lanes have read their whole row)
         float* zr = p.y32 + row * p.ldy32;
 #pragma unroll
         for (int j = 0; j < J; ++j) {
-            const int col = 32 * VW * j + VW * lane;
+            const int col = G * VW * j + VW * sl;
             if constexpr (VW == 4)
                 *reinterpret_cast<float4*>(zr + col) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
             else if constexpr (VW == 2)
@@ -168,7 +196,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
         }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int o = G / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float mean = sum / static_cast<float>(D);
     float sq = 0.0f;
 #pragma unroll
@@ -179,12 +207,12 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
             sq += dlt * dlt;
         }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    for (int o = G / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     const float rstd = rsqrtf(sq / static_cast<float>(D) + p.eps);
     float amax_re = 0.0f, amax_im = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-        const int col = 32 * VW * j + VW * lane;
+        const int col = G * VW * j + VW * sl;
         float wf[VW], bf[VW];
         if constexpr (VW == 4) {
             const uint2 wv = *reinterpret_cast<const uint2*>(p.w + col);
@@ -212,11 +240,11 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
                 amax_im = fmaxf(amax_im, a);
         }
     }
-    if (!PLAIN && p.y32 != nullptr && !p.y32_prenorm) {
+    if (!PLAIN && live && p.y32 != nullptr && !p.y32_prenorm) {
         float* zr = p.y32 + row * p.ldy32;
 #pragma unroll
         for (int j = 0; j < J; ++j) {
-            const int col = 32 * VW * j + VW * lane;
+            const int col = G * VW * j + VW * sl;
             if constexpr (VW == 4)
                 *reinterpret_cast<float4*>(zr + col) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
             else if constexpr (VW == 2)
@@ -229,7 +257,7 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
     float s_re = 0.0f, s_im = 0.0f, qmax = 0.0f, qmin = 0.0f;
     if (QUANT) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
+        for (int o = G / 2; o > 0; o >>= 1) {
             amax_re = fmaxf(amax_re, __shfl_xor_sync(0xffffffffu, amax_re, o));
             amax_im = fmaxf(amax_im, __shfl_xor_sync(0xffffffffu, amax_im, o));
         }
@@ -239,23 +267,24 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
         s_re = __fmul_rn(__frcp_rn(fmaxf(__half2float(__float2half_rn(amax_re)), 1e-5f)), qmax);
         s_im = __fmul_rn(__frcp_rn(fmaxf(__half2float(__float2half_rn(amax_im)), 1e-5f)), qmax);
         // q takes the 2^act_bits integers in [qmin, qmax] and -0 (rint of a small
-        // negative h): the warp divides each once (IEEE, as per element) into its
-        // table, slot 2^act_bits holding fl(-0 / s)
+        // negative h): the row's lanes divide each once (IEEE, as per element) into
+        // its table, slot 2^act_bits holding fl(-0 / s)
         const int nq = 1 << p.act_bits;
-        for (int t = lane; t < nq; t += 32) {
-            qtab[0][t] = __fdiv_rn(qmin + static_cast<float>(t), s_re);
-            qtab[1][t] = __fdiv_rn(qmin + static_cast<float>(t), s_im);
+        for (int t = sl; t < nq; t += G) {
+            qtab_re[t] = __fdiv_rn(qmin + static_cast<float>(t), s_re);
+            qtab_im[t] = __fdiv_rn(qmin + static_cast<float>(t), s_im);
         }
-        if (lane == 0) {
-            qtab[0][nq] = __fdiv_rn(-0.0f, s_re);
-            qtab[1][nq] = __fdiv_rn(-0.0f, s_im);
+        if (sl == 0) {
+            qtab_re[nq] = __fdiv_rn(-0.0f, s_re);
+            qtab_im[nq] = __fdiv_rn(-0.0f, s_im);
         }
         __syncwarp();
     }
+    if (!live) return;
     __half* yr = p.y + row * p.ldy;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-        const int col = 32 * VW * j + VW * lane;
+        const int col = G * VW * j + VW * sl;
         float o[VW];
 #pragma unroll
         for (int e = 0; e < VW; ++e) {
@@ -264,8 +293,8 @@ __global__ void __launch_bounds__(256) layernorm_f32_f16_kernel(const LayerNormP
                 const float s = (col + e < D / 2) ? s_re : s_im;
                 const float h = __half2float(__float2half_rn(o[e]));
                 const float q = fminf(fmaxf(rintf(__fmul_rn(h, s)), qmin), qmax);
-                o[e] = qtab[(col + e < D / 2) ? 0 : 1][__float_as_uint(q) == 0x80000000u ? (1 << p.act_bits)
-                                                                                     : static_cast<int>(q - qmin)];
+                const float* tab = (col + e < D / 2) ? qtab_re : qtab_im;
+                o[e] = tab[__float_as_uint(q) == 0x80000000u ? (1 << p.act_bits) : static_cast<int>(q - qmin)];
             }
         }
         if constexpr (VW == 4) {

@@ -1041,14 +1041,15 @@ int rpfq_layernorm_ex_sm100(const RpfqLayerNormArgs* a, rpfq_stream_t stream) {
     p.merge_side = a->merge_side;
     p.err = st->err_word;
     const int warps = 8;
-    const int64_t blocks = (m + warps - 1) / warps;
+    const int64_t rows_per_block = static_cast<int64_t>(warps) * (32 / ln_lanes_per_row(d));
+    const int64_t blocks = (m + rows_per_block - 1) / rows_per_block;
     if (blocks > 0x7fffffff) return fail(RPFQ_ERR_UNSUPPORTED, "rpfq_layernorm_sm100: m too large");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned nb = static_cast<unsigned>(blocks);
     const bool plain = !a->rows && !a->add && !a->merge_side && !a->y32;
-    // the fused quantizer's per-warp quotient tables (dynamic shared memory)
+    // the fused quantizer's per-row quotient tables (dynamic shared memory)
     const bool quant = a->act_bits > 0;
-    const size_t qtab = quant ? static_cast<size_t>(warps) * 2 * kLnQtab * sizeof(float) : 0;
+    const size_t qtab = quant ? static_cast<size_t>(ln_qtab_floats(d, warps, a->act_bits)) * sizeof(float) : 0;
     switch (d) {
 #define RPFQ_LN_LAUNCH(D, PL, Q) launch_kernel(layernorm_f32_f16_kernel<D, PL, Q>, dim3(nb), dim3(warps * 32), qtab, s, 1, p)
 #define RPFQ_LN_CASE(D)                                                                                            \

@@ -232,9 +232,11 @@ def test_gemm_split_k_automatic_choice(cuda):
 @pytest.mark.parametrize("act_bits", [0, 4])
 def test_layernorm_kernel(cuda, d, act_bits):
     """fp32 -> fp16 LayerNorm vs torch (fp16 rounding), and the fused
-    act-quant equals LN followed by the act-quant kernel, bit for bit."""
+    act-quant equals LN followed by the act-quant kernel, bit for bit. m = 1003
+    leaves the last warp of the 96- / 192-wide layouts (4 / 2 rows per warp)
+    partly empty."""
     g = torch.Generator().manual_seed(d)
-    m = 1000
+    m = 1003
     x = (torch.randn(m, d, generator=g) * 4 + 1).to(cuda)
     w = (torch.randn(d, generator=g) * 0.2 + 1).half().to(cuda)
     b = (torch.randn(d, generator=g) * 0.1).half().to(cuda)
@@ -428,6 +430,10 @@ def test_layernorm_row_gather(cuda):
     torch.cuda.synchronize()
     assert _lib.device_error() == 901
     assert torch.count_nonzero(out[10]) == 0
+    # the rows that share a warp with the bad one (four 96-wide rows per warp) are written as usual
+    full0 = ops.layernorm(x, w, b, 1e-5)
+    keep = torch.arange(m, device=cuda) != 10
+    assert torch.equal(out[keep], full0[perm.long()][keep])
 
 
 @pytest.mark.parametrize("c,side,act_bits", [(96, 56, 0), (192, 28, 4), (384, 14, 0)])
