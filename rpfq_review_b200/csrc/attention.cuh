@@ -1,6 +1,7 @@
 // Short-sequence multi-head attention on tcgen05 for the ViT / DeiT token
 // counts (L <= 256 keys, head dim 64): softmax(Q K^T / sqrt(64)) V per
-// (image, head), all keys in one tile, so no online rescaling.
+// (image, head), all keys in one tile, so O is never rescaled (only the
+// weights already written, in the rare case described at the softmax).
 //
 // Input: the qkv GEMM output [B, L, 3 d] (fp16; per token q heads, k heads, v
 // heads, 64 columns each), read through a 3-D tensor map [B][L][3 d] so that
