@@ -26,8 +26,10 @@
 //        per row: tcgen05.ld, bias, GELU, residual, pack, 128-B-swizzled smem
 //        staging, TMA store of a [32 rows x 128 B] box. The residual step is
 //        TMA-loaded into the warp's staging slot one step ahead (two slots
-//        per warp) and the output is written over it; WG0 warp 2 prefetches
-//        each tile's residual into L2 two tiles ahead.
+//        per warp) and the output is written over it. (An L2 prefetch of each
+//        tile's residual two tiles ahead was measured: its lines were evicted
+//        before use, so the residual came from DRAM twice — fc2 633 against
+//        482 MB read, proj + 8 % time — and it was taken out.)
 // Register split: 128 x 40 + 256 x 232 = 64512 = 384 threads x 168 at launch.
 //
 // Split-K (one CTA per tile, p.splits > 1; small M, where the tiles alone
@@ -615,35 +617,6 @@ __global__ void __launch_bounds__(384, 1)
                 umma_commit(drain_bar);
             volatile int no_abort = 0;
             wait_bar(drain_bar, 0, &no_abort, p.err, 203);
-        } else if (warp == 2 && lane == 0 && use_res) {
-            // -------------------------------------------------------- residual prefetcher
-            // The residual of this CTA's tile i+2 is prefetched into L2 (one TMA
-            // box per column half) when tile i's accumulator is complete, i.e.
-            // about two main loops before the epilogue reads it.
-            constexpr int PCW = OUT_F32 ? 32 : 64;  // residual box: 32 rows x 128 B
-            auto prefetch_item = [&](const WorkItem& it) {
-                if (it.mode == kItemHead) return;  // no epilogue output
-                const int t = it.tile;
-                const int r0 = (t / num_n) * C::TILE_M + static_cast<int>(rank) * C::BM;
-                const int c0 = (t % num_n) * BN + it.n_off;
-                for (int c = c0; c < c0 + it.width && c < p.n; c += PCW)
-                    for (int r = r0; r < r0 + C::BM && r < p.m; r += 32) tma_prefetch_l2_2d(&tm_r, c, r);
-            };
-            auto lead = schedule();  // two items ahead of the accumulators
-            WorkItem wl;
-            for (int i = 0; i < 2 && lead.next(wl); ++i) prefetch_item(wl);
-            auto sched = schedule();
-            WorkItem w;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            while (sched.next(w)) {
-                if (!wait_bar(&tfull_bar[acc], acc_phase, abort_flag, p.err, 401)) break;
-                if (lead.next(wl)) prefetch_item(wl);
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1;
-                }
-            }
         }
         if constexpr (!PAIR) {
             if (splits > 1) {

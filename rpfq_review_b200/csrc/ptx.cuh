@@ -189,13 +189,6 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes
                  : "memory");
 }
 
-// Prefetch a 2-D box of a tensor map into L2 (no shared memory involved).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int32_t c0, int32_t c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
-                 "r"(c0), "r"(c1)
-                 : "memory");
-}
-
 template <int N>
 __device__ __forceinline__ void bulk_wait_group_read() {
     asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
