@@ -779,8 +779,8 @@ def run_b200(args):
 # exact shape (files profiles/gemm_f16_sm100_{qkv,proj_residual,fc1_gelu,
 # fc2_residual}_50432x*.md), with the algorithmic bytes 2MK + 2NK + 2N + e*MN
 # of each (e = 2 for fp16 out, 8 for fp32 out + fp32 residual read).
-_VITB256_GEMM_TRAFFIC = {"qkv": (260.6e6, 313.4e6), "proj_residual": (414.7e6, 388.5e6),
-                         "fc1_gelu": (334.5e6, 392.0e6), "fc2_residual": (760.3e6, 624.4e6)}
+_VITB256_GEMM_TRAFFIC = {"qkv": (258.0e6, 313.4e6), "proj_residual": (336.9e6, 388.5e6),
+                         "fc1_gelu": (334.5e6, 392.0e6), "fc2_residual": (619.6e6, 624.4e6)}
 
 
 def _gemm_traffic(cfg, batch, args):
