@@ -632,7 +632,10 @@ def run_b200(args):
     # Every step copies its images in and its logits out inside the timed
     # region; the next step's images travel on a copy stream into the other of
     # two input buffers while the current step computes (a second graph reads
-    # the second buffer). Same step count as the device-timed leg.
+    # the second buffer), and each step's logits (this rank's rows) go to the
+    # host on a third stream while the next step computes (an output buffer is
+    # written again only after its copy has read it; the timed region ends
+    # after the last copy). Same step count as the device-timed leg.
     e2e_steps = args.e2e_steps or args.steps
     host_imgs = images.cpu().pin_memory()
     host_outs = [torch.empty((B, cfg.classes), dtype=torch.float32).pin_memory() for _ in range(2)]
@@ -642,18 +645,19 @@ def run_b200(args):
         with torch.cuda.graph(graph2):
             static_out2 = model(images2)
 
-        def step_on(buf):
+        def forward_on(buf):
             (graph if buf == 0 else graph2).replay()
-            out = static_out if buf == 0 else static_out2
-            if gather is not None:
-                gather(out)
-            return out
+            return static_out if buf == 0 else static_out2
     else:
-        def step_on(buf):
-            out = model(images if buf == 0 else images2)
-            if gather is not None:
-                gather(out)
-            return out
+        def forward_on(buf):
+            return model(images if buf == 0 else images2)
+
+    def step_on(buf):
+        # the step's collective runs; this rank reads back its own logits
+        out = forward_on(buf)
+        if gather is not None:
+            gather(out)
+        return out
     bufs = [images, images2]
     copy_stream = torch.cuda.Stream(dev)
     copied = [torch.cuda.Event() for _ in range(2)]
@@ -676,13 +680,26 @@ def run_b200(args):
 
     prefetch(0)
     compute = torch.cuda.current_stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
+    produced = [torch.cuda.Event() for _ in range(2)]
+    read_out = [torch.cuda.Event() for _ in range(2)]  # step s's logits copied out (buffer s % 2)
     for s_ in range(e2e_steps):
+        b = s_ % 2
         if s_ + 1 < e2e_steps:
             prefetch(s_ + 1)
-        compute.wait_event(copied[s_ % 2])
-        out = step_on(s_ % 2)
-        consumed[s_ % 2].record(compute)
-        host_outs[s_ % 2].copy_(out, non_blocking=True)
+        compute.wait_event(copied[b])
+        if s_ >= 2:
+            compute.wait_event(read_out[b])  # the graph output this step rewrites
+        out = forward_on(b)
+        consumed[b].record(compute)
+        if gather is not None:
+            gather(out)
+        produced[b].record(compute)
+        with torch.cuda.stream(d2h_stream):
+            d2h_stream.wait_event(produced[b])
+            host_outs[b].copy_(out, non_blocking=True)
+            read_out[b].record(d2h_stream)
+    compute.wait_stream(d2h_stream)
     e1.record()
     barrier()
     host_out = host_outs[(e2e_steps - 1) % 2]
